@@ -1,0 +1,179 @@
+/*
+ * gdn.h -- C ABI of the B200 GatedDeltaNet (GDN) layer step.
+ *
+ * This is the drop-in boundary for the GDN path of qwen-mlx.  It replaces:
+ *   - the recurrence entry point  gated_delta_kernel   (src/models/metal_gdn.rs:170-218)
+ *   - the fused S=1 / S>1 layer body between the projections of
+ *     GatedDeltaNet::forward_with_cache                (src/models/qwen3_5.rs:588-665)
+ *   - the compiled beta/g closure  compiled_beta_g     (src/models/compiled_ops.rs:68-94)
+ *   - the executor's per-step stack/unstack of per-sequence states
+ *     Qwen35Executor::{stack_caches,unstack_caches}    (src/scheduler/mlx_executor.rs:92-130)
+ *     by a device-resident, slot-indexed state pool.
+ *
+ * Conventions
+ *   - bf16 tensors are passed as uint16_t bit patterns (gdn_bf16).
+ *   - Every function returns GDN_OK (0) or a GDN_E_* code; nothing throws or
+ *     aborts across the ABI.  gdn_last_error() returns a message for the last
+ *     failure on the calling thread.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Compute calls are asynchronous on that stream and take DEVICE pointers;
+ *     calls documented as "synchronous" take host pointers.
+ *   - A pool belongs to one device; calls switch to that device and restore
+ *     the caller's current device before returning.
+ *   - Only head_k_dim = head_v_dim = 128 and conv_kernel = 4 are specialised;
+ *     other shapes return GDN_E_UNSUPPORTED.
+ *
+ * Layouts (row-major, the reference's own):
+ *   recurrent state of one (slot, layer):  [Hv][dv][dk] f32   (metal_gdn.rs:144-152)
+ *   conv state of one (slot, layer):       [K-1][D] bf16      (qwen3_5.rs:598-604)
+ *   conv weight:                           [D][K] bf16        (qwen3_5.rs:1058-1066, [D,K,1])
+ *   D = 2*Hk*dk + Hv*dv channels in the order q | k | v       (qwen3_5.rs:513, :627-629)
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__) || defined(__clang__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_OK 0
+#define GDN_E_INVALID 1     /* null pointer, negative size, inconsistent arguments */
+#define GDN_E_UNSUPPORTED 2 /* shape not specialised on this build */
+#define GDN_E_BAD_SLOT 3    /* slot id out of range, or used twice in one batch */
+#define GDN_E_BAD_SEQLENS 4 /* cu_seqlens not starting at 0, decreasing, or not ending at n_tokens */
+#define GDN_E_CUDA 5        /* CUDA runtime error (message in gdn_last_error) */
+#define GDN_E_NOMEM 6       /* device allocation failed */
+#define GDN_E_DEVICE 7      /* a device-side bounds check tripped (see gdn_pool_check) */
+
+typedef uint16_t gdn_bf16;
+
+/* Model shapes.  Mirrors the GDN fields of Qwen35Config (src/models/qwen3_5.rs:30-70). */
+typedef struct gdn_config {
+    int32_t hidden;       /* hidden_size */
+    int32_t n_k_heads;    /* linear_num_key_heads */
+    int32_t n_v_heads;    /* linear_num_value_heads (multiple of n_k_heads) */
+    int32_t head_k_dim;   /* linear_key_head_dim  (128) */
+    int32_t head_v_dim;   /* linear_value_head_dim (128) */
+    int32_t conv_kernel;  /* linear_conv_kernel_dim (4) */
+    int32_t n_layers;     /* number of GDN layers held by a pool */
+    float rms_norm_eps;   /* rms_norm_eps of the gated output norm */
+} gdn_config;
+
+/* Per-layer parameters of the fused step (GatedDeltaNet fields, qwen3_5.rs:466-490). Device pointers. */
+typedef struct gdn_layer_weights {
+    const gdn_bf16* conv_w; /* [D][K]  conv1d.weight */
+    const float* A_log;     /* [Hv]    A_log */
+    const float* dt_bias;   /* [Hv]    dt_bias */
+    const gdn_bf16* norm_w; /* [dv]    norm.weight (RMSNormGated) */
+} gdn_layer_weights;
+
+/* Projection outputs feeding one layer step and its output, packed by token.
+ * Each buffer is [n_tokens][ld] with its own row stride (elements), so a single
+ * merged projection output [N][D + Hv*dv + 2*Hv] can be passed three times.
+ * ab holds b in columns [0,Hv) and a in [Hv,2Hv): the reference's merged
+ * order (qwen3_5.rs:583, :1038). */
+typedef struct gdn_step_io {
+    const gdn_bf16* qkv; int64_t ld_qkv; /* [N][D]     in_proj_qkv output (pre-conv) */
+    const gdn_bf16* z;   int64_t ld_z;   /* [N][Hv*dv] in_proj_z output */
+    const gdn_bf16* ab;  int64_t ld_ab;  /* [N][2*Hv]  in_proj_b | in_proj_a outputs */
+    gdn_bf16* out;       int64_t ld_out; /* [N][Hv*dv] silu(z) * rms_norm(y): input of out_proj */
+} gdn_step_io;
+
+typedef struct gdn_pool gdn_pool;
+
+/* Message of the last failing call on this thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+
+/* Library version string. */
+GDN_API const char* gdn_version(void);
+
+/* ---------------------------------------------------------------- state pool
+ * Replaces the executor's per-sequence Qwen35State caches (mlx_executor.rs:19-21)
+ * and their stack/unstack (mlx_executor.rs:92-130): a sequence's state lives in
+ * a fixed slot for its whole life, and a step addresses slots by id.
+ * Device layout: rec  [n_layers][n_slots][Hv][dv][dk] f32
+ *                conv [n_layers][n_slots][K-1][D] bf16
+ * A new pool is zeroed (the reference's missing-cache zeros, qwen3_5.rs:598-601, :644-648). */
+GDN_API int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool** out);
+GDN_API int gdn_pool_destroy(gdn_pool* pool);
+
+/* Device pointers to one layer's slice of the pool (slot 0 of that layer). */
+GDN_API int gdn_pool_layer_state(gdn_pool* pool, int32_t layer, float** rec, gdn_bf16** conv);
+
+/* Bytes of device memory held by the pool (states + bookkeeping). */
+GDN_API int gdn_pool_bytes(const gdn_pool* pool, size_t* bytes);
+
+/* Zero the state of `n` slots (all layers): admission of a new sequence
+ * (replaces qwen3_5.rs:598-601, :644-648).  slots: host array. Asynchronous. */
+GDN_API int gdn_slot_reset(gdn_pool* pool, const int32_t* slots, int32_t n, void* stream);
+
+/* Copy one (slot, layer) state out of / into the pool in the reference layout:
+ * rec [Hv][dv][dk] f32 (the reference's [1,Hv,dv,dk] cache.1) and conv [K-1][D]
+ * bf16 (cache.0).  Host pointers; synchronous.  Either pointer may be NULL. */
+GDN_API int gdn_slot_export(gdn_pool* pool, int32_t slot, int32_t layer, float* rec, gdn_bf16* conv);
+GDN_API int gdn_slot_import(gdn_pool* pool, int32_t slot, int32_t layer, const float* rec, const gdn_bf16* conv);
+
+/* Host-side check of a batch's routing tables (host pointers): every slot in
+ * range and used once, cu_seqlens[0] == 0, non-decreasing, cu_seqlens[n_seq] == n_tokens. */
+GDN_API int gdn_validate_batch(const gdn_pool* pool, const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq,
+                       int32_t n_tokens);
+
+/* The same check without a pool (n_slots given directly); needs no GPU. */
+GDN_API int gdn_validate_tables(int32_t n_slots, const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq,
+                                int32_t n_tokens);
+
+/* Read and optionally clear the pool's device error word (synchronous).  Kernels
+ * skip any sequence whose slot id or token range fails their bounds checks and
+ * record GDN_E_BAD_SLOT / GDN_E_BAD_SEQLENS as bit (1 << code) in this word. */
+GDN_API int gdn_pool_check(gdn_pool* pool, int32_t* flags, int reset);
+
+/* ---------------------------------------------------------------- compute */
+
+/* One fused GDN layer step over a packed ragged batch (qwen3_5.rs:588-665 and
+ * compiled_ops.rs:12-49): causal depthwise conv + SiLU with the conv state
+ * update, q/k RMSNorm (gains 1/dk and dk^-1/2), beta = sigmoid(b),
+ * g = exp(-exp(A_log) * softplus(a + dt_bias)), the gated delta rule on the
+ * slot's f32 state (in place), and silu(z) * rms_norm(y, norm_w, eps).
+ * Sequence i owns tokens [cu_seqlens[i], cu_seqlens[i+1]) and slot slot_ids[i].
+ * A sequence of one token uses the reference's S=1 conv rounding
+ * (qwen3_5.rs:593-610), a longer one its conv1d rounding (:611-624).
+ * slot_ids / cu_seqlens: DEVICE arrays.  Asynchronous on `stream`. */
+GDN_API int gdn_layer_step(gdn_pool* pool, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                   const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens,
+                   void* stream);
+
+/* The gated delta recurrence alone on pool state (metal_gdn.rs:10-67), packed
+ * and ragged: q,k [N][Hk][dk] bf16, v [N][Hv][dv] bf16, g [N][Hv] f32,
+ * beta [N][Hv] bf16 -> y [N][Hv][dv] bf16; state of slot_ids[i] updated in place. */
+GDN_API int gdn_recurrence(gdn_pool* pool, int32_t layer, const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                   const float* g, const gdn_bf16* beta, const int32_t* slot_ids, const int32_t* cu_seqlens,
+                   int32_t n_seq, int32_t n_tokens, gdn_bf16* y, void* stream);
+
+/* Reference-shaped recurrence: the argument meaning of gated_delta_kernel
+ * (metal_gdn.rs:170-173).  q,k [B,T,Hk,dk], v [B,T,Hv,dv], g [B,T,Hv] f32,
+ * beta [B,T,Hv] bf16, state_in [B,Hv,dv,dk] f32 -> y [B,T,Hv,dv] bf16 and
+ * state_out [B,Hv,dv,dk] f32.  state_out may equal state_in (in place) or be a
+ * separate buffer (the reference's functional form).  Device pointers. */
+GDN_API int gdn_gated_delta_kernel(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* g,
+                           const gdn_bf16* beta, const float* state_in, int32_t seq_len, int32_t batch, int32_t hk,
+                           int32_t hv, int32_t dk, int32_t dv, gdn_bf16* y, float* state_out, void* stream);
+
+/* beta and g alone (compiled_beta_g, compiled_ops.rs:68-94): ab [N][ld_ab] (b | a)
+ * -> beta [N][Hv] bf16, g [N][Hv] f32.  Device pointers. */
+GDN_API int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
+               const float* dt_bias, gdn_bf16* beta, float* g, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,104 @@
+"""ctypes declarations of include/gdn.h for libgdn_b200.so.
+
+The library is the product; this module only binds it.  Loading fails loudly
+when the library has not been built: there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libgdn_b200.so"
+
+GDN_OK = 0
+GDN_E_INVALID = 1
+GDN_E_UNSUPPORTED = 2
+GDN_E_BAD_SLOT = 3
+GDN_E_BAD_SEQLENS = 4
+GDN_E_CUDA = 5
+GDN_E_NOMEM = 6
+GDN_E_DEVICE = 7
+
+# Every function declared in include/gdn.h, with (restype, argtypes).
+_vp = C.c_void_p
+_i32 = C.c_int32
+_i64 = C.c_int64
+_int = C.c_int
+
+
+class GdnConfigC(C.Structure):
+    _fields_ = [("hidden", _i32), ("n_k_heads", _i32), ("n_v_heads", _i32), ("head_k_dim", _i32),
+                ("head_v_dim", _i32), ("conv_kernel", _i32), ("n_layers", _i32), ("rms_norm_eps", C.c_float)]
+
+
+class GdnLayerWeightsC(C.Structure):
+    _fields_ = [("conv_w", _vp), ("A_log", _vp), ("dt_bias", _vp), ("norm_w", _vp)]
+
+
+class GdnStepIOC(C.Structure):
+    _fields_ = [("qkv", _vp), ("ld_qkv", _i64), ("z", _vp), ("ld_z", _i64), ("ab", _vp), ("ld_ab", _i64),
+                ("out", _vp), ("ld_out", _i64)]
+
+
+SIGNATURES = {
+    "gdn_last_error": (C.c_char_p, []),
+    "gdn_version": (C.c_char_p, []),
+    "gdn_pool_create": (_int, [_int, C.POINTER(GdnConfigC), _i32, C.POINTER(_vp)]),
+    "gdn_pool_destroy": (_int, [_vp]),
+    "gdn_pool_layer_state": (_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_vp)]),
+    "gdn_pool_bytes": (_int, [_vp, C.POINTER(C.c_size_t)]),
+    "gdn_slot_reset": (_int, [_vp, _vp, _i32, _vp]),
+    "gdn_slot_export": (_int, [_vp, _i32, _i32, _vp, _vp]),
+    "gdn_slot_import": (_int, [_vp, _i32, _i32, _vp, _vp]),
+    "gdn_validate_batch": (_int, [_vp, _vp, _vp, _i32, _i32]),
+    "gdn_validate_tables": (_int, [_i32, _vp, _vp, _i32, _i32]),
+    "gdn_pool_check": (_int, [_vp, C.POINTER(_i32), _int]),
+    "gdn_layer_step": (_int, [_vp, _i32, C.POINTER(GdnLayerWeightsC), C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32,
+                              _vp]),
+    "gdn_recurrence": (_int, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp]),
+    "gdn_gated_delta_kernel": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+                                      _vp]),
+    "gdn_beta_g": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+}
+
+
+class GdnError(RuntimeError):
+    def __init__(self, code: int, func: str, msg: str):
+        super().__init__(f"{func} failed with code {code}: {msg}")
+        self.code = code
+        self.func = func
+
+
+_lib = None
+
+
+def lib():
+    """Load libgdn_b200.so (raises if it is missing or lacks a declared symbol)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python qwen-mlx_b200/build.py` (no CPU fallback exists)")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().gdn_last_error().decode()
+
+
+def check(rc: int, func: str):
+    if rc != GDN_OK:
+        raise GdnError(rc, func, last_error())
+
+
+def call(name: str, *args):
+    rc = getattr(lib(), name)(*args)
+    check(rc, name)
+    return rc

@@ -1,0 +1,381 @@
+// gdn_api.cu -- C ABI of include/gdn.h: slot-indexed state pool, routing
+// validation, error reporting and the launch of the fused kernels.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "gdn.h"
+#include "gdn_internal.h"
+
+#define GDN_VERSION_STRING "gdn-b200 0.1.0 (sm_100a)"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int ok() {
+    g_last_error.clear();
+    return GDN_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(GDN_E_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Switches to `dev` for the lifetime of the guard and restores the caller's device.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t status = cudaSuccess;
+    explicit DeviceGuard(int dev) {
+        status = cudaGetDevice(&prev);
+        if (status == cudaSuccess && prev != dev) status = cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+struct gdn_pool {
+    int device;
+    gdn_config cfg;
+    int32_t n_slots;
+    int32_t D;
+    size_t rec_slot_elems;   // Hv*dv*dk
+    size_t conv_slot_elems;  // (K-1)*D
+    float* rec;              // [n_layers][n_slots][Hv][dv][dk]
+    uint16_t* conv;          // [n_layers][n_slots][K-1][D]
+    int32_t* err;            // device error word
+};
+
+static int check_cfg(const gdn_config* c) {
+    if (!c) return fail(GDN_E_INVALID, "config is NULL");
+    if (c->n_k_heads <= 0 || c->n_v_heads <= 0 || c->n_layers <= 0 || c->hidden <= 0)
+        return fail(GDN_E_INVALID, "config has a non-positive size (hk=%d hv=%d layers=%d hidden=%d)", c->n_k_heads,
+                    c->n_v_heads, c->n_layers, c->hidden);
+    if (c->n_v_heads % c->n_k_heads)
+        return fail(GDN_E_INVALID, "n_v_heads (%d) must be a multiple of n_k_heads (%d)", c->n_v_heads, c->n_k_heads);
+    if (c->head_k_dim != gdn::DK_ABI || c->head_v_dim != gdn::DV_ABI)
+        return fail(GDN_E_UNSUPPORTED, "only head_k_dim = head_v_dim = 128 is specialised (got %d, %d)",
+                    c->head_k_dim, c->head_v_dim);
+    if (c->conv_kernel != 4) return fail(GDN_E_UNSUPPORTED, "only conv_kernel = 4 is specialised (got %d)", c->conv_kernel);
+    if (c->n_v_heads / c->n_k_heads > 8)
+        return fail(GDN_E_UNSUPPORTED, "n_v_heads / n_k_heads = %d exceeds the portable cluster size 8",
+                    c->n_v_heads / c->n_k_heads);
+    if (!(c->rms_norm_eps >= 0.0f)) return fail(GDN_E_INVALID, "rms_norm_eps must be >= 0");
+    return GDN_OK;
+}
+
+extern "C" {
+
+const char* gdn_last_error(void) { return g_last_error.c_str(); }
+
+const char* gdn_version(void) { return GDN_VERSION_STRING; }
+
+int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool** out) {
+    if (!out) return fail(GDN_E_INVALID, "out is NULL");
+    *out = nullptr;
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (n_slots <= 0) return fail(GDN_E_INVALID, "n_slots must be positive (got %d)", n_slots);
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev) return fail(GDN_E_INVALID, "device %d out of range [0,%d)", device, ndev);
+    DeviceGuard g(device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+
+    gdn_pool* p = new (std::nothrow) gdn_pool();
+    if (!p) return fail(GDN_E_NOMEM, "host allocation failed");
+    p->device = device;
+    p->cfg = *cfg;
+    p->n_slots = n_slots;
+    p->D = 2 * cfg->n_k_heads * cfg->head_k_dim + cfg->n_v_heads * cfg->head_v_dim;
+    p->rec_slot_elems = (size_t)cfg->n_v_heads * cfg->head_v_dim * cfg->head_k_dim;
+    p->conv_slot_elems = (size_t)(cfg->conv_kernel - 1) * p->D;
+    const size_t rec_bytes = sizeof(float) * p->rec_slot_elems * n_slots * cfg->n_layers;
+    const size_t conv_bytes = sizeof(uint16_t) * p->conv_slot_elems * n_slots * cfg->n_layers;
+    e = cudaMalloc(&p->rec, rec_bytes);
+    if (e != cudaSuccess) {
+        delete p;
+        return fail(GDN_E_NOMEM, "cudaMalloc of %zu B of recurrent state failed: %s", rec_bytes, cudaGetErrorString(e));
+    }
+    e = cudaMalloc(&p->conv, conv_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(p->rec);
+        delete p;
+        return fail(GDN_E_NOMEM, "cudaMalloc of %zu B of conv state failed: %s", conv_bytes, cudaGetErrorString(e));
+    }
+    e = cudaMalloc(&p->err, sizeof(int32_t));
+    if (e != cudaSuccess) {
+        cudaFree(p->rec);
+        cudaFree(p->conv);
+        delete p;
+        return fail(GDN_E_NOMEM, "cudaMalloc of the error word failed: %s", cudaGetErrorString(e));
+    }
+    e = cudaMemset(p->rec, 0, rec_bytes);
+    if (e == cudaSuccess) e = cudaMemset(p->conv, 0, conv_bytes);
+    if (e == cudaSuccess) e = cudaMemset(p->err, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p->rec);
+        cudaFree(p->conv);
+        cudaFree(p->err);
+        delete p;
+        return cuda_fail(e, "zeroing the pool");
+    }
+    *out = p;
+    return ok();
+}
+
+int gdn_pool_destroy(gdn_pool* p) {
+    if (!p) return ok();
+    DeviceGuard g(p->device);
+    cudaFree(p->rec);
+    cudaFree(p->conv);
+    cudaFree(p->err);
+    delete p;
+    return ok();
+}
+
+int gdn_pool_layer_state(gdn_pool* p, int32_t layer, float** rec, gdn_bf16** conv) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (layer < 0 || layer >= p->cfg.n_layers)
+        return fail(GDN_E_INVALID, "layer %d out of range [0,%d)", layer, p->cfg.n_layers);
+    if (rec) *rec = p->rec + (size_t)layer * p->n_slots * p->rec_slot_elems;
+    if (conv) *conv = p->conv + (size_t)layer * p->n_slots * p->conv_slot_elems;
+    return ok();
+}
+
+int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
+    if (!p || !bytes) return fail(GDN_E_INVALID, "NULL argument");
+    *bytes = (sizeof(float) * p->rec_slot_elems + sizeof(uint16_t) * p->conv_slot_elems) * (size_t)p->n_slots *
+                 p->cfg.n_layers +
+             sizeof(int32_t);
+    return ok();
+}
+
+int gdn_slot_reset(gdn_pool* p, const int32_t* slots, int32_t n, void* stream) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (n < 0 || (n > 0 && !slots)) return fail(GDN_E_INVALID, "bad slot list");
+    for (int32_t i = 0; i < n; ++i)
+        if (slots[i] < 0 || slots[i] >= p->n_slots)
+            return fail(GDN_E_BAD_SLOT, "slot %d out of range [0,%d)", slots[i], p->n_slots);
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    cudaStream_t s = (cudaStream_t)stream;
+    for (int32_t l = 0; l < p->cfg.n_layers; ++l)
+        for (int32_t i = 0; i < n; ++i) {
+            const size_t idx = (size_t)l * p->n_slots + slots[i];
+            cudaError_t e = cudaMemsetAsync(p->rec + idx * p->rec_slot_elems, 0, sizeof(float) * p->rec_slot_elems, s);
+            if (e == cudaSuccess)
+                e = cudaMemsetAsync(p->conv + idx * p->conv_slot_elems, 0, sizeof(uint16_t) * p->conv_slot_elems, s);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync (slot reset)");
+        }
+    return ok();
+}
+
+static int slot_copy(gdn_pool* p, int32_t slot, int32_t layer, void* rec, void* conv, bool to_host) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (slot < 0 || slot >= p->n_slots) return fail(GDN_E_BAD_SLOT, "slot %d out of range [0,%d)", slot, p->n_slots);
+    if (layer < 0 || layer >= p->cfg.n_layers)
+        return fail(GDN_E_INVALID, "layer %d out of range [0,%d)", layer, p->cfg.n_layers);
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    const size_t idx = (size_t)layer * p->n_slots + slot;
+    cudaError_t e = cudaSuccess;
+    if (rec) {
+        float* d = p->rec + idx * p->rec_slot_elems;
+        e = to_host ? cudaMemcpy(rec, d, sizeof(float) * p->rec_slot_elems, cudaMemcpyDeviceToHost)
+                    : cudaMemcpy(d, rec, sizeof(float) * p->rec_slot_elems, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy (recurrent state)");
+    }
+    if (conv) {
+        uint16_t* d = p->conv + idx * p->conv_slot_elems;
+        e = to_host ? cudaMemcpy(conv, d, sizeof(uint16_t) * p->conv_slot_elems, cudaMemcpyDeviceToHost)
+                    : cudaMemcpy(d, conv, sizeof(uint16_t) * p->conv_slot_elems, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy (conv state)");
+    }
+    return ok();
+}
+
+int gdn_slot_export(gdn_pool* p, int32_t slot, int32_t layer, float* rec, gdn_bf16* conv) {
+    return slot_copy(p, slot, layer, rec, conv, true);
+}
+
+int gdn_slot_import(gdn_pool* p, int32_t slot, int32_t layer, const float* rec, const gdn_bf16* conv) {
+    return slot_copy(p, slot, layer, const_cast<float*>(rec), const_cast<gdn_bf16*>(conv), false);
+}
+
+int gdn_validate_tables(int32_t n_slots, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                        int32_t n_tokens) {
+    if (n_slots <= 0) return fail(GDN_E_INVALID, "n_slots must be positive (got %d)", n_slots);
+    if (n_seq < 0 || n_tokens < 0) return fail(GDN_E_INVALID, "negative n_seq or n_tokens");
+    if (n_seq > 0 && (!slot_ids || !cu)) return fail(GDN_E_INVALID, "NULL routing table");
+    if (n_seq == 0) {
+        if (n_tokens != 0) return fail(GDN_E_BAD_SEQLENS, "n_seq = 0 but n_tokens = %d", n_tokens);
+        return ok();
+    }
+    if (cu[0] != 0) return fail(GDN_E_BAD_SEQLENS, "cu_seqlens[0] = %d, expected 0", cu[0]);
+    for (int32_t i = 0; i < n_seq; ++i)
+        if (cu[i + 1] < cu[i])
+            return fail(GDN_E_BAD_SEQLENS, "cu_seqlens decreases at %d (%d -> %d)", i, cu[i], cu[i + 1]);
+    if (cu[n_seq] != n_tokens)
+        return fail(GDN_E_BAD_SEQLENS, "cu_seqlens[%d] = %d, expected n_tokens = %d", n_seq, cu[n_seq], n_tokens);
+    std::vector<unsigned char> seen((size_t)n_slots, 0);
+    for (int32_t i = 0; i < n_seq; ++i) {
+        const int32_t s = slot_ids[i];
+        if (s < 0 || s >= n_slots) return fail(GDN_E_BAD_SLOT, "slot_ids[%d] = %d out of range [0,%d)", i, s, n_slots);
+        if (seen[s]) return fail(GDN_E_BAD_SLOT, "slot %d appears twice in one batch", s);
+        seen[s] = 1;
+    }
+    return ok();
+}
+
+int gdn_validate_batch(const gdn_pool* p, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                       int32_t n_tokens) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    return gdn_validate_tables(p->n_slots, slot_ids, cu, n_seq, n_tokens);
+}
+
+int gdn_pool_check(gdn_pool* p, int32_t* flags, int reset) {
+    if (!p || !flags) return fail(GDN_E_INVALID, "NULL argument");
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(flags, p->err, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && reset) e = cudaMemset(p->err, 0, sizeof(int32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "reading the error word");
+    return ok();
+}
+
+static gdn::StepArgs base_args(gdn_pool* p, int32_t layer) {
+    gdn::StepArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.rec = p->rec + (size_t)layer * p->n_slots * p->rec_slot_elems;
+    a.conv = p->conv + (size_t)layer * p->n_slots * p->conv_slot_elems;
+    a.n_slots = p->n_slots;
+    a.hk = p->cfg.n_k_heads;
+    a.hv = p->cfg.n_v_heads;
+    a.D = p->D;
+    a.eps = p->cfg.rms_norm_eps;
+    a.err = p->err;
+    return a;
+}
+
+static int check_common(gdn_pool* p, int32_t layer, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                        int32_t n_tokens) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (layer < 0 || layer >= p->cfg.n_layers)
+        return fail(GDN_E_INVALID, "layer %d out of range [0,%d)", layer, p->cfg.n_layers);
+    if (n_seq < 0 || n_tokens < 0) return fail(GDN_E_INVALID, "negative n_seq or n_tokens");
+    if (n_seq > 65535) return fail(GDN_E_UNSUPPORTED, "n_seq %d exceeds 65535 per call", n_seq);
+    if (n_seq > 0 && (!slot_ids || !cu)) return fail(GDN_E_INVALID, "NULL routing table");
+    return GDN_OK;
+}
+
+int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                   const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, void* stream) {
+    int rc = check_common(p, layer, slot_ids, cu, n_seq, n_tokens);
+    if (rc) return rc;
+    if (!w || !w->conv_w || !w->A_log || !w->dt_bias || !w->norm_w) return fail(GDN_E_INVALID, "NULL layer weight");
+    if (!io || !io->qkv || !io->z || !io->ab || !io->out) return fail(GDN_E_INVALID, "NULL step buffer");
+    if (((uintptr_t)w->conv_w & 7u) != 0) return fail(GDN_E_INVALID, "conv_w must be 8-byte aligned");
+    if (io->ld_qkv < p->D || io->ld_z < (int64_t)p->cfg.n_v_heads * 128 || io->ld_ab < 2 * p->cfg.n_v_heads ||
+        io->ld_out < (int64_t)p->cfg.n_v_heads * 128)
+        return fail(GDN_E_INVALID, "row stride smaller than the row");
+    if (n_seq == 0) return ok();
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    gdn::StepArgs a = base_args(p, layer);
+    a.slot_ids = slot_ids;
+    a.cu_seqlens = cu;
+    a.n_seq = n_seq;
+    a.n_tokens = n_tokens;
+    a.qkv = io->qkv; a.ld_qkv = io->ld_qkv;
+    a.z = io->z; a.ld_z = io->ld_z;
+    a.ab = io->ab; a.ld_ab = io->ld_ab;
+    a.out = io->out; a.ld_out = io->ld_out;
+    a.conv_w = w->conv_w;
+    a.A_log = w->A_log;
+    a.dt_bias = w->dt_bias;
+    a.norm_w = w->norm_w;
+    cudaError_t e = gdn::launch_layer_step(a, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");
+    return ok();
+}
+
+int gdn_recurrence(gdn_pool* p, int32_t layer, const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                   const float* g, const gdn_bf16* beta, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                   int32_t n_tokens, gdn_bf16* y, void* stream) {
+    int rc = check_common(p, layer, slot_ids, cu, n_seq, n_tokens);
+    if (rc) return rc;
+    if (!q || !k || !v || !g || !beta || !y) return fail(GDN_E_INVALID, "NULL tensor");
+    if (n_seq == 0) return ok();
+    DeviceGuard dg(p->device);
+    if (dg.status != cudaSuccess) return cuda_fail(dg.status, "cudaSetDevice");
+    gdn::StepArgs a = base_args(p, layer);
+    a.slot_ids = slot_ids;
+    a.cu_seqlens = cu;
+    a.n_seq = n_seq;
+    a.n_tokens = n_tokens;
+    a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta; a.y = y;
+    cudaError_t e = gdn::launch_recurrence(a, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_recurrence launch");
+    return ok();
+}
+
+int gdn_gated_delta_kernel(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* g,
+                           const gdn_bf16* beta, const float* state_in, int32_t seq_len, int32_t batch, int32_t hk,
+                           int32_t hv, int32_t dk, int32_t dv, gdn_bf16* y, float* state_out, void* stream) {
+    if (!q || !k || !v || !g || !beta || !state_in || !y || !state_out) return fail(GDN_E_INVALID, "NULL tensor");
+    if (seq_len < 0 || batch < 0 || hk <= 0 || hv <= 0 || hv % hk)
+        return fail(GDN_E_INVALID, "bad shape (T=%d B=%d hk=%d hv=%d)", seq_len, batch, hk, hv);
+    if (dk != 128 || dv != 128) return fail(GDN_E_UNSUPPORTED, "only dk = dv = 128 is specialised (got %d, %d)", dk, dv);
+    if (batch > 65535) return fail(GDN_E_UNSUPPORTED, "batch %d exceeds 65535 per call", batch);
+    if ((long long)batch * seq_len > 0x7fffffffLL) return fail(GDN_E_UNSUPPORTED, "B*T overflows int32");
+    if ((((uintptr_t)state_in) | ((uintptr_t)state_out)) & 15u)
+        return fail(GDN_E_INVALID, "state_in / state_out must be 16-byte aligned");
+    if (batch == 0) return ok();
+    gdn::StepArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.rec = state_out;
+    a.rec_in = (state_in == state_out) ? nullptr : state_in;
+    a.n_seq = batch;
+    a.n_slots = batch;
+    a.T_dense = seq_len;
+    a.n_tokens = batch * seq_len;
+    a.hk = hk;
+    a.hv = hv;
+    a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta; a.y = y;
+    cudaError_t e = gdn::launch_recurrence(a, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_gated_delta_kernel launch");
+    return ok();
+}
+
+int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
+               const float* dt_bias, gdn_bf16* beta, float* g, void* stream) {
+    if (!ab || !A_log || !dt_bias || !beta || !g) return fail(GDN_E_INVALID, "NULL tensor");
+    if (n_tokens < 0 || hv <= 0 || ld_ab < 2 * hv) return fail(GDN_E_INVALID, "bad shape");
+    cudaError_t e = gdn::launch_beta_g(ab, ld_ab, n_tokens, hv, A_log, dt_bias, beta, g, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_beta_g launch");
+    return ok();
+}
+
+}  // extern "C"

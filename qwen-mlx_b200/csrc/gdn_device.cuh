@@ -1,0 +1,79 @@
+// gdn_device.cuh -- device helpers shared by the GDN kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int DK = 128;        // head_k_dim (specialised)
+constexpr int DV = 128;        // head_v_dim (specialised)
+constexpr int KC = 4;          // conv taps (linear_conv_kernel_dim)
+constexpr int NT = 256;        // threads per CTA of the step kernel
+constexpr int NW = NT / 32;    // warps per CTA
+constexpr int RPW = DV / NW;   // state rows (dv) per warp = 16
+
+// Error bits recorded in the pool's device error word (1 << GDN_E_*).
+constexpr int ERR_BAD_SLOT = 1 << 3;
+constexpr int ERR_BAD_SEQLENS = 1 << 4;
+
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+__device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+// Round an f32 value to bf16 precision (round-to-nearest-even) and widen back.
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+
+__device__ __forceinline__ float sigmoid_f32(float x) { return 1.0f / (1.0f + expf(-x)); }
+// nn::silu on a bf16 value: computed in f32, rounded once to bf16.
+__device__ __forceinline__ float silu_bf(float x) { return rbf(x * sigmoid_f32(x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Reduce-scatter of 16 per-lane partials across the warp: returns the full
+// 32-lane sum of row (lane >> 1).  Lanes 2r and 2r+1 both hold row r's sum.
+// 16 shuffles instead of the 80 of 16 independent butterflies.
+__device__ __forceinline__ float reduce_scatter16(const float (&p)[16], int lane) {
+    float a8[8];
+    const bool b4 = lane & 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float send = b4 ? p[j] : p[j + 8];
+        float keep = b4 ? p[j + 8] : p[j];
+        a8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float a4[4];
+    const bool b3 = lane & 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float send = b3 ? a8[j] : a8[j + 4];
+        float keep = b3 ? a8[j + 4] : a8[j];
+        a4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float a2[2];
+    const bool b2 = lane & 4;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        float send = b2 ? a4[j] : a4[j + 2];
+        float keep = b2 ? a4[j + 2] : a4[j];
+        a2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const bool b1 = lane & 2;
+    float send = b1 ? a2[0] : a2[1];
+    float keep = b1 ? a2[1] : a2[0];
+    float a1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+}
+
+// Thread-block-cluster split barrier (all threads of every CTA in the cluster).
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+}  // namespace gdn

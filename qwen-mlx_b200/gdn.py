@@ -1,0 +1,184 @@
+"""Host-side mirror of the reference GDN interfaces over the C ABI.
+
+  gated_delta_kernel(...)      -- metal_gdn.rs:170-218, same argument meaning,
+                                  functional (returns y and a new state)
+  StatePool                    -- the slot-indexed device state pool that replaces
+                                  Qwen35State + stack/unstack (mlx_executor.rs:19-130)
+  StatePool.layer_step(...)    -- the fused layer body of GatedDeltaNet::forward_with_cache
+                                  between the projections (qwen3_5.rs:588-665)
+  beta_g(...)                  -- compiled_beta_g (compiled_ops.rs:68-94)
+
+torch is used only to hold device memory and streams; every computation runs
+in libgdn_b200.so.  bf16 tensors are torch.bfloat16 on the device and uint16
+bit patterns on the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import abi
+from .synth import GdnConfig
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream):
+    if stream is None:
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if isinstance(stream, torch.cuda.Stream):
+        return C.c_void_p(stream.cuda_stream)
+    return C.c_void_p(int(stream))
+
+
+def bf16_to_device(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint16).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def bf16_to_host(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def f32_to_device(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(device)
+
+
+def _check_dev(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def gated_delta_kernel(q, k, v, g, beta, state, seq_len, batch, hk, hv, dk, dv, out_state=None, stream=None):
+    """Gated delta recurrence with the argument meaning of metal_gdn.rs:170-173.
+
+    q, k [B,T,Hk,dk] bf16; v [B,T,Hv,dv] bf16; g [B,T,Hv] f32; beta [B,T,Hv] bf16;
+    state [B,Hv,dv,dk] f32.  Returns (y [B,T,Hv,dv] bf16, new_state [B,Hv,dv,dk] f32);
+    `state` is left untouched unless `out_state is state` (in-place update).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta), ("state", state)):
+        _check_dev(t, name)
+    y = torch.empty((batch, seq_len, hv, dv), dtype=torch.bfloat16, device=q.device)
+    new_state = torch.empty_like(state) if out_state is None else out_state
+    abi.call("gdn_gated_delta_kernel", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), seq_len, batch,
+             hk, hv, dk, dv, _ptr(y), _ptr(new_state), _stream(stream))
+    return y, new_state
+
+
+def beta_g(ab, A_log, dt_bias, hv, stream=None):
+    """compiled_beta_g over an [N, >=2*Hv] (b | a) buffer: returns (beta bf16 [N,Hv], g f32 [N,Hv])."""
+    n = ab.shape[0]
+    beta = torch.empty((n, hv), dtype=torch.bfloat16, device=ab.device)
+    g = torch.empty((n, hv), dtype=torch.float32, device=ab.device)
+    abi.call("gdn_beta_g", _ptr(ab), ab.stride(0), n, hv, _ptr(A_log), _ptr(dt_bias), _ptr(beta), _ptr(g),
+             _stream(stream))
+    return beta, g
+
+
+class LayerWeights:
+    """Device copies of one layer's step parameters (conv_w [D,K], A_log, dt_bias, norm_w)."""
+
+    def __init__(self, w: dict, device):
+        self.conv_w = bf16_to_device(w["conv_w"], device)
+        self.A_log = f32_to_device(w["A_log"], device)
+        self.dt_bias = f32_to_device(w["dt_bias"], device)
+        self.norm_w = bf16_to_device(w["norm_w"], device)
+        self.c = abi.GdnLayerWeightsC(self.conv_w.data_ptr(), self.A_log.data_ptr(), self.dt_bias.data_ptr(),
+                                      self.norm_w.data_ptr())
+
+
+class StatePool:
+    """Slot-indexed device pool of GDN states for `cfg.n_layers` layers."""
+
+    def __init__(self, cfg: GdnConfig, n_slots: int, device: int = 0):
+        self.cfg = cfg
+        self.n_slots = n_slots
+        self.device = device
+        c = abi.GdnConfigC(cfg.hidden, cfg.hk, cfg.hv, cfg.dk, cfg.dv, cfg.conv_k, cfg.n_layers, cfg.eps)
+        h = C.c_void_p()
+        abi.call("gdn_pool_create", device, C.byref(c), n_slots, C.byref(h))
+        self.h = h
+
+    def close(self):
+        if self.h is not None and self.h.value:
+            abi.call("gdn_pool_destroy", self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ---------------------------------------------------------------- state
+    def nbytes(self) -> int:
+        n = C.c_size_t()
+        abi.call("gdn_pool_bytes", self.h, C.byref(n))
+        return int(n.value)
+
+    def layer_state_ptrs(self, layer: int):
+        rec, conv = C.c_void_p(), C.c_void_p()
+        abi.call("gdn_pool_layer_state", self.h, layer, C.byref(rec), C.byref(conv))
+        return rec.value, conv.value
+
+    def reset(self, slots, stream=None):
+        arr = np.ascontiguousarray(slots, dtype=np.int32)
+        abi.call("gdn_slot_reset", self.h, arr.ctypes.data_as(C.c_void_p), len(arr), _stream(stream))
+
+    def export(self, slot: int, layer: int):
+        cfg = self.cfg
+        rec = np.zeros((cfg.hv, cfg.dv, cfg.dk), np.float32)
+        conv = np.zeros((cfg.conv_k - 1, cfg.conv_dim), np.uint16)
+        torch.cuda.synchronize(self.device)
+        abi.call("gdn_slot_export", self.h, slot, layer, rec.ctypes.data_as(C.c_void_p),
+                 conv.ctypes.data_as(C.c_void_p))
+        return rec, conv
+
+    def import_(self, slot: int, layer: int, rec=None, conv=None):
+        torch.cuda.synchronize(self.device)
+        r = np.ascontiguousarray(rec, dtype=np.float32) if rec is not None else None
+        c = np.ascontiguousarray(conv, dtype=np.uint16) if conv is not None else None
+        abi.call("gdn_slot_import", self.h, slot, layer, r.ctypes.data_as(C.c_void_p) if r is not None else None,
+                 c.ctypes.data_as(C.c_void_p) if c is not None else None)
+
+    def check(self, reset: bool = True) -> int:
+        f = C.c_int32()
+        abi.call("gdn_pool_check", self.h, C.byref(f), 1 if reset else 0)
+        return int(f.value)
+
+    def validate(self, slot_ids, cu_seqlens, n_tokens=None):
+        s = np.ascontiguousarray(slot_ids, dtype=np.int32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        n_tokens = int(cu[-1]) if n_tokens is None else n_tokens
+        abi.call("gdn_validate_batch", self.h, s.ctypes.data_as(C.c_void_p), cu.ctypes.data_as(C.c_void_p),
+                 len(s), n_tokens)
+
+    # ---------------------------------------------------------------- compute
+    def layer_step(self, layer: int, w: LayerWeights, qkv, z, ab, out, slot_ids, cu_seqlens, n_tokens: int,
+                   stream=None):
+        """Fused layer step; qkv/z/ab/out are [N, ld] device tensors, tables are device int32."""
+        io = abi.GdnStepIOC(qkv.data_ptr(), qkv.stride(0), z.data_ptr(), z.stride(0), ab.data_ptr(), ab.stride(0),
+                            out.data_ptr(), out.stride(0))
+        abi.call("gdn_layer_step", self.h, layer, C.byref(w.c), C.byref(io), _ptr(slot_ids), _ptr(cu_seqlens),
+                 slot_ids.numel(), n_tokens, _stream(stream))
+
+    def layer_step_raw(self, layer: int, w_c, io_c, slot_ptr, cu_ptr, n_seq, n_tokens, stream_ptr):
+        """Same as layer_step with prebuilt ctypes arguments (no per-call Python allocation)."""
+        rc = abi.lib().gdn_layer_step(self.h, layer, w_c, io_c, slot_ptr, cu_ptr, n_seq, n_tokens, stream_ptr)
+        if rc:
+            abi.check(rc, "gdn_layer_step")
+
+    def recurrence(self, layer: int, q, k, v, g, beta, y, slot_ids, cu_seqlens, n_tokens: int, stream=None):
+        abi.call("gdn_recurrence", self.h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(slot_ids),
+                 _ptr(cu_seqlens), slot_ids.numel(), n_tokens, _ptr(y), _stream(stream))
