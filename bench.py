@@ -1,0 +1,461 @@
+"""Benchmark of the GDN-stack decode step (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference] [--no-sweep]
+
+Workload (BASELINE config 2 shape): the 30-layer GatedDeltaNet stack of
+Qwen3.5-35B-A3B (hidden 2048, Hk 16, Hv 32, dk = dv = 128, conv 4), batched
+S=1 decode of B sequences per GPU (default 8).  One step = one decode token for
+every sequence through all 30 fused layer steps (gdn_layer_step: conv + SiLU,
+q/k norm, gates, gated delta rule on the slot's f32 state, gated RMSNorm).  The
+per-layer projection outputs (qkv | z | b | a) are synthetic bf16 resident in
+HBM; the in/out projection GEMMs are not part of the timed step.  Pre-existing
+states are a seeded random f32 fill (decode cost does not depend on context
+length).  A step touches 1.04 GB of state at B=8, far more than the 126 MB L2,
+so no L2 flush is needed between steps.
+
+Multi-GPU: one process per GPU (torchrun); each GPU owns its own slot pool of B
+sequences (slot-range sharding), there is no collective on the data path; the
+NCCL group only provides the barrier and the max-over-ranks time.  value =
+all ranks' tokens / max-over-ranks device time ("scaling": "weak").
+
+--impl reference times the CPU restatement of the reference layer (oracle/,
+the reference's MLX/Metal path cannot run here) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GDN-stack decode tok/s at B=1..2048 over 1/2/4/8 B200; % HBM roofline"
+UNIT = "tok/s"
+N_LAYERS = 30
+# Algorithmic bytes of one fused decode layer step (per sequence, and per launch constant):
+#   state f32 r+w 2*32*128*128*4 + conv bf16 r+w 2*3*8192*2 + qkv 8192*2 + z 4096*2 + a,b 64*2 + out 4096*2
+BYTES_PER_SEQ_LAYER = 2 * 32 * 128 * 128 * 4 + 2 * 3 * 8192 * 2 + 8192 * 2 + 4096 * 2 + 64 * 2 + 4096 * 2
+#   conv weight 8192*4*2 + A_log 32*4 + dt_bias 32*4 + norm_w 128*2
+BYTES_PER_LAUNCH_CONST = 8192 * 4 * 2 + 32 * 4 + 32 * 4 + 128 * 2
+assert BYTES_PER_SEQ_LAYER == 4_325_504 and BYTES_PER_LAUNCH_CONST == 66_048
+PROJ_LD = 8192 + 4096 + 64     # merged projection output row: qkv | z | b | a
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the decode layer step from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "gdn_layer_step_decode.txt"
+    if not f.exists():
+        return None, None
+    vals = {}
+    for line in f.read_text().splitlines():
+        if ":" in line and line.split(":", 1)[0].strip() in ("traffic_bytes_per_seq", "traffic_batch"):
+            k, v = line.split(":", 1)
+            vals[k.strip()] = float(v.split()[0])
+    if "traffic_bytes_per_seq" not in vals:
+        return None, None
+    return vals["traffic_bytes_per_seq"], vals.get("traffic_batch")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_bench_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        return world, rank, local, dist, timedelta
+    return 1, 0, 0, None, None
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+
+def cpu_baseline(batch: int, budget_s: float = 12.0):
+    """Time the oracle (CPU restatement of the reference layer) on a bounded sample of the
+    same workload: repeated B-sequence decode layer steps; tok/s scaled to the 30-layer stack."""
+    import __graft_entry__ as ge
+    O = ge.load_oracle()
+    synth = ge.load_package().synth
+    cfg = synth.GdnConfig(n_layers=1)
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    w = synth.layer_weights(cfg, 0, with_proj=False)
+    inp = synth.step_inputs(cfg, batch, seed=0, tag="cpu")
+    conv, rec = synth.random_states(cfg, batch, seed=0, tag="cpu")
+    cu = np.arange(batch + 1, dtype=np.int32)
+    O.layer_step(cfg, w, inp["qkv"], inp["z"], inp["ab"], conv, rec, cu)   # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        _, conv, rec, _ = O.layer_step(cfg, w, inp["qkv"], inp["z"], inp["ab"], conv, rec, cu)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    per_stack_step = dt / n * N_LAYERS
+    return {"value": batch / per_stack_step, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} oracle decode layer steps of B={batch} in {dt:.1f} s, scaled x{N_LAYERS} layers/step"}
+
+
+def run_reference(args):
+    world, rank, local, dist, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return
+    import __graft_entry__ as ge
+    O = ge.load_oracle()
+    synth = ge.load_package().synth
+    cfg = synth.GdnConfig(n_layers=1)
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    B = args.batch
+    # Bounded sample per step: L_S of the 30 layers, scaled to the full stack.
+    L_S = 3
+    ws = [synth.layer_weights(cfg, l, with_proj=False) for l in range(L_S)]
+    inps = [synth.step_inputs(cfg, B, seed=0, tag=f"ref{l}") for l in range(L_S)]
+    states = [synth.random_states(cfg, B, seed=0, tag=f"ref{l}") for l in range(L_S)]
+    cu = np.arange(B + 1, dtype=np.int32)
+
+    def step():
+        for l in range(L_S):
+            conv, rec = states[l]
+            _, conv, rec, _ = O.layer_step(cfg, ws[l], inps[l]["qkv"], inps[l]["z"], inps[l]["ab"], conv, rec, cu)
+            states[l] = (conv, rec)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    ms_per_step = dt / args.steps * 1e3 * N_LAYERS / L_S
+    value = B / (ms_per_step / 1e3)
+    sample = f"{L_S} of {N_LAYERS} layers per step (scaled x{N_LAYERS // L_S}), B={B} decode, {args.steps} steps"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 state, bf16 io", "data": "synthetic",
+            "config": {"workload": f"config2: 30-layer GDN stack, batched S=1 decode, B={B}",
+                       "batch_per_gpu": B, "layers": N_LAYERS, "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample + "; CPU restatement of the reference layer (MLX/Metal unavailable)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+def _cudart():
+    """The CUDA runtime torch already loaded (used only to fill the pool with random state)."""
+    for line in open("/proc/self/maps"):
+        if "libcudart.so" in line:
+            return C.CDLL(line.split()[-1])
+    raise RuntimeError("libcudart not loaded")
+
+
+def _gpu_uuid(torch, dev):
+    """nvidia-smi -i identifier of this process's GPU (UUID; the CUDA index may be remapped)."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index)
+
+
+def run_ours(args):
+    import torch
+    world, rank, local, dist, timedelta = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if dist is not None:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=dev)
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    import importlib
+    synth = importlib.import_module("qwen_mlx_b200.synth")
+    gdn = importlib.import_module("qwen_mlx_b200.gdn")
+    abi = importlib.import_module("qwen_mlx_b200.abi")
+    lib = abi.lib()
+
+    cfg = synth.GdnConfig(n_layers=N_LAYERS)
+    B = args.batch
+    sweep_bs = [] if (args.no_sweep or world > 1) else [1, 8, 64, 256, 1024, 2048]
+    n_slots = max([B] + sweep_bs)
+    pool = gdn.StatePool(cfg, n_slots=n_slots, device=local)
+    cudart = _cudart()
+    cudart.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    tile = cfg.hv * cfg.dv * cfg.dk
+    fill = (torch.randn(n_slots * tile, device=dev, generator=gen) * 0.05).float()
+    cfill = torch.randn(n_slots * 3 * cfg.conv_dim, device=dev, generator=gen).to(torch.bfloat16)
+    for l in range(N_LAYERS):
+        rec_p, conv_p = pool.layer_state_ptrs(l)
+        assert cudart.cudaMemcpy(rec_p, fill.data_ptr(), fill.numel() * 4, 3) == 0
+        assert cudart.cudaMemcpy(conv_p, cfill.data_ptr(), cfill.numel() * 2, 3) == 0
+    del fill, cfill
+
+    # weights (synthetic, seeded) and per-layer projection outputs resident in HBM
+    lws = [gdn.LayerWeights(synth.layer_weights(cfg, l, with_proj=False), dev) for l in range(N_LAYERS)]
+    slots_all = torch.arange(n_slots, dtype=torch.int32, device=dev)
+    cu_all = torch.arange(n_slots + 1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def buffers(b):
+        """Contiguous per-layer projection outputs [L, b, qkv|z|b|a] and step outputs [L, b, Hv*dv]."""
+        proj = torch.randn((N_LAYERS, b, PROJ_LD), device=dev, generator=gen).to(torch.bfloat16)
+        out = torch.empty((N_LAYERS, b, cfg.z_dim), dtype=torch.bfloat16, device=dev)
+        return proj, out
+
+    def make_io(proj, out, l):
+        base = proj[l]
+        return abi.GdnStepIOC(base.data_ptr(), PROJ_LD, base.data_ptr() + 8192 * 2, PROJ_LD,
+                              base.data_ptr() + (8192 + 4096) * 2, PROJ_LD, out[l].data_ptr(), cfg.z_dim)
+
+    def step_fn(b, proj, out):
+        ios = [make_io(proj, out, l) for l in range(N_LAYERS)]
+        wcs = [lw.c for lw in lws]
+        sptr = C.c_void_p(slots_all.data_ptr())
+        cptr = C.c_void_p(cu_all.data_ptr())
+
+        def step():
+            for l in range(N_LAYERS):
+                rc = lib.gdn_layer_step(pool.h, l, C.byref(wcs[l]), C.byref(ios[l]), sptr, cptr, b, b, sp)
+                if rc:
+                    abi.check(rc, "gdn_layer_step")
+        return step
+
+    def capture(b, proj, out):
+        step = step_fn(b, proj, out)
+        with torch.cuda.stream(stream):
+            step()                      # eager warm-up (also validates arguments)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        return g
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def time_graph(g, steps, warmup):
+        """Device time of `steps` replays of the step graph; replays run on `stream`, events on `stream`."""
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                g.replay()
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize(dev)
+        barrier()
+        return e0.elapsed_time(e1)
+
+    def soak(g, seconds):
+        """Replay the step graph for `seconds` (clock sampling under the same load)."""
+        t_end = time.perf_counter() + seconds
+        with torch.cuda.stream(stream):
+            while time.perf_counter() < t_end:
+                for _ in range(20):
+                    g.replay()
+                stream.synchronize()
+
+    hbm_peak, peak_kind = measured_peaks()
+
+    # ---- headline: B sequences per GPU
+    proj_h, out_h = buffers(B)
+    g = capture(B, proj_h, out_h)
+    clocks = ClockSampler(_gpu_uuid(torch, dev))
+    clocks.start()
+    soak(g, 1.0)
+    ms = time_graph(g, args.steps, max(args.warmup, 3))
+    soak(g, 0.5)
+    clk = clocks.stop()
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * B * args.steps / (ms / 1e3)
+    gpu_launches = args.steps * N_LAYERS
+
+    # ---- roofline of the dominant kernel (the fused layer step), per launch
+    launch_ms = ms_per_step / N_LAYERS     # average launch duration inside the timed graph (gaps included)
+    alg_bytes = B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST
+    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    tr_per_seq, _ = profiled_traffic()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                "traffic": (tr_per_seq * B if tr_per_seq else None), "peak_kind": peak_kind,
+                "kernel": "gdn_step_kernel<fused>", "launch_us": launch_ms * 1e3,
+                "alg_bytes_per_launch": alg_bytes,
+                "step_frac": (B * N_LAYERS * BYTES_PER_SEQ_LAYER + N_LAYERS * BYTES_PER_LAUNCH_CONST)
+                / (ms_per_step / 1e3) / 1e9 / hbm_peak}
+
+    # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
+    in_host = torch.empty((N_LAYERS, B, PROJ_LD), dtype=torch.bfloat16).pin_memory()
+    in_host.copy_(proj_h.cpu())
+    out_host = torch.empty((N_LAYERS, B, cfg.z_dim), dtype=torch.bfloat16).pin_memory()
+    proj_b = proj_h
+    out_b = out_h
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            proj_b.copy_(in_host, non_blocking=True)
+            g.replay()
+            out_host.copy_(out_b, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    stream.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * B * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": in_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2}
+
+    # ---- B sweep (1 GPU only): device tok/s and step-level HBM fraction
+    sweep = {}
+    for b in sweep_bs:
+        if b == B:
+            sweep[str(b)] = {"tok_s": value / world, "hbm_frac": roofline["step_frac"]}
+            continue
+        proj_s, out_s = buffers(b)
+        gb = capture(b, proj_s, out_s)
+        st = max(3, min(args.steps, int(2000 / max(b, 1))))
+        msb = time_graph(gb, st, 3)
+        step_bytes = N_LAYERS * (b * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
+        sweep[str(b)] = {"tok_s": b * st / (msb / 1e3), "hbm_frac": step_bytes / (msb / st / 1e3) / 1e9 / hbm_peak}
+        del gb, proj_s, out_s
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(B)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 state, bf16 io", "data": "synthetic",
+                "config": {"workload": f"config2: 30-layer GDN stack, batched S=1 decode, B={B} per GPU",
+                           "batch_per_gpu": B, "layers": N_LAYERS, "parallelism": f"slot-range shards x{world}",
+                           "timed_step": "30 fused gdn_layer_step launches (CUDA graph); projections not included",
+                           "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
+                               N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
+                "clocks": clk, "sweep": sweep or None}
+    if dist is not None:
+        dist.barrier()
+        del g
+        dist.destroy_process_group()
+    pool.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

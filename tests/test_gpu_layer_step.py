@@ -119,7 +119,7 @@ def test_ragged_prefill_and_decode_scrambled(H, synth, oracle):
     ref = oracle.layer_step(cfg, h.w, inp["qkv"], inp["z"], inp["ab"], conv0, rec0, cu)
     _compare(synth, out, ref[0], h.states(0, slots), (ref[1], ref[2]), lens)
     # the empty sequence's state is untouched, bit for bit
-    c, r = h.pool.export(9, 0)
+    r, c = h.pool.export(9, 0)
     assert np.array_equal(r, rec0[4]) and np.array_equal(c, conv0[4])
 
 
@@ -204,11 +204,11 @@ def test_export_import_round_trip_and_reset(H, synth):
     cfg = h.cfg
     conv0, rec0 = synth.random_states(cfg, 1, seed=4, tag="rt")
     h.pool.import_(2, 1, rec0[0], conv0[0])
-    c, r = h.pool.export(2, 1)
+    r, c = h.pool.export(2, 1)
     assert np.array_equal(r.view(np.uint32), rec0[0].view(np.uint32)) and np.array_equal(c, conv0[0])
     h.pool.reset([2])
     torch.cuda.synchronize()
-    c, r = h.pool.export(2, 1)
+    r, c = h.pool.export(2, 1)
     assert not r.any() and not c.any()
 
 
