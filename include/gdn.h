@@ -106,6 +106,12 @@ GDN_API const char* gdn_version(void);
 GDN_API int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool** out);
 GDN_API int gdn_pool_destroy(gdn_pool* pool);
 
+/* Size the pool's step scratch for up to `max_tokens` packed tokens per call
+ * (a new pool holds max(n_slots, 1024)).  The scratch holds one 1040-byte record
+ * per (v-head, token): 33 KiB per token for Hv = 32.  Synchronous; call it before
+ * capturing a step into a CUDA graph, never while a step is in flight. */
+GDN_API int gdn_pool_reserve_tokens(gdn_pool* pool, int32_t max_tokens);
+
 /* Device pointers to one layer's slice of the pool (slot 0 of that layer). */
 GDN_API int gdn_pool_layer_state(gdn_pool* pool, int32_t layer, float** rec, gdn_bf16** conv);
 

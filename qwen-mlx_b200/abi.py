@@ -46,6 +46,7 @@ SIGNATURES = {
     "gdn_version": (C.c_char_p, []),
     "gdn_pool_create": (_int, [_int, C.POINTER(GdnConfigC), _i32, C.POINTER(_vp)]),
     "gdn_pool_destroy": (_int, [_vp]),
+    "gdn_pool_reserve_tokens": (_int, [_vp, _i32]),
     "gdn_pool_layer_state": (_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_vp)]),
     "gdn_pool_bytes": (_int, [_vp, C.POINTER(C.c_size_t)]),
     "gdn_slot_reset": (_int, [_vp, _vp, _i32, _vp]),

@@ -62,7 +62,25 @@ struct gdn_pool {
     float* rec;              // [n_layers][n_slots][Hv][dv][dk]
     uint16_t* conv;          // [n_layers][n_slots][K-1][D]
     int32_t* err;            // device error word
+    uint8_t* recs;           // scratch: per-(v-head, token) records of the layer step [Hv][rec_cap][REC_BYTES]
+    long long rec_cap;       // tokens per call the scratch holds
 };
+
+static int reserve_records(gdn_pool* p, long long tokens) {
+    if (tokens <= p->rec_cap) return GDN_OK;
+    const size_t bytes = (size_t)tokens * p->cfg.n_v_heads * gdn::REC_BYTES;
+    uint8_t* buf = nullptr;
+    cudaError_t e = cudaMalloc(&buf, bytes);
+    if (e != cudaSuccess)
+        return fail(GDN_E_NOMEM, "cudaMalloc of %zu B of step scratch failed: %s", bytes, cudaGetErrorString(e));
+    if (p->recs) {
+        cudaDeviceSynchronize();
+        cudaFree(p->recs);
+    }
+    p->recs = buf;
+    p->rec_cap = tokens;
+    return GDN_OK;
+}
 
 static int check_cfg(const gdn_config* c) {
     if (!c) return fail(GDN_E_INVALID, "config is NULL");
@@ -140,8 +158,27 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         delete p;
         return cuda_fail(e, "zeroing the pool");
     }
+    p->recs = nullptr;
+    p->rec_cap = 0;
+    rc = reserve_records(p, n_slots > 1024 ? n_slots : 1024);
+    if (rc) {
+        cudaFree(p->rec);
+        cudaFree(p->conv);
+        cudaFree(p->err);
+        delete p;
+        return rc;
+    }
     *out = p;
     return ok();
+}
+
+int gdn_pool_reserve_tokens(gdn_pool* p, int32_t max_tokens) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (max_tokens < 0) return fail(GDN_E_INVALID, "max_tokens must be >= 0");
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    int rc = reserve_records(p, max_tokens);
+    return rc ? rc : ok();
 }
 
 int gdn_pool_destroy(gdn_pool* p) {
@@ -150,6 +187,7 @@ int gdn_pool_destroy(gdn_pool* p) {
     cudaFree(p->rec);
     cudaFree(p->conv);
     cudaFree(p->err);
+    cudaFree(p->recs);
     delete p;
     return ok();
 }
@@ -167,7 +205,7 @@ int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
     if (!p || !bytes) return fail(GDN_E_INVALID, "NULL argument");
     *bytes = (sizeof(float) * p->rec_slot_elems + sizeof(uint16_t) * p->conv_slot_elems) * (size_t)p->n_slots *
                  p->cfg.n_layers +
-             sizeof(int32_t);
+             sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES;
     return ok();
 }
 
@@ -300,23 +338,47 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     if (io->ld_qkv < p->D || io->ld_z < (int64_t)p->cfg.n_v_heads * 128 || io->ld_ab < 2 * p->cfg.n_v_heads ||
         io->ld_out < (int64_t)p->cfg.n_v_heads * 128)
         return fail(GDN_E_INVALID, "row stride smaller than the row");
-    if (n_seq == 0) return ok();
+    if (n_tokens > p->rec_cap)
+        return fail(GDN_E_INVALID, "n_tokens %d exceeds the pool's reserved %lld tokens per call (gdn_pool_reserve_tokens)",
+                    n_tokens, p->rec_cap);
+    if (n_seq == 0 || n_tokens == 0) return ok();
     DeviceGuard g(p->device);
     if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
-    gdn::StepArgs a = base_args(p, layer);
-    a.slot_ids = slot_ids;
-    a.cu_seqlens = cu;
-    a.n_seq = n_seq;
-    a.n_tokens = n_tokens;
-    a.qkv = io->qkv; a.ld_qkv = io->ld_qkv;
-    a.z = io->z; a.ld_z = io->ld_z;
-    a.ab = io->ab; a.ld_ab = io->ld_ab;
-    a.out = io->out; a.ld_out = io->ld_out;
-    a.conv_w = w->conv_w;
-    a.A_log = w->A_log;
-    a.dt_bias = w->dt_bias;
-    a.norm_w = w->norm_w;
-    cudaError_t e = gdn::launch_layer_step(a, (cudaStream_t)stream);
+    float* rec = p->rec + (size_t)layer * p->n_slots * p->rec_slot_elems;
+    uint16_t* conv = p->conv + (size_t)layer * p->n_slots * p->conv_slot_elems;
+    gdn::PrepArgs pa;
+    std::memset(&pa, 0, sizeof pa);
+    pa.qkv = io->qkv; pa.ld_qkv = io->ld_qkv;
+    pa.z = io->z; pa.ld_z = io->ld_z;
+    pa.ab = io->ab; pa.ld_ab = io->ld_ab;
+    pa.conv = conv;
+    pa.conv_w = w->conv_w;
+    pa.A_log = w->A_log;
+    pa.dt_bias = w->dt_bias;
+    pa.slot_ids = slot_ids;
+    pa.cu_seqlens = cu;
+    pa.n_seq = n_seq; pa.n_slots = p->n_slots; pa.n_tokens = n_tokens;
+    pa.hk = p->cfg.n_k_heads; pa.hv = p->cfg.n_v_heads; pa.D = p->D;
+    pa.rec = p->recs;
+    pa.rec_cap = p->rec_cap;
+    pa.err = p->err;
+    gdn::RecurArgs ra;
+    std::memset(&ra, 0, sizeof ra);
+    ra.rec = rec;
+    ra.rec_in = nullptr;
+    ra.conv = conv;
+    ra.qkv = io->qkv; ra.ld_qkv = io->ld_qkv;
+    ra.recs = p->recs;
+    ra.rec_cap = p->rec_cap;
+    ra.norm_w = w->norm_w;
+    ra.eps = p->cfg.rms_norm_eps;
+    ra.out = io->out; ra.ld_out = io->ld_out;
+    ra.slot_ids = slot_ids;
+    ra.cu_seqlens = cu;
+    ra.n_seq = n_seq; ra.n_slots = p->n_slots; ra.n_tokens = n_tokens;
+    ra.hk = p->cfg.n_k_heads; ra.hv = p->cfg.n_v_heads; ra.D = p->D;
+    ra.err = p->err;
+    cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");
     return ok();
 }

@@ -1,0 +1,427 @@
+// gdn_decode.cu -- the fused GDN layer step as two kernels chained with
+// programmatic dependent launch (sm_100a).
+//
+// K1 gdn_prep_kernel (token-parallel, small): for every packed token and
+//    k-head group, the causal depthwise conv + SiLU of its q, k and v channels
+//    (reference rounding: S=1 -> bf16 products and bf16 sum, qwen3_5.rs:602-610;
+//    S>1 -> f32 conv1d, qwen3_5.rs:617-623), q/k RMSNorm with gains 1/dk and
+//    bf16(dk^-1/2) (qwen3_5.rs:636-639), beta and g (compiled_ops.rs:30-43) and
+//    silu(z) (qwen3_5.rs:664).  It writes one 1040-byte record per (v-head,
+//    token) into the pool's scratch: q | k | v | silu(z) (bf16 x 128 each) |
+//    g (f32) | beta (f32 holding the bf16 value) | pad.  K1 only reads the conv
+//    state.
+// K2 gdn_recur_kernel (persistent, one CTA per SM): work item = (sequence,
+//    v-head).  A producer warp streams each item's 64 KiB f32 state tile
+//    ([dv][dk], metal_gdn.rs:25-26) and its token records into a 3-stage
+//    shared-memory ring with bulk async copies completing on mbarriers; 8
+//    consumer warps pull the tile into registers (warp w: rows 16w..16w+15,
+//    lane l: columns 4l..4l+3), run the gated delta rule per token
+//    (metal_gdn.rs:37-62), write the gated RMSNorm output silu(z) *
+//    rms_norm(y, norm_w, eps) (qwen3_5.rs:660-665), store the tile back with
+//    128-bit evict-first stores, and write the conv-state windows back (the
+//    v channels of the item's head, and the q/k channels when the head is the
+//    first of its k-head group).  K1 has completed before any K2 write
+//    (griddepcontrol.wait), so no window is overwritten before it is read.
+//
+// PDL: K1 waits for its predecessor before touching memory, then lets K2
+// launch; K2 starts streaming state tiles (which K1 never touches) before its
+// own griddepcontrol.wait and only reads K1's records after it.
+#include "gdn_device.cuh"
+#include "gdn_internal.h"
+#include "gdn_ptx.cuh"
+
+namespace gdn {
+
+constexpr int K2_CONSUMER_WARPS = 8;
+constexpr int K2_CONSUMERS = K2_CONSUMER_WARPS * 32;
+constexpr int K2_THREADS = K2_CONSUMERS + 32;
+constexpr int NSTAGE = 3;
+constexpr int TILE_BYTES = DV * DK * 4;                               // 65536
+constexpr int STAGE_BYTES = TILE_BYTES + REC_PER_STAGE * REC_BYTES;   // 73856
+constexpr int K2_SMEM = NSTAGE * STAGE_BYTES + 2 * NSTAGE * 8 + NSTAGE * 16 + 2 * DV * 4 + 4 * 4;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;                     // 2 s bound on every wait
+static_assert(STAGE_BYTES % 16 == 0, "stage alignment");
+static_assert(K2_SMEM <= 232448, "shared memory budget");
+
+// ------------------------------------------------------------------ K1
+
+// Sequence owning packed token n: cu[i] <= n < cu[i+1].  Returns -1 if the tables do not cover n.
+__device__ __forceinline__ int find_seq(const int32_t* __restrict__ cu, int n_seq, int n) {
+    if (n < n_seq && __ldg(cu + n) == n && __ldg(cu + n + 1) == n + 1) return n;  // one token per sequence
+    int lo = 0, hi = n_seq;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(cu + mid) <= n) lo = mid; else hi = mid;
+    }
+    if (n_seq <= 0 || __ldg(cu + lo) > n || __ldg(cu + lo + 1) <= n) return -1;
+    return lo;
+}
+
+// silu(conv) of channel ch for token t of a sequence (t0, T) on slot `cs` (conv state [K-1][D]).
+__device__ __forceinline__ float conv_token(const PrepArgs& a, uint16_t* cs, int ch, int t0, int t, bool decode) {
+    const uint2 wu = __ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)ch * KC));
+    const float w[4] = {__uint_as_float(wu.x << 16), __uint_as_float(wu.x & 0xffff0000u),
+                        __uint_as_float(wu.y << 16), __uint_as_float(wu.y & 0xffff0000u)};
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < KC; ++j) {
+        const int p = t + j;  // index into padded = [conv_state (K-1 rows); tokens]
+        x[j] = p < KC - 1 ? bf2f(cs[(size_t)p * a.D + ch]) : bf2f(a.qkv[(long long)(t0 + p - (KC - 1)) * a.ld_qkv + ch]);
+    }
+    float acc;
+    if (decode) {
+        // A one-token sequence: this thread is the only reader of the channel's window in this call,
+        // so it shifts the window in place (new state = last K-1 rows of [old window; x]).
+#pragma unroll
+        for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = f2bf(x[j + 1]);
+        acc = rbf(x[0] * w[0]);
+        acc = acc + rbf(x[1] * w[1]);
+        acc = acc + rbf(x[2] * w[2]);
+        acc = acc + rbf(x[3] * w[3]);
+    } else {
+        acc = x[0] * w[0];
+        acc = acc + x[1] * w[1];
+        acc = acc + x[2] * w[2];
+        acc = acc + x[3] * w[3];
+    }
+    return silu_bf(rbf(acc));
+}
+
+__global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ float s_red[8];
+
+    const int n = blockIdx.x;
+    const int hk = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ratio = a.hv / a.hk;
+
+    const int seq = find_seq(a.cu_seqlens, a.n_seq, n);
+    if (seq < 0) {
+        if (tid == 0 && hk == 0) atomicOr(a.err, ERR_BAD_SEQLENS);
+        return;
+    }
+    const int t0 = __ldg(a.cu_seqlens + seq);
+    const int T = __ldg(a.cu_seqlens + seq + 1) - t0;
+    const int slot = __ldg(a.slot_ids + seq);
+    if (slot < 0 || slot >= a.n_slots || t0 + T > a.n_tokens) {
+        if (tid == 0 && hk == 0 && n == t0) atomicOr(a.err, slot < 0 || slot >= a.n_slots ? ERR_BAD_SLOT : ERR_BAD_SEQLENS);
+        return;
+    }
+    const int t = n - t0;
+    const bool decode = (T == 1);
+    uint16_t* cs = a.conv + (size_t)slot * (KC - 1) * a.D;
+
+    // q (tid < 128) or k (tid >= 128) channel of this k-head, then its RMSNorm over 128 channels
+    const bool low = tid < 128;
+    const int c = tid & 127;
+    const int qk_ch = (low ? 0 : a.hk * DK) + hk * DK + c;
+    const float o = conv_token(a, cs, qk_ch, t0, t, decode);
+    const float ss = warp_sum(o * o);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    const float tot = low ? (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]) : (s_red[4] + s_red[5]) + (s_red[6] + s_red[7]);
+    const float nrm = 1.0f / sqrtf(tot / (float)DK + 1e-6f);
+    const float gain = low ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
+    const uint16_t qk_val = f2bf(rbf(o * nrm) * gain);
+
+    // records of the v-heads of this k-head group
+    for (int j = 0; j < ratio; ++j) {
+        const int hv = hk * ratio + j;
+        uint8_t* rec = a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES;
+        reinterpret_cast<uint16_t*>(rec)[(low ? 0 : 128) + c] = qk_val;
+    }
+    // v channels and silu(z) of those heads: 128 * ratio values each, 256 threads
+    for (int idx = tid; idx < ratio * DV; idx += 256) {
+        const int hv = hk * ratio + idx / DV;
+        const int cv = idx % DV;
+        uint8_t* rec = a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES;
+        const float v = conv_token(a, cs, 2 * a.hk * DK + hv * DV + cv, t0, t, decode);
+        reinterpret_cast<uint16_t*>(rec)[256 + cv] = f2bf(v);
+        const float zs = silu_bf(bf2f(a.z[(long long)n * a.ld_z + (long long)hv * DV + cv]));
+        reinterpret_cast<uint16_t*>(rec)[384 + cv] = f2bf(zs);
+    }
+    if (tid < ratio) {
+        const int hv = hk * ratio + tid;
+        const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
+        const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
+        const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+        float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
+        gb[0] = expf(-(expf(a.A_log[hv]) * sp));
+        gb[1] = rbf(sigmoid_f32(b));
+    }
+}
+
+// ------------------------------------------------------------------ K2
+
+// All 288 threads meet here.  Normally every issued copy was consumed; after a
+// timed-out wait, thread 0 waits (bounded) for copies still in flight so the
+// CTA never exits with an async write pending into its shared memory.
+__device__ __forceinline__ void drain_and_exit(uint64_t* full, volatile int* s_issued, volatile int* s_consumed,
+                                               int tid) {
+    __syncwarp();
+    named_bar_sync(2, K2_THREADS);
+    if (tid == 0) {
+        const int issued = *s_issued, consumed = *s_consumed;
+        for (int k = consumed; k < issued; ++k)
+            mbar_wait_bounded(&full[k % NSTAGE], (uint32_t)(k / NSTAGE) & 1u, WAIT_LIMIT_NS);
+    }
+}
+
+// Per-stage header written by the producer before it arms the stage's full barrier.
+struct StageHdr {
+    int slot, hv, t0, T;  // T < 0: end of this CTA's work
+};
+
+__global__ void __launch_bounds__(K2_THREADS, 1) gdn_recur_kernel(const RecurArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES);
+    uint64_t* empty = full + NSTAGE;
+    StageHdr* hdr = reinterpret_cast<StageHdr*>(empty + NSTAGE);
+    float* s_y = reinterpret_cast<float*>(hdr + NSTAGE);   // [2][DV], double-buffered per token
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_y + 2 * DV);
+    volatile int* s_issued = s_abort + 1;    // items whose copies the producer issued
+    volatile int* s_consumed = s_abort + 2;  // items the consumers took out of the ring
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_items = a.n_seq * a.hv;
+    const int ratio = a.hv / a.hk;
+
+    if (tid == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], K2_CONSUMER_WARPS);
+        }
+        *s_abort = 0;
+        *s_issued = 0;
+        *s_consumed = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == K2_CONSUMER_WARPS) {
+        // ------------------------------------------------ producer (one lane)
+        if (lane == 0) {
+            const float* st_src = a.rec_in ? a.rec_in : a.rec;
+            int k = 0;
+            bool waited = false;
+            int pend_stage[NSTAGE], pend_hv[NSTAGE], pend_t0[NSTAGE], pend_n[NSTAGE];
+            int npend = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int seq = item / a.hv;
+                const int hv = item - seq * a.hv;
+                const int t0 = __ldg(a.cu_seqlens + seq);
+                const int T = __ldg(a.cu_seqlens + seq + 1) - t0;
+                const int slot = __ldg(a.slot_ids + seq);
+                const bool bad_slot = slot < 0 || slot >= a.n_slots;
+                const bool bad_len = T < 0 || t0 < 0 || t0 + T > a.n_tokens;
+                if (bad_slot || bad_len) {
+                    if (hv == 0) atomicOr(a.err, (bad_slot ? ERR_BAD_SLOT : 0) | (bad_len ? ERR_BAD_SEQLENS : 0));
+                    continue;
+                }
+                if (T == 0) continue;
+                const int s = k % NSTAGE;
+                const uint32_t ph = (uint32_t)(k / NSTAGE) & 1u;
+                if (k >= NSTAGE && !mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_LIMIT_NS)) {
+                    atomicOr(a.err, ERR_TIMEOUT);
+                    *s_abort = 1;
+                    ok = false;
+                    break;
+                }
+                const int nrec = T < REC_PER_STAGE ? T : REC_PER_STAGE;
+                uint8_t* stage = smem + s * STAGE_BYTES;
+                hdr[s].slot = slot;
+                hdr[s].hv = hv;
+                hdr[s].t0 = t0;
+                hdr[s].T = T;
+                mbar_arrive_expect_tx(&full[s], TILE_BYTES + nrec * REC_BYTES);
+                bulk_g2s(stage, st_src + ((size_t)slot * a.hv + hv) * (DV * DK), TILE_BYTES, &full[s]);
+                if (!waited) {
+                    pend_stage[npend] = s; pend_hv[npend] = hv; pend_t0[npend] = t0; pend_n[npend] = nrec;
+                    if (++npend == NSTAGE) {
+                        pdl_wait();
+                        waited = true;
+                        for (int q = 0; q < npend; ++q)
+                            bulk_g2s(smem + pend_stage[q] * STAGE_BYTES + TILE_BYTES,
+                                     a.recs + ((long long)pend_hv[q] * a.rec_cap + pend_t0[q]) * REC_BYTES,
+                                     pend_n[q] * REC_BYTES, &full[pend_stage[q]]);
+                        npend = 0;
+                    }
+                } else {
+                    bulk_g2s(stage + TILE_BYTES, a.recs + ((long long)hv * a.rec_cap + t0) * REC_BYTES,
+                             nrec * REC_BYTES, &full[s]);
+                }
+                ++k;
+            }
+            if (!waited) {
+                pdl_wait();
+                for (int q = 0; q < npend; ++q)
+                    bulk_g2s(smem + pend_stage[q] * STAGE_BYTES + TILE_BYTES,
+                             a.recs + ((long long)pend_hv[q] * a.rec_cap + pend_t0[q]) * REC_BYTES,
+                             pend_n[q] * REC_BYTES, &full[pend_stage[q]]);
+            }
+            *s_issued = k;
+            if (ok) {
+                // end-of-work marker in the next stage
+                const int s = k % NSTAGE;
+                const uint32_t ph = (uint32_t)(k / NSTAGE) & 1u;
+                if (k < NSTAGE || mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_LIMIT_NS)) {
+                    hdr[s].T = -1;
+                    mbar_arrive(&full[s]);
+                } else {
+                    atomicOr(a.err, ERR_TIMEOUT);
+                    *s_abort = 1;
+                }
+            }
+        }
+        drain_and_exit(full, s_issued, s_consumed, tid);
+        return;
+    }
+
+    // ---------------------------------------------------- consumers (256 threads)
+    pdl_wait();
+    const int oc = warp * 16 + (lane & 15);          // output column of this lane in the epilogue
+    const float nw = bf2f(a.norm_w[oc]);
+    const int myrow = warp * RPW + (lane >> 1);
+    int buf = 0;
+    int k = 0;
+    while (true) {
+        const int s = k % NSTAGE;
+        const uint32_t ph = (uint32_t)(k / NSTAGE) & 1u;
+        if (!mbar_wait_bounded(&full[s], ph, WAIT_LIMIT_NS)) {
+            atomicOr(a.err, ERR_TIMEOUT);
+            *s_abort = 1;
+        }
+        if (*s_abort) break;
+        const StageHdr h = hdr[s];
+        if (h.T < 0) break;
+        ++k;
+
+        const uint8_t* stage = smem + s * STAGE_BYTES;
+        const float* tile = reinterpret_cast<const float*>(stage);
+        float4 S[RPW];
+#pragma unroll
+        for (int j = 0; j < RPW; ++j) S[j] = *reinterpret_cast<const float4*>(tile + (warp * RPW + j) * DK + lane * 4);
+
+        for (int t = 0; t < h.T; ++t) {
+            const uint8_t* rec = t < REC_PER_STAGE ? stage + TILE_BYTES + t * REC_BYTES
+                                                   : a.recs + ((long long)h.hv * a.rec_cap + h.t0 + t) * REC_BYTES;
+            const uint2 qu = *reinterpret_cast<const uint2*>(rec + lane * 8);
+            const uint2 ku = *reinterpret_cast<const uint2*>(rec + 256 + lane * 8);
+            const float vv = bf2f(reinterpret_cast<const uint16_t*>(rec)[256 + myrow]);
+            const float zs = bf2f(reinterpret_cast<const uint16_t*>(rec)[384 + oc]);
+            const float gt = reinterpret_cast<const float*>(rec + 1024)[0];
+            const float bt = reinterpret_cast<const float*>(rec + 1024)[1];
+            if (t == h.T - 1) {
+                // every read of this stage is done: hand it back to the producer
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            const float4 q4 = make_float4(__uint_as_float(qu.x << 16), __uint_as_float(qu.x & 0xffff0000u),
+                                          __uint_as_float(qu.y << 16), __uint_as_float(qu.y & 0xffff0000u));
+            const float4 k4 = make_float4(__uint_as_float(ku.x << 16), __uint_as_float(ku.x & 0xffff0000u),
+                                          __uint_as_float(ku.y << 16), __uint_as_float(ku.y & 0xffff0000u));
+            float p[RPW];
+#pragma unroll
+            for (int j = 0; j < RPW; ++j) {
+                S[j].x *= gt; S[j].y *= gt; S[j].z *= gt; S[j].w *= gt;
+                p[j] = S[j].x * k4.x + S[j].y * k4.y + S[j].z * k4.z + S[j].w * k4.w;
+            }
+            const float kv = reduce_scatter16(p, lane);
+            const float delta = (vv - kv) * bt;
+#pragma unroll
+            for (int j = 0; j < RPW; ++j) {
+                const float d = __shfl_sync(0xffffffffu, delta, 2 * j);
+                S[j].x += k4.x * d; S[j].y += k4.y * d; S[j].z += k4.z * d; S[j].w += k4.w * d;
+                p[j] = S[j].x * q4.x + S[j].y * q4.y + S[j].z * q4.z + S[j].w * q4.w;
+            }
+            const float yv = reduce_scatter16(p, lane);
+            float* sy = s_y + buf * DV;
+            if (!(lane & 1)) sy[myrow] = rbf(yv);
+            named_bar_sync(1, K2_CONSUMERS);
+            // gated RMSNorm epilogue: every warp reduces all 128 y (same order, same result),
+            // lanes 0..15 of warp w write output columns 16w..16w+15
+            const float4 y4 = *reinterpret_cast<const float4*>(sy + lane * 4);
+            const float ss = warp_sum(y4.x * y4.x + y4.y * y4.y + y4.z * y4.z + y4.w * y4.w);
+            if (lane < 16) {
+                const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
+                const float yn = rbf(rbf(sy[oc] * nrm) * nw);
+                a.out[(long long)(h.t0 + t) * a.ld_out + (long long)h.hv * DV + oc] = f2bf(zs * yn);
+            }
+            buf ^= 1;
+        }
+
+        // state tile back to the pool (evict-first: it is not re-read in this step)
+        float* dst = a.rec + ((size_t)h.slot * a.hv + h.hv) * (DV * DK) + (warp * RPW) * DK + lane * 4;
+#pragma unroll
+        for (int j = 0; j < RPW; ++j) __stcs(reinterpret_cast<float4*>(dst + j * DK), S[j]);
+
+        if (h.T > 1) {
+            // conv-state windows of a multi-token sequence: the last K-1 rows of [old window; tokens]
+            // (one-token sequences were shifted in place by the prep kernel)
+            uint16_t* cs = a.conv + (size_t)h.slot * (KC - 1) * a.D;
+            const int hk = h.hv / ratio;
+            for (int idx = tid; idx < DV + ((h.hv % ratio == 0) ? 2 * DK : 0); idx += K2_CONSUMERS) {
+                const int ch = idx < DV ? 2 * a.hk * DK + h.hv * DV + idx
+                                        : ((idx - DV) < DK ? hk * DK + (idx - DV) : a.hk * DK + hk * DK + (idx - DV - DK));
+                uint16_t w[KC - 1];
+#pragma unroll
+                for (int j = 0; j < KC - 1; ++j) {
+                    const int p = h.T + j;
+                    w[j] = p < KC - 1 ? cs[(size_t)p * a.D + ch]
+                                      : a.qkv[(long long)(h.t0 + p - (KC - 1)) * a.ld_qkv + ch];
+                }
+#pragma unroll
+                for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = w[j];
+            }
+        }
+    }
+    if (tid == 0) *s_consumed = k;
+    drain_and_exit(full, s_issued, s_consumed, tid);
+}
+
+static int g_num_sms[64] = {0};
+
+cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (g_num_sms[dev] == 0) {
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(gdn_recur_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K2_SMEM);
+        if (e != cudaSuccess) return e;
+        g_num_sms[dev] = sms;
+    }
+    if (p.n_tokens == 0 || r.n_seq == 0) return cudaSuccess;
+
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+
+    cudaLaunchConfig_t c1 = {};
+    c1.gridDim = dim3((unsigned)p.n_tokens, (unsigned)p.hk, 1);
+    c1.blockDim = dim3(256, 1, 1);
+    c1.stream = stream;
+    c1.attrs = attr;
+    c1.numAttrs = 1;
+    e = cudaLaunchKernelEx(&c1, gdn_prep_kernel, p);
+    if (e != cudaSuccess) return e;
+
+    const int n_items = r.n_seq * r.hv;
+    cudaLaunchConfig_t c2 = {};
+    c2.gridDim = dim3((unsigned)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]), 1, 1);
+    c2.blockDim = dim3(K2_THREADS, 1, 1);
+    c2.dynamicSmemBytes = K2_SMEM;
+    c2.stream = stream;
+    c2.attrs = attr;
+    c2.numAttrs = 1;
+    return cudaLaunchKernelEx(&c2, gdn_recur_kernel, r);
+}
+
+}  // namespace gdn

@@ -17,6 +17,7 @@ constexpr int RPW = DV / NW;   // state rows (dv) per warp = 16
 // Error bits recorded in the pool's device error word (1 << GDN_E_*).
 constexpr int ERR_BAD_SLOT = 1 << 3;
 constexpr int ERR_BAD_SEQLENS = 1 << 4;
+constexpr int ERR_TIMEOUT = 1 << 7;  // a bounded device wait gave up (GDN_E_DEVICE)
 
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
 __device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }

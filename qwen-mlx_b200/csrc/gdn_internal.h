@@ -43,7 +43,47 @@ struct StepArgs {
     int32_t* err;
 };
 
+// Per-(v-head, token) record written by the prep kernel and streamed by the
+// recurrence kernel: q | k | v | silu(z) (bf16 x 128 each) | g f32 | beta f32 | pad.
+constexpr int REC_BYTES = 1040;
+constexpr int REC_PER_STAGE = 4;   // token records staged with each state tile
+
+struct PrepArgs {
+    const uint16_t* qkv; long long ld_qkv;
+    const uint16_t* z; long long ld_z;
+    const uint16_t* ab; long long ld_ab;
+    uint16_t* conv;              // layer slice of the conv-state pool [n_slots][KC-1][D]
+    const uint16_t* conv_w;
+    const float* A_log;
+    const float* dt_bias;
+    const int32_t* slot_ids;
+    const int32_t* cu_seqlens;
+    int32_t n_seq, n_slots, n_tokens;
+    int32_t hk, hv, D;
+    uint8_t* rec;                // scratch records [Hv][rec_cap][REC_BYTES]
+    long long rec_cap;
+    int32_t* err;
+};
+
+struct RecurArgs {
+    float* rec;                  // state written here [n_slots][Hv][DV][DK]
+    const float* rec_in;         // read from here when non-null, else from rec
+    uint16_t* conv;              // conv-state pool slice (windows written back)
+    const uint16_t* qkv; long long ld_qkv;
+    const uint8_t* recs;
+    long long rec_cap;
+    const uint16_t* norm_w;
+    float eps;
+    uint16_t* out; long long ld_out;
+    const int32_t* slot_ids;
+    const int32_t* cu_seqlens;
+    int32_t n_seq, n_slots, n_tokens;
+    int32_t hk, hv, D;
+    int32_t* err;
+};
+
 cudaError_t launch_layer_step(const StepArgs& a, cudaStream_t stream);
+cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
 cudaError_t launch_recurrence(const StepArgs& a, cudaStream_t stream);
 cudaError_t launch_beta_g(const uint16_t* ab, long long ld_ab, int n_tokens, int hv, const float* A_log,
                           const float* dt_bias, uint16_t* beta, float* g, cudaStream_t stream);

@@ -127,6 +127,9 @@ class StatePool:
         abi.call("gdn_pool_bytes", self.h, C.byref(n))
         return int(n.value)
 
+    def reserve_tokens(self, max_tokens: int):
+        abi.call("gdn_pool_reserve_tokens", self.h, int(max_tokens))
+
     def layer_state_ptrs(self, layer: int):
         rec, conv = C.c_void_p(), C.c_void_p()
         abi.call("gdn_pool_layer_state", self.h, layer, C.byref(rec), C.byref(conv))
