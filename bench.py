@@ -257,7 +257,7 @@ def run_ours(args):
 
     cfg = synth.GdnConfig(n_layers=N_LAYERS)
     B = args.batch
-    sweep_bs = [] if (args.no_sweep or world > 1) else [1, 8, 64, 256, 1024, 2048]
+    sweep_bs = [] if (args.no_sweep or world > 1) else [1, 2, 4, 8, 16, 32, 64, 256, 1024, 2048]
     n_slots = max([B] + sweep_bs)
     pool = gdn.StatePool(cfg, n_slots=n_slots, device=local)
     cudart = _cudart()

@@ -307,12 +307,9 @@ static gdn::StepArgs base_args(gdn_pool* p, int32_t layer) {
     gdn::StepArgs a;
     std::memset(&a, 0, sizeof a);
     a.rec = p->rec + (size_t)layer * p->n_slots * p->rec_slot_elems;
-    a.conv = p->conv + (size_t)layer * p->n_slots * p->conv_slot_elems;
     a.n_slots = p->n_slots;
     a.hk = p->cfg.n_k_heads;
     a.hv = p->cfg.n_v_heads;
-    a.D = p->D;
-    a.eps = p->cfg.rms_norm_eps;
     a.err = p->err;
     return a;
 }

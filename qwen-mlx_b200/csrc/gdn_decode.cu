@@ -45,9 +45,8 @@ static_assert(K2_SMEM <= 232448, "shared memory budget");
 
 // ------------------------------------------------------------------ K1
 
-// Sequence owning packed token n: cu[i] <= n < cu[i+1].  Returns -1 if the tables do not cover n.
+// Sequence owning packed token n: cu[i] <= n < cu[i+1] (binary search).  -1 if the tables do not cover n.
 __device__ __forceinline__ int find_seq(const int32_t* __restrict__ cu, int n_seq, int n) {
-    if (n < n_seq && __ldg(cu + n) == n && __ldg(cu + n + 1) == n + 1) return n;  // one token per sequence
     int lo = 0, hi = n_seq;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -57,23 +56,17 @@ __device__ __forceinline__ int find_seq(const int32_t* __restrict__ cu, int n_se
     return lo;
 }
 
-// silu(conv) of channel ch for token t of a sequence (t0, T) on slot `cs` (conv state [K-1][D]).
-__device__ __forceinline__ float conv_token(const PrepArgs& a, uint16_t* cs, int ch, int t0, int t, bool decode) {
-    const uint2 wu = __ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)ch * KC));
-    const float w[4] = {__uint_as_float(wu.x << 16), __uint_as_float(wu.x & 0xffff0000u),
-                        __uint_as_float(wu.y << 16), __uint_as_float(wu.y & 0xffff0000u)};
-    float x[4];
-#pragma unroll
-    for (int j = 0; j < KC; ++j) {
-        const int p = t + j;  // index into padded = [conv_state (K-1 rows); tokens]
-        x[j] = p < KC - 1 ? bf2f(cs[(size_t)p * a.D + ch]) : bf2f(a.qkv[(long long)(t0 + p - (KC - 1)) * a.ld_qkv + ch]);
-    }
+__device__ __forceinline__ void unpack_w4(uint2 wu, float (&w)[4]) {
+    w[0] = __uint_as_float(wu.x << 16);
+    w[1] = __uint_as_float(wu.x & 0xffff0000u);
+    w[2] = __uint_as_float(wu.y << 16);
+    w[3] = __uint_as_float(wu.y & 0xffff0000u);
+}
+
+// silu(sum_j w[j] * x[j]) with the reference's decode (bf16 products + bf16 sum) or conv1d (f32) rounding.
+__device__ __forceinline__ float conv_silu(const float (&x)[4], const float (&w)[4], bool decode) {
     float acc;
     if (decode) {
-        // A one-token sequence: this thread is the only reader of the channel's window in this call,
-        // so it shifts the window in place (new state = last K-1 rows of [old window; x]).
-#pragma unroll
-        for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = f2bf(x[j + 1]);
         acc = rbf(x[0] * w[0]);
         acc = acc + rbf(x[1] * w[1]);
         acc = acc + rbf(x[2] * w[2]);
@@ -87,6 +80,23 @@ __device__ __forceinline__ float conv_token(const PrepArgs& a, uint16_t* cs, int
     return silu_bf(rbf(acc));
 }
 
+// Conv taps x[0..3] = padded[t..t+3] of channel ch, padded = [conv window (K-1 rows); tokens].
+// x[3] (the current token) is passed in; the window rows come from `cs` or from earlier tokens.
+__device__ __forceinline__ void load_taps(const PrepArgs& a, const uint16_t* cs, int ch, int t0, int t, float xcur,
+                                          float (&x)[4]) {
+#pragma unroll
+    for (int j = 0; j < KC - 1; ++j) {
+        const int p = t + j;
+        x[j] = p < KC - 1 ? bf2f(cs[(size_t)p * a.D + ch]) : bf2f(a.qkv[(long long)(t0 + p - (KC - 1)) * a.ld_qkv + ch]);
+    }
+    x[KC - 1] = xcur;
+}
+
+// One CTA per (packed token, k-head); 256 threads = 128 q + 128 k channels, and the
+// v channels / z columns of the k-head's v-heads (Hv/Hk * 128 of each).
+// Loads are issued in two batches: everything indexed by the token (inputs, weights,
+// and the routing entries of the sequence the token belongs to when each sequence
+// has one token), then the slot's conv windows.
 __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     pdl_wait();
     pdl_launch_dependents();
@@ -96,15 +106,54 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     const int hk = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ratio = a.hv / a.hk;
+    const bool low = tid < 128;
+    const int c = tid & 127;
+    const int qk_ch = (low ? 0 : a.hk * DK) + hk * DK + c;
+    const int nv = ratio * DV;             // v channels of this k-head group
+    const int v_idx0 = tid;                // first v channel handled by this thread (ratio <= 2: the only one)
 
-    const int seq = find_seq(a.cu_seqlens, a.n_seq, n);
-    if (seq < 0) {
-        if (tid == 0 && hk == 0) atomicOr(a.err, ERR_BAD_SEQLENS);
-        return;
+    // ---- batch 1: token-indexed loads (no dependence on the routing tables)
+    const int guess = n < a.n_seq ? n : a.n_seq - 1;
+    const int cu_g0 = __ldg(a.cu_seqlens + guess);
+    const int cu_g1 = __ldg(a.cu_seqlens + guess + 1);
+    const int slot_g = __ldg(a.slot_ids + guess);
+    const float x_qk = bf2f(a.qkv[(long long)n * a.ld_qkv + qk_ch]);
+    float w_qk[4];
+    unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)qk_ch * KC)), w_qk);
+    float x_v = 0.f, z_v = 0.f, w_v[4] = {0.f, 0.f, 0.f, 0.f};
+    int v_ch = 0, v_hv = 0, v_c = 0;
+    if (v_idx0 < nv) {
+        v_hv = hk * ratio + v_idx0 / DV;
+        v_c = v_idx0 % DV;
+        v_ch = 2 * a.hk * DK + v_hv * DV + v_c;
+        x_v = bf2f(a.qkv[(long long)n * a.ld_qkv + v_ch]);
+        z_v = bf2f(a.z[(long long)n * a.ld_z + (long long)v_hv * DV + v_c]);
+        unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)v_ch * KC)), w_v);
+    }
+    float gb_b = 0.f, gb_a = 0.f, gb_alog = 0.f, gb_dt = 0.f;
+    if (tid < ratio) {
+        const int hv = hk * ratio + tid;
+        gb_b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
+        gb_a = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
+        gb_alog = a.A_log[hv];
+        gb_dt = a.dt_bias[hv];
+    }
+
+    // ---- routing
+    int seq, slot;
+    if (cu_g0 <= n && n < cu_g1) {
+        seq = guess;
+        slot = slot_g;
+    } else {
+        seq = find_seq(a.cu_seqlens, a.n_seq, n);
+        if (seq < 0) {
+            if (tid == 0 && hk == 0) atomicOr(a.err, ERR_BAD_SEQLENS);
+            return;
+        }
+        slot = __ldg(a.slot_ids + seq);
     }
     const int t0 = __ldg(a.cu_seqlens + seq);
     const int T = __ldg(a.cu_seqlens + seq + 1) - t0;
-    const int slot = __ldg(a.slot_ids + seq);
     if (slot < 0 || slot >= a.n_slots || t0 + T > a.n_tokens) {
         if (tid == 0 && hk == 0 && n == t0) atomicOr(a.err, slot < 0 || slot >= a.n_slots ? ERR_BAD_SLOT : ERR_BAD_SEQLENS);
         return;
@@ -113,11 +162,23 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     const bool decode = (T == 1);
     uint16_t* cs = a.conv + (size_t)slot * (KC - 1) * a.D;
 
-    // q (tid < 128) or k (tid >= 128) channel of this k-head, then its RMSNorm over 128 channels
-    const bool low = tid < 128;
-    const int c = tid & 127;
-    const int qk_ch = (low ? 0 : a.hk * DK) + hk * DK + c;
-    const float o = conv_token(a, cs, qk_ch, t0, t, decode);
+    // ---- batch 2: conv windows (and earlier tokens of a multi-token sequence)
+    float xq[4], xv[4] = {0.f, 0.f, 0.f, 0.f};
+    load_taps(a, cs, qk_ch, t0, t, x_qk, xq);
+    if (v_idx0 < nv) load_taps(a, cs, v_ch, t0, t, x_v, xv);
+    if (decode) {
+        // A one-token sequence: this thread is the only reader of these windows in this call,
+        // so it shifts them in place (new window = last K-1 rows of [old window; x]).
+#pragma unroll
+        for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + qk_ch] = f2bf(xq[j + 1]);
+        if (v_idx0 < nv) {
+#pragma unroll
+            for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + v_ch] = f2bf(xv[j + 1]);
+        }
+    }
+
+    // ---- q / k: conv, SiLU, RMSNorm with the scale folded into the gain
+    const float o = conv_silu(xq, w_qk, decode);
     const float ss = warp_sum(o * o);
     if (lane == 0) s_red[warp] = ss;
     __syncthreads();
@@ -125,31 +186,40 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     const float nrm = 1.0f / sqrtf(tot / (float)DK + 1e-6f);
     const float gain = low ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
     const uint16_t qk_val = f2bf(rbf(o * nrm) * gain);
-
-    // records of the v-heads of this k-head group
     for (int j = 0; j < ratio; ++j) {
-        const int hv = hk * ratio + j;
-        uint8_t* rec = a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES;
+        uint8_t* rec = a.rec + ((long long)(hk * ratio + j) * a.rec_cap + n) * REC_BYTES;
         reinterpret_cast<uint16_t*>(rec)[(low ? 0 : 128) + c] = qk_val;
     }
-    // v channels and silu(z) of those heads: 128 * ratio values each, 256 threads
-    for (int idx = tid; idx < ratio * DV; idx += 256) {
+    // ---- v and silu(z)
+    if (v_idx0 < nv) {
+        uint8_t* rec = a.rec + ((long long)v_hv * a.rec_cap + n) * REC_BYTES;
+        reinterpret_cast<uint16_t*>(rec)[256 + v_c] = f2bf(conv_silu(xv, w_v, decode));
+        reinterpret_cast<uint16_t*>(rec)[384 + v_c] = f2bf(silu_bf(z_v));
+    }
+    // groups wider than 256 v channels (Hv/Hk > 2): remaining channels, one pass each
+    for (int idx = 256 + tid; idx < nv; idx += 256) {
         const int hv = hk * ratio + idx / DV;
         const int cv = idx % DV;
+        const int ch = 2 * a.hk * DK + hv * DV + cv;
+        float w4[4], x4[4];
+        unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)ch * KC)), w4);
+        load_taps(a, cs, ch, t0, t, bf2f(a.qkv[(long long)n * a.ld_qkv + ch]), x4);
+        if (decode) {
+#pragma unroll
+            for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = f2bf(x4[j + 1]);
+        }
         uint8_t* rec = a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES;
-        const float v = conv_token(a, cs, 2 * a.hk * DK + hv * DV + cv, t0, t, decode);
-        reinterpret_cast<uint16_t*>(rec)[256 + cv] = f2bf(v);
-        const float zs = silu_bf(bf2f(a.z[(long long)n * a.ld_z + (long long)hv * DV + cv]));
-        reinterpret_cast<uint16_t*>(rec)[384 + cv] = f2bf(zs);
+        reinterpret_cast<uint16_t*>(rec)[256 + cv] = f2bf(conv_silu(x4, w4, decode));
+        reinterpret_cast<uint16_t*>(rec)[384 + cv] =
+            f2bf(silu_bf(bf2f(a.z[(long long)n * a.ld_z + (long long)hv * DV + cv])));
     }
+    // ---- gates (compiled_beta_g)
     if (tid < ratio) {
         const int hv = hk * ratio + tid;
-        const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
-        const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
-        const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+        const float sp = logf(expf(gb_a + gb_dt) + 1.0f);
         float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
-        gb[0] = expf(-(expf(a.A_log[hv]) * sp));
-        gb[1] = rbf(sigmoid_f32(b));
+        gb[0] = expf(-(expf(gb_alog) * sp));
+        gb[1] = rbf(sigmoid_f32(gb_b));
     }
 }
 
@@ -210,12 +280,27 @@ __global__ void __launch_bounds__(K2_THREADS, 1) gdn_recur_kernel(const RecurArg
             int pend_stage[NSTAGE], pend_hv[NSTAGE], pend_t0[NSTAGE], pend_n[NSTAGE];
             int npend = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-                const int seq = item / a.hv;
-                const int hv = item - seq * a.hv;
-                const int t0 = __ldg(a.cu_seqlens + seq);
-                const int T = __ldg(a.cu_seqlens + seq + 1) - t0;
-                const int slot = __ldg(a.slot_ids + seq);
+            // routing entries of the next item are loaded one iteration ahead
+            int item = blockIdx.x;
+            int nx_t0 = 0, nx_t1 = 0, nx_slot = 0;
+            if (item < n_items) {
+                const int sq = item / a.hv;
+                nx_t0 = __ldg(a.cu_seqlens + sq);
+                nx_t1 = __ldg(a.cu_seqlens + sq + 1);
+                nx_slot = __ldg(a.slot_ids + sq);
+            }
+            for (; item < n_items && ok; item += gridDim.x) {
+                const int hv = item % a.hv;
+                const int t0 = nx_t0;
+                const int T = nx_t1 - nx_t0;
+                const int slot = nx_slot;
+                const int next = item + gridDim.x;
+                if (next < n_items) {
+                    const int sq = next / a.hv;
+                    nx_t0 = __ldg(a.cu_seqlens + sq);
+                    nx_t1 = __ldg(a.cu_seqlens + sq + 1);
+                    nx_slot = __ldg(a.slot_ids + sq);
+                }
                 const bool bad_slot = slot < 0 || slot >= a.n_slots;
                 const bool bad_len = T < 0 || t0 < 0 || t0 + T > a.n_tokens;
                 if (bad_slot || bad_len) {

@@ -10,7 +10,7 @@ namespace gdn {
 constexpr int DK = 128;        // head_k_dim (specialised)
 constexpr int DV = 128;        // head_v_dim (specialised)
 constexpr int KC = 4;          // conv taps (linear_conv_kernel_dim)
-constexpr int NT = 256;        // threads per CTA of the step kernel
+constexpr int NT = 256;        // threads per CTA of the recurrence kernel
 constexpr int NW = NT / 32;    // warps per CTA
 constexpr int RPW = DV / NW;   // state rows (dv) per warp = 16
 
@@ -67,14 +67,6 @@ __device__ __forceinline__ float reduce_scatter16(const float (&p)[16], int lane
     float keep = b1 ? a2[1] : a2[0];
     float a1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
     return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
-}
-
-// Thread-block-cluster split barrier (all threads of every CTA in the cluster).
-__device__ __forceinline__ void cluster_arrive_release() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
 
 }  // namespace gdn

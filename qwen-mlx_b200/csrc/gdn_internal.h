@@ -11,28 +11,17 @@ namespace gdn {
 constexpr int DK_ABI = 128;
 constexpr int DV_ABI = 128;
 
-// Arguments of the step / recurrence kernel.  Pointers are device pointers.
+// Arguments of the stand-alone recurrence kernel.  Pointers are device pointers.
 struct StepArgs {
     // state (one layer's slice of the pool, or dense [B] arrays for the functional form)
     float* rec;            // [n_slots][Hv][DV][DK] f32, written
     const float* rec_in;   // read from here when non-null (functional form), else from rec
-    uint16_t* conv;        // [n_slots][KC-1][D] bf16 (fused mode)
     // routing
     const int32_t* slot_ids;    // [n_seq]; null: slot = sequence index
     const int32_t* cu_seqlens;  // [n_seq+1]; null: T_dense tokens per sequence
     int32_t n_seq, n_slots, T_dense, n_tokens;
-    int32_t hk, hv, D;
-    // fused-mode inputs and parameters
-    const uint16_t* qkv; long long ld_qkv;
-    const uint16_t* z; long long ld_z;
-    const uint16_t* ab; long long ld_ab;
-    uint16_t* out; long long ld_out;
-    const uint16_t* conv_w;
-    const float* A_log;
-    const float* dt_bias;
-    const uint16_t* norm_w;
-    float eps;
-    // recurrence-mode inputs / output
+    int32_t hk, hv;
+    // inputs / output
     const uint16_t* q;
     const uint16_t* k;
     const uint16_t* v;
@@ -82,7 +71,6 @@ struct RecurArgs {
     int32_t* err;
 };
 
-cudaError_t launch_layer_step(const StepArgs& a, cudaStream_t stream);
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
 cudaError_t launch_recurrence(const StepArgs& a, cudaStream_t stream);
 cudaError_t launch_beta_g(const uint16_t* ab, long long ld_ab, int n_tokens, int hv, const float* A_log,
