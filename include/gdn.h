@@ -178,6 +178,27 @@ GDN_API int gdn_gated_delta_kernel(const gdn_bf16* q, const gdn_bf16* k, const g
 GDN_API int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
                const float* dt_bias, gdn_bf16* beta, float* g, void* stream);
 
+/* ------------------------------------------------------- no-allocation variant
+ * No counterpart in the reference.  The fused layer step of gdn_layer_step for
+ * callers that may not allocate device memory -- e.g. an engine that reserves a
+ * fixed device arena at start-up and forbids cudaMalloc afterwards, or a host
+ * framework whose caching allocator owns all device memory.  The caller passes
+ * the state of ONE layer in memory it owns: rec_state [n_slots][Hv][dv][dk] f32
+ * (16-byte aligned) and conv_state [n_slots][K-1][D] bf16, plus the same weights,
+ * step buffers and DEVICE routing tables as gdn_layer_step.  The step's scratch
+ * comes from a fixed array compiled into this library (4,259,840 bytes on every
+ * device that loads it, kept until exit): at most 4096 records, i.e.
+ * n_tokens * n_v_heads <= 4096 (128 tokens per call at 32 v-heads); larger calls
+ * return GDN_E_INVALID.  This function never allocates.  Its first call on a
+ * device looks up the scratch's device address; make that first call before
+ * capturing a stream into a CUDA graph.  All calls share the scratch, so calls
+ * that overlap on the GPU (other streams or threads) race: serialise them.
+ * Asynchronous on `stream`; device-side bounds-check bits are not reported, so
+ * validate the tables with gdn_validate_tables. */
+GDN_API int gdn_layer_step_noalloc(const gdn_config* cfg, int32_t n_slots, float* rec_state, gdn_bf16* conv_state,
+                                   const gdn_layer_weights* w, const gdn_step_io* io, const int32_t* slot_ids,
+                                   const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,8 @@ SIGNATURES = {
     "gdn_gated_delta_kernel": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                       _vp]),
     "gdn_beta_g": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gdn_layer_step_noalloc": (_int, [C.POINTER(GdnConfigC), _i32, _vp, _vp, C.POINTER(GdnLayerWeightsC),
+                                      C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32, _vp]),
 }
 
 

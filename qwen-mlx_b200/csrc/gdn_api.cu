@@ -52,6 +52,11 @@ struct DeviceGuard {
 
 }  // namespace
 
+namespace gdn {
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int record_ok() { return ok(); }
+}  // namespace gdn
+
 struct gdn_pool {
     int device;
     gdn_config cfg;

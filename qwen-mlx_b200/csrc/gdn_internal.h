@@ -72,6 +72,10 @@ struct RecurArgs {
 };
 
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
+
+// Set the calling thread's gdn_last_error() message and return `code` / GDN_OK.
+int record_error(int code, const char* msg);
+int record_ok();
 cudaError_t launch_recurrence(const StepArgs& a, cudaStream_t stream);
 cudaError_t launch_beta_g(const uint16_t* ab, long long ld_ab, int n_tokens, int hv, const float* A_log,
                           const float* dt_bias, uint16_t* beta, float* g, cudaStream_t stream);
