@@ -157,6 +157,40 @@ GDN_API int gdn_layer_step(gdn_pool* pool, int32_t layer, const gdn_layer_weight
                    const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens,
                    void* stream);
 
+/* Parameters of a whole mixer layer (GatedDeltaNet, qwen3_5.rs:466-503) and of its
+ * decoder-layer input norm.  Device pointers.  w_in holds the four input
+ * projections stacked by rows in the reference's merged order (qwen3_5.rs:1038-1047):
+ * in_proj_qkv (D rows) | in_proj_z (Hv*dv) | in_proj_b (Hv) | in_proj_a (Hv). */
+typedef struct gdn_mixer_weights {
+    gdn_layer_weights step;      /* conv_w, A_log, dt_bias, norm_w */
+    const gdn_bf16* w_in;        /* [D + Hv*dv + 2*Hv][hidden] */
+    const gdn_bf16* w_out;       /* [hidden][Hv*dv]  out_proj */
+    const gdn_bf16* pre_norm_w;  /* [hidden] input_layernorm gain (used by gdn_stack_step) */
+} gdn_mixer_weights;
+
+/* One projection (nn::Linear without bias, qwen3_5.rs:572-586, :668):
+ * y[m][n] = bf16(sum_k x[m][k] * w[n][k]) with f32 accumulation, for m < n_tokens,
+ * n < n_out, k < n_in.  x [n_tokens][ld_x], w [n_out][n_in], y [n_tokens][ld_y] bf16.
+ * Runs cuBLASLt (library GEMM) on the pool's handle and stream.  Asynchronous. */
+GDN_API int gdn_linear(gdn_pool* pool, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x,
+                       int64_t ld_x, const gdn_bf16* w, gdn_bf16* y, int64_t ld_y, void* stream);
+
+/* A whole mixer layer (GatedDeltaNet::forward_with_cache, qwen3_5.rs:559-669):
+ * y = out_proj(gdn_layer_step(in_proj(x))) over a packed ragged batch.
+ * x [n_tokens][ld_x], y [n_tokens][ld_y] bf16, hidden columns.  The projections are
+ * bf16 GEMMs with f32 accumulation run by cuBLASLt (library GEMM).  Asynchronous. */
+GDN_API int gdn_mixer_step(gdn_pool* pool, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x,
+                           int64_t ld_x, gdn_bf16* y, int64_t ld_y, const int32_t* slot_ids,
+                           const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens, void* stream);
+
+/* The residual GDN stack: for l = 0 .. n_layers-1,
+ *   h <- h + mixer_l(rms_norm(h, layers[l].pre_norm_w, rms_norm_eps))
+ * (the decoder layer of qwen3_5.rs:729-739 restricted to its mixer), in place on
+ * h [n_tokens][ld_h] bf16.  layers: n_layers entries (host array of device pointers). */
+GDN_API int gdn_stack_step(gdn_pool* pool, const gdn_mixer_weights* layers, gdn_bf16* h, int64_t ld_h,
+                           const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens,
+                           void* stream);
+
 /* The gated delta recurrence alone on pool state (metal_gdn.rs:10-67), packed
  * and ragged: q,k [N][Hk][dk] bf16, v [N][Hv][dv] bf16, g [N][Hv] f32,
  * beta [N][Hv] bf16 -> y [N][Hv][dv] bf16; state of slot_ids[i] updated in place. */

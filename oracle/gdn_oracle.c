@@ -69,6 +69,12 @@ static inline int conv_dim(const orc_cfg* c) { return 2 * c->hk * c->dk + c->hv 
 
 /* ------------------------------------------------------------ building blocks */
 
+static inline float lane_tree_sum_fwd(float* p) {
+    for (int off = 16; off > 0; off >>= 1)
+        for (int l = 0; l < off; ++l) p[l] = p[l] + p[l + off];
+    return p[0];
+}
+
 /* MLX fast::rms_norm over one row of n bf16 values; w == NULL means a constant gain. */
 static void rms_norm_row(const uint16_t* x, const uint16_t* w, uint16_t w_const, int n, float eps,
                          uint16_t* out) {
@@ -90,11 +96,21 @@ void orc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int32_t n,
     for (int64_t r = 0; r < rows; ++r) rms_norm_row(x + r * n, w, 0, n, eps, out + r * n);
 }
 
+/* Accumulation order of the f32 dot products in orc_linear.  The reference's GEMM
+ * (MLX matmul / quantized_matmul, qwen3_5.rs:572-586, :668) accumulates in f32 in an
+ * order the reference does not fix.  0: sequential over k (default).  1: 32
+ * interleaved partial sums (k mod 32) combined by a pairwise tree -- a different,
+ * equally valid order, used by the tests to measure how much the layer's output
+ * depends on the order. */
+static int g_linear_order = 0;
+void orc_set_linear_order(int order) { g_linear_order = order; }
+
 /* Linear without bias (nn::Linear / matmul): out[m][n] = bf16(sum_k x[m][k] w[n][k]) with f32 accumulation. */
 void orc_linear(const uint16_t* x, const uint16_t* w, int64_t M, int32_t N, int32_t K, uint16_t* out) {
     float* wf = (float*)malloc(sizeof(float) * (size_t)N * K);
     float* xf = (float*)malloc(sizeof(float) * (size_t)M * K);
     if (!wf || !xf) { free(wf); free(xf); return; }
+    const int order = g_linear_order;
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)N * K; ++i) wf[i] = bf(w[i]);
 #pragma omp parallel for schedule(static)
@@ -105,7 +121,22 @@ void orc_linear(const uint16_t* x, const uint16_t* w, int64_t M, int32_t N, int3
             const float* xr = xf + m * K;
             const float* wr = wf + (int64_t)n * K;
             float acc = 0.0f;
-            for (int32_t k = 0; k < K; ++k) acc += xr[k] * wr[k];
+            if (order == 1) {
+                float part[32];
+                for (int l = 0; l < 32; ++l) part[l] = 0.0f;
+                for (int32_t k = 0; k < K; ++k) part[k & 31] += xr[k] * wr[k];
+                acc = lane_tree_sum_fwd(part);
+            } else if (order == 2) {
+                for (int32_t k0 = 0; k0 < K; k0 += 16) {
+                    float blk = 0.0f;
+                    for (int32_t k = k0; k < k0 + 16 && k < K; ++k) blk += xr[k] * wr[k];
+                    acc += blk;
+                }
+            } else if (order == 3) {
+                for (int32_t k = K - 1; k >= 0; --k) acc += xr[k] * wr[k];
+            } else {
+                for (int32_t k = 0; k < K; ++k) acc += xr[k] * wr[k];
+            }
             out[m * N + n] = tobf(acc);
         }
     free(wf);

@@ -78,6 +78,8 @@ def lib():
         L.orc_stack_step.restype = C.c_int
         L.orc_conv.argtypes = [C.POINTER(OrcCfg), _u16p, C.c_int64, C.c_int32, _u16p, _u16p, _u16p]
         L.orc_conv.restype = C.c_int
+        L.orc_set_linear_order.argtypes = [C.c_int]
+        L.orc_set_linear_order.restype = None
         L.orc_num_threads.restype = C.c_int
         L.orc_set_num_threads.argtypes = [C.c_int]
         _lib = L
@@ -102,6 +104,12 @@ def _c(a, dt):
 
 def cfg_struct(cfg) -> OrcCfg:
     return OrcCfg(cfg.hidden, cfg.hk, cfg.hv, cfg.dk, cfg.dv, cfg.conv_k, cfg.eps)
+
+
+def set_linear_order(order: int):
+    """Accumulation order of orc_linear: 0 sequential (default); 1 32 interleaved partial sums + tree;
+    2 blocks of 16 accumulated in order; 3 reverse sequential."""
+    lib().orc_set_linear_order(int(order))
 
 
 def set_threads(n: int):

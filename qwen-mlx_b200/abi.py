@@ -41,6 +41,10 @@ class GdnStepIOC(C.Structure):
                 ("out", _vp), ("ld_out", _i64)]
 
 
+class GdnMixerWeightsC(C.Structure):
+    _fields_ = [("step", GdnLayerWeightsC), ("w_in", _vp), ("w_out", _vp), ("pre_norm_w", _vp)]
+
+
 SIGNATURES = {
     "gdn_last_error": (C.c_char_p, []),
     "gdn_version": (C.c_char_p, []),
@@ -57,6 +61,10 @@ SIGNATURES = {
     "gdn_pool_check": (_int, [_vp, C.POINTER(_i32), _int]),
     "gdn_layer_step": (_int, [_vp, _i32, C.POINTER(GdnLayerWeightsC), C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32,
                               _vp]),
+    "gdn_linear": (_int, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp]),
+    "gdn_mixer_step": (_int, [_vp, _i32, C.POINTER(GdnMixerWeightsC), _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32,
+                              _vp]),
+    "gdn_stack_step": (_int, [_vp, C.POINTER(GdnMixerWeightsC), _vp, _i64, _vp, _vp, _i32, _i32, _vp]),
     "gdn_recurrence": (_int, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp]),
     "gdn_gated_delta_kernel": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                       _vp]),

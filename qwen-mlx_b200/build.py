@@ -5,7 +5,8 @@
 Compiles every CUDA source under csrc/ with nvcc for sm_100a
 (-gencode arch=compute_100a,code=sm_100a) into qwen-mlx_b200/libgdn_b200.so,
 which exports the C ABI declared in include/gdn.h.  The CUDA runtime is linked
-statically, so the library loads on any box with the driver.
+statically; cuBLASLt (the projection GEMMs) dynamically, with an rpath to the
+toolkit.
 """
 from __future__ import annotations
 
@@ -45,6 +46,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if verbose:
         cmd += ["-Xptxas", "-v"]
     cmd += [str(s) for s in sources()] + ["-o", str(LIB)]
+    # cuBLASLt (projection GEMMs); rpath so the library loads without LD_LIBRARY_PATH
+    cmd += ["-L/usr/local/cuda/lib64", "-lcublasLt", "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
     subprocess.run(cmd, check=True)
     return LIB
 

@@ -67,22 +67,41 @@ struct gdn_pool {
     float* rec;              // [n_layers][n_slots][Hv][dv][dk]
     uint16_t* conv;          // [n_layers][n_slots][K-1][D]
     int32_t* err;            // device error word
+    gdn::GemmCtx* gemm;      // cuBLASLt handle for the projections
+    void* gemm_ws;           // its workspace
+    uint16_t* proj;          // scratch [rec_cap][D + Hv*dv + 2*Hv]: projection outputs
+    uint16_t* gated;         // scratch [rec_cap][Hv*dv]: layer-step output (out_proj input)
+    uint16_t* hn;            // scratch [rec_cap][hidden]: normed stack input
+    uint16_t* mix;           // scratch [rec_cap][hidden]: mixer output
     uint8_t* recs;           // scratch: per-(v-head, token) records of the layer step [Hv][rec_cap][REC_BYTES]
     long long rec_cap;       // tokens per call the scratch holds
 };
 
+static long long proj_ld(const gdn_pool* p) { return (long long)p->D + p->cfg.n_v_heads * 128 + 2 * p->cfg.n_v_heads; }
+
 static int reserve_records(gdn_pool* p, long long tokens) {
     if (tokens <= p->rec_cap) return GDN_OK;
-    const size_t bytes = (size_t)tokens * p->cfg.n_v_heads * gdn::REC_BYTES;
+    const size_t rec_bytes = (size_t)tokens * p->cfg.n_v_heads * gdn::REC_BYTES;
+    const size_t proj_bytes = (size_t)tokens * proj_ld(p) * 2;
+    const size_t gated_bytes = (size_t)tokens * p->cfg.n_v_heads * 128 * 2;
+    const size_t hid_bytes = (size_t)tokens * p->cfg.hidden * 2;
     uint8_t* buf = nullptr;
-    cudaError_t e = cudaMalloc(&buf, bytes);
-    if (e != cudaSuccess)
-        return fail(GDN_E_NOMEM, "cudaMalloc of %zu B of step scratch failed: %s", bytes, cudaGetErrorString(e));
+    uint16_t *proj = nullptr, *gated = nullptr, *hn = nullptr, *mix = nullptr;
+    cudaError_t e = cudaMalloc(&buf, rec_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&proj, proj_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&gated, gated_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&hn, hid_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&mix, hid_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(buf); cudaFree(proj); cudaFree(gated); cudaFree(hn); cudaFree(mix);
+        return fail(GDN_E_NOMEM, "cudaMalloc of step scratch for %lld tokens failed: %s", tokens, cudaGetErrorString(e));
+    }
     if (p->recs) {
         cudaDeviceSynchronize();
-        cudaFree(p->recs);
+        cudaFree(p->recs); cudaFree(p->proj); cudaFree(p->gated); cudaFree(p->hn); cudaFree(p->mix);
     }
     p->recs = buf;
+    p->proj = proj; p->gated = gated; p->hn = hn; p->mix = mix;
     p->rec_cap = tokens;
     return GDN_OK;
 }
@@ -164,12 +183,23 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         return cuda_fail(e, "zeroing the pool");
     }
     p->recs = nullptr;
+    p->proj = p->gated = p->hn = p->mix = nullptr;
     p->rec_cap = 0;
+    p->gemm = nullptr;
+    p->gemm_ws = nullptr;
     rc = reserve_records(p, n_slots > 1024 ? n_slots : 1024);
+    if (rc == GDN_OK) {
+        const size_t ws = 32u << 20;
+        e = cudaMalloc(&p->gemm_ws, ws);
+        if (e == cudaSuccess) p->gemm = gdn::gemm_create(p->gemm_ws, ws);
+        if (e != cudaSuccess || !p->gemm) rc = fail(GDN_E_NOMEM, "cuBLASLt handle / workspace creation failed");
+    }
     if (rc) {
         cudaFree(p->rec);
         cudaFree(p->conv);
         cudaFree(p->err);
+        cudaFree(p->recs); cudaFree(p->proj); cudaFree(p->gated); cudaFree(p->hn); cudaFree(p->mix);
+        cudaFree(p->gemm_ws);
         delete p;
         return rc;
     }
@@ -193,6 +223,12 @@ int gdn_pool_destroy(gdn_pool* p) {
     cudaFree(p->conv);
     cudaFree(p->err);
     cudaFree(p->recs);
+    cudaFree(p->proj);
+    cudaFree(p->gated);
+    cudaFree(p->hn);
+    cudaFree(p->mix);
+    gdn::gemm_destroy(p->gemm);
+    cudaFree(p->gemm_ws);
     delete p;
     return ok();
 }
@@ -210,7 +246,8 @@ int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
     if (!p || !bytes) return fail(GDN_E_INVALID, "NULL argument");
     *bytes = (sizeof(float) * p->rec_slot_elems + sizeof(uint16_t) * p->conv_slot_elems) * (size_t)p->n_slots *
                  p->cfg.n_layers +
-             sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES;
+             sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES +
+             (size_t)p->rec_cap * 2 * (proj_ld(p) + p->cfg.n_v_heads * 128 + 2 * p->cfg.hidden) + (32u << 20);
     return ok();
 }
 
@@ -382,6 +419,93 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     ra.err = p->err;
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");
+    return ok();
+}
+
+static bool mixer_weights_ok(const gdn_mixer_weights* w) {
+    return w && w->w_in && w->w_out && w->step.conv_w && w->step.A_log && w->step.dt_bias && w->step.norm_w;
+}
+
+// One mixer layer on the pool's scratch: x -> proj -> fused step -> gated -> y.
+static int mixer_layer(gdn_pool* p, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x, int64_t ld_x,
+                       gdn_bf16* y, int64_t ld_y, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                       int32_t n_tokens, void* stream) {
+    const int H = p->cfg.hidden;
+    const int zd = p->cfg.n_v_heads * 128;
+    const long long ldp = proj_ld(p);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (gdn::gemm_bf16_nt(p->gemm, n_tokens, (int)ldp, H, x, ld_x, w->w_in, p->proj, ldp, s))
+        return fail(GDN_E_CUDA, "cuBLASLt in-projection GEMM failed (M=%d N=%lld K=%d)", n_tokens, ldp, H);
+    gdn_step_io io;
+    io.qkv = p->proj; io.ld_qkv = ldp;
+    io.z = p->proj + p->D; io.ld_z = ldp;
+    io.ab = p->proj + p->D + zd; io.ld_ab = ldp;
+    io.out = p->gated; io.ld_out = zd;
+    int rc = gdn_layer_step(p, layer, &w->step, &io, slot_ids, cu, n_seq, n_tokens, stream);
+    if (rc) return rc;
+    if (gdn::gemm_bf16_nt(p->gemm, n_tokens, H, zd, p->gated, zd, w->w_out, y, ld_y, s))
+        return fail(GDN_E_CUDA, "cuBLASLt out-projection GEMM failed (M=%d N=%d K=%d)", n_tokens, H, zd);
+    return GDN_OK;
+}
+
+int gdn_linear(gdn_pool* p, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x, int64_t ld_x,
+               const gdn_bf16* w, gdn_bf16* y, int64_t ld_y, void* stream) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (n_tokens < 0 || n_out <= 0 || n_in <= 0 || ld_x < n_in || ld_y < n_out)
+        return fail(GDN_E_INVALID, "bad GEMM shape (M=%d N=%d K=%d ld_x=%lld ld_y=%lld)", n_tokens, n_out, n_in,
+                    (long long)ld_x, (long long)ld_y);
+    if (n_tokens == 0) return ok();
+    if (!x || !w || !y) return fail(GDN_E_INVALID, "NULL tensor");
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    if (gdn::gemm_bf16_nt(p->gemm, n_tokens, n_out, n_in, x, ld_x, w, y, ld_y, (cudaStream_t)stream))
+        return fail(GDN_E_CUDA, "cuBLASLt GEMM failed (M=%d N=%d K=%d)", n_tokens, n_out, n_in);
+    return ok();
+}
+
+int gdn_mixer_step(gdn_pool* p, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x, int64_t ld_x,
+                   gdn_bf16* y, int64_t ld_y, const int32_t* slot_ids, const int32_t* cu, int32_t n_seq,
+                   int32_t n_tokens, void* stream) {
+    int rc = check_common(p, layer, slot_ids, cu, n_seq, n_tokens);
+    if (rc) return rc;
+    if (!mixer_weights_ok(w)) return fail(GDN_E_INVALID, "NULL mixer weight");
+    if (!x || !y || ld_x < p->cfg.hidden || ld_y < p->cfg.hidden) return fail(GDN_E_INVALID, "bad x / y buffer");
+    if (n_tokens > p->rec_cap)
+        return fail(GDN_E_INVALID, "n_tokens %d exceeds the pool's reserved %lld tokens per call", n_tokens, p->rec_cap);
+    if (n_seq == 0 || n_tokens == 0) return ok();
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    rc = mixer_layer(p, layer, w, x, ld_x, y, ld_y, slot_ids, cu, n_seq, n_tokens, stream);
+    return rc ? rc : ok();
+}
+
+int gdn_stack_step(gdn_pool* p, const gdn_mixer_weights* layers, gdn_bf16* h, int64_t ld_h,
+                   const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, void* stream) {
+    int rc = check_common(p, 0, slot_ids, cu, n_seq, n_tokens);
+    if (rc) return rc;
+    if (!layers || !h || ld_h < p->cfg.hidden) return fail(GDN_E_INVALID, "bad layers / h");
+    for (int l = 0; l < p->cfg.n_layers; ++l)
+        if (!mixer_weights_ok(&layers[l]) || !layers[l].pre_norm_w)
+            return fail(GDN_E_INVALID, "NULL weight in layer %d", l);
+    if (n_tokens > p->rec_cap)
+        return fail(GDN_E_INVALID, "n_tokens %d exceeds the pool's reserved %lld tokens per call", n_tokens, p->rec_cap);
+    if (n_seq == 0 || n_tokens == 0) return ok();
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int H = p->cfg.hidden;
+    const float eps = p->cfg.rms_norm_eps;
+    for (int l = 0; l < p->cfg.n_layers; ++l) {
+        // h <- h + mix_{l-1} (from layer 1 on), hn <- rms_norm(h, pre_norm_w[l])
+        cudaError_t e = gdn::launch_add_rmsnorm(h, ld_h, l ? p->mix : nullptr, H, h, layers[l].pre_norm_w, p->hn, H,
+                                                n_tokens, H, eps, s);
+        if (e != cudaSuccess) return cuda_fail(e, "pre-norm launch");
+        rc = mixer_layer(p, l, &layers[l], p->hn, H, p->mix, H, slot_ids, cu, n_seq, n_tokens, stream);
+        if (rc) return rc;
+    }
+    cudaError_t e = gdn::launch_add_rmsnorm(h, ld_h, p->mix, H, h, layers[0].pre_norm_w, nullptr, H, n_tokens, H,
+                                            eps, s);
+    if (e != cudaSuccess) return cuda_fail(e, "residual launch");
     return ok();
 }
 

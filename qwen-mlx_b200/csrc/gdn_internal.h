@@ -73,6 +73,16 @@ struct RecurArgs {
 
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
 
+// Projections and the decoder pre-norm / residual (gdn_proj.cu).
+struct GemmCtx;
+GemmCtx* gemm_create(void* workspace, size_t ws_bytes);
+void gemm_destroy(GemmCtx* g);
+int gemm_bf16_nt(GemmCtx* g, int M, int N, int K, const uint16_t* x, long long ldx, const uint16_t* w,
+                 uint16_t* out, long long ldo, cudaStream_t stream);
+cudaError_t launch_add_rmsnorm(const uint16_t* h_in, long long ld_h, const uint16_t* o, long long ld_o,
+                               uint16_t* h_out, const uint16_t* w, uint16_t* hn, long long ld_hn, int rows, int H,
+                               float eps, cudaStream_t stream);
+
 // Set the calling thread's gdn_last_error() message and return `code` / GDN_OK.
 int record_error(int code, const char* msg);
 int record_ok();

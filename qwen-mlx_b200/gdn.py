@@ -92,6 +92,20 @@ class LayerWeights:
                                       self.norm_w.data_ptr())
 
 
+class MixerWeights:
+    """Device copies of one whole mixer layer: step parameters, merged in-projection
+    [qkv | z | b | a] rows (the reference's merged order), out-projection and the
+    decoder input-norm gain."""
+
+    def __init__(self, w: dict, device):
+        self.step = LayerWeights(w, device)
+        w_in = np.concatenate([w["w_qkv"], w["w_z"], w["w_b"], w["w_a"]], axis=0)
+        self.w_in = bf16_to_device(w_in, device)
+        self.w_out = bf16_to_device(w["w_out"], device)
+        self.pre_w = bf16_to_device(w["pre_w"], device)
+        self.c = abi.GdnMixerWeightsC(self.step.c, self.w_in.data_ptr(), self.w_out.data_ptr(), self.pre_w.data_ptr())
+
+
 class StatePool:
     """Slot-indexed device pool of GDN states for `cfg.n_layers` layers."""
 
@@ -181,6 +195,22 @@ class StatePool:
         rc = abi.lib().gdn_layer_step(self.h, layer, w_c, io_c, slot_ptr, cu_ptr, n_seq, n_tokens, stream_ptr)
         if rc:
             abi.check(rc, "gdn_layer_step")
+
+    def linear(self, x, w, y, stream=None):
+        """y = x @ w.T (bf16, f32 accumulation): x [M, K], w [N, K], y [M, N] device tensors."""
+        abi.call("gdn_linear", self.h, x.shape[0], w.shape[0], w.shape[1], _ptr(x), x.stride(0), _ptr(w), _ptr(y),
+                 y.stride(0), _stream(stream))
+
+    def mixer_step(self, layer: int, w: MixerWeights, x, y, slot_ids, cu_seqlens, n_tokens: int, stream=None):
+        """Whole mixer layer: y = out_proj(step(in_proj(x))); x, y [N, hidden] device bf16."""
+        abi.call("gdn_mixer_step", self.h, layer, C.byref(w.c), _ptr(x), x.stride(0), _ptr(y), y.stride(0),
+                 _ptr(slot_ids), _ptr(cu_seqlens), slot_ids.numel(), n_tokens, _stream(stream))
+
+    def stack_step(self, ws, h, slot_ids, cu_seqlens, n_tokens: int, stream=None):
+        """Residual GDN stack over all pool layers, in place on h [N, hidden] device bf16."""
+        arr = (abi.GdnMixerWeightsC * len(ws))(*[w.c for w in ws])
+        abi.call("gdn_stack_step", self.h, arr, _ptr(h), h.stride(0), _ptr(slot_ids), _ptr(cu_seqlens),
+                 slot_ids.numel(), n_tokens, _stream(stream))
 
     def recurrence(self, layer: int, q, k, v, g, beta, y, slot_ids, cu_seqlens, n_tokens: int, stream=None):
         abi.call("gdn_recurrence", self.h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(slot_ids),
