@@ -59,6 +59,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-mixer", action="store_true")
     return p.parse_args()
 
 
@@ -239,6 +240,94 @@ def _gpu_uuid(torch, dev):
         return str(dev.index)
 
 
+# Bytes of one mixer layer's projection weights: in_proj (8192 + 4096 + 64 rows) and out_proj, bf16.
+MIXER_WEIGHT_BYTES = ((8192 + 4096 + 64) * 2048 + 2048 * 4096) * 2
+assert MIXER_WEIGHT_BYTES == 67_371_008
+
+
+def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrier, dist, world, args, hbm_peak):
+    """Config 2 through gdn_stack_step: h <- h + mixer_l(rms_norm(h)) over 30 layers (projections by
+    cuBLASLt).  Device tok/s, and e2e with the step's x copied in and h copied out."""
+    import importlib
+    synth = importlib.import_module("qwen_mlx_b200.synth")
+    mws = []
+    keep = []
+    for l in range(N_LAYERS):
+        w = synth.layer_weights(cfg, l, with_proj=False)
+        step = gdn.LayerWeights(w, dev)
+        w_in = (torch.randn((8192 + 4096 + 64, cfg.hidden), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w_out = (torch.randn((cfg.hidden, cfg.z_dim), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        pre = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
+        keep.append((step, w_in, w_out, pre))
+        mws.append(abi.GdnMixerWeightsC(step.c, w_in.data_ptr(), w_out.data_ptr(), pre.data_ptr()))
+    arr = (abi.GdnMixerWeightsC * N_LAYERS)(*mws)
+    h = torch.randn((B, cfg.hidden), device=dev, generator=gen).to(torch.bfloat16)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def step():
+        rc = lib.gdn_stack_step(pool.h, arr, C.c_void_p(h.data_ptr()), cfg.hidden, C.c_void_p(slots.data_ptr()),
+                                C.c_void_p(cu.data_ptr()), B, B, sp)
+        if rc:
+            abi.check(rc, "gdn_stack_step")
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+    stream.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    # e2e: this step's hidden states in (pinned host -> device), the updated hidden states out
+    x_host = torch.empty((B, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(h.cpu())
+    y_host = torch.empty_like(x_host).pin_memory()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            h.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(h, non_blocking=True)
+    stream.synchronize()
+    barrier()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            h.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(h, non_blocking=True)
+        e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0].item()), float(t[1].item())
+    step_bytes = N_LAYERS * (MIXER_WEIGHT_BYTES + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
+    del g
+    return {"tok_s": world * B * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps,
+            "hbm_frac_of_measured": step_bytes / (ms / args.steps / 1e3) / 1e9 / hbm_peak,
+            "bytes_per_step": step_bytes,
+            "e2e_tok_s": world * B * args.steps / (e2e_ms / 1e3), "h2d_bytes_per_step": x_host.numel() * 2,
+            "d2h_bytes_per_step": y_host.numel() * 2,
+            "note": "30 x (pre-norm + in_proj GEMM + gdn_layer_step + out_proj GEMM + residual); GEMMs are cuBLASLt"}
+
+
 def run_ours(args):
     import torch
     world, rank, local, dist, timedelta = dist_setup(args.gpus)
@@ -364,7 +453,7 @@ def run_ours(args):
         ms = float(t.item())
     ms_per_step = ms / args.steps
     value = world * B * args.steps / (ms / 1e3)
-    gpu_launches = args.steps * N_LAYERS
+    gpu_launches = args.steps * N_LAYERS * 2     # gdn_prep_kernel + gdn_recur_kernel per layer
 
     # ---- roofline of the dominant kernel (the fused layer step), per launch
     launch_ms = ms_per_step / N_LAYERS     # average launch duration inside the timed graph (gaps included)
@@ -373,7 +462,8 @@ def run_ours(args):
     tr_per_seq, _ = profiled_traffic()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                 "traffic": (tr_per_seq * B if tr_per_seq else None), "peak_kind": peak_kind,
-                "kernel": "gdn_step_kernel<fused>", "launch_us": launch_ms * 1e3,
+                "kernel": "gdn_layer_step = gdn_prep_kernel + gdn_recur_kernel (PDL-chained)",
+                "launch_us": launch_ms * 1e3,
                 "alg_bytes_per_launch": alg_bytes,
                 "step_frac": (B * N_LAYERS * BYTES_PER_SEQ_LAYER + N_LAYERS * BYTES_PER_LAUNCH_CONST)
                 / (ms_per_step / 1e3) / 1e9 / hbm_peak}
@@ -411,6 +501,12 @@ def run_ours(args):
     e2e = {"value": world * B * args.steps / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": in_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2}
 
+    # ---- the whole mixer stack (projections + pre-norm + residual) at the same B
+    mixer = None
+    if not args.no_mixer:
+        mixer = run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrier, dist, world, args,
+                                hbm_peak)
+
     # ---- B sweep (1 GPU only): device tok/s and step-level HBM fraction
     sweep = {}
     for b in sweep_bs:
@@ -439,7 +535,7 @@ def run_ours(args):
                            "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
                                N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
-                "clocks": clk, "sweep": sweep or None}
+                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer}
     if dist is not None:
         dist.barrier()
         del g
