@@ -417,7 +417,12 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     ra.n_seq = n_seq; ra.n_slots = p->n_slots; ra.n_tokens = n_tokens;
     ra.hk = p->cfg.n_k_heads; ra.hv = p->cfg.n_v_heads; ra.D = p->D;
     ra.err = p->err;
+    // A call with more tokens than sequences has multi-token segments: the long ones run the
+    // chunked tensor-core kernel after the streaming kernel has done the rest.
+    const bool has_long = n_tokens > n_seq;
+    ra.wy_min_t = has_long ? gdn::WY_MIN_T : 0;
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
+    if (e == cudaSuccess && has_long) e = gdn::launch_wy(ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");
     return ok();
 }

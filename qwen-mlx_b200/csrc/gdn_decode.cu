@@ -8,8 +8,8 @@
 //    bf16(dk^-1/2) (qwen3_5.rs:636-639), beta and g (compiled_ops.rs:30-43) and
 //    silu(z) (qwen3_5.rs:664).  It writes one 1040-byte record per (v-head,
 //    token) into the pool's scratch: q | k | v | silu(z) (bf16 x 128 each) |
-//    g (f32) | beta (f32 holding the bf16 value) | pad.  K1 only reads the conv
-//    state.
+//    g (f32) | beta (f32 holding the bf16 value) | log g (f32) | pad.  K1 reads
+//    the conv state, and shifts the windows of one-token sequences in place.
 // K2 gdn_recur_kernel (persistent, one CTA per SM): work item = (sequence,
 //    v-head).  A producer warp streams each item's 64 KiB f32 state tile
 //    ([dv][dk], metal_gdn.rs:25-26) and its token records into a 3-stage
@@ -218,8 +218,10 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
         const int hv = hk * ratio + tid;
         const float sp = logf(expf(gb_a + gb_dt) + 1.0f);
         float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
-        gb[0] = expf(-(expf(gb_alog) * sp));
+        const float logdecay = -(expf(gb_alog) * sp);
+        gb[0] = expf(logdecay);
         gb[1] = rbf(sigmoid_f32(gb_b));
+        gb[2] = logdecay;  // log g, for the chunked prefill kernel
     }
 }
 
@@ -308,6 +310,7 @@ __global__ void __launch_bounds__(K2_THREADS, 1) gdn_recur_kernel(const RecurArg
                     continue;
                 }
                 if (T == 0) continue;
+                if (a.wy_min_t > 0 && T >= a.wy_min_t) continue;  // handled by the chunked prefill kernel
                 const int s = k % NSTAGE;
                 const uint32_t ph = (uint32_t)(k / NSTAGE) & 1u;
                 if (k >= NSTAGE && !mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_LIMIT_NS)) {

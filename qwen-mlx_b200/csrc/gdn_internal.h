@@ -33,7 +33,7 @@ struct StepArgs {
 };
 
 // Per-(v-head, token) record written by the prep kernel and streamed by the
-// recurrence kernel: q | k | v | silu(z) (bf16 x 128 each) | g f32 | beta f32 | pad.
+// recurrence kernels: q | k | v | silu(z) (bf16 x 128 each) | g f32 | beta f32 | log g f32 | pad.
 constexpr int REC_BYTES = 1040;
 constexpr int REC_PER_STAGE = 4;   // token records staged with each state tile
 
@@ -69,8 +69,13 @@ struct RecurArgs {
     int32_t n_seq, n_slots, n_tokens;
     int32_t hk, hv, D;
     int32_t* err;
+    int32_t wy_min_t;            // > 0: segments of at least this many tokens go to the chunked kernel
 };
 
+// Sequences of at least this many tokens in one call run the chunked (WY) tensor-core kernel.
+constexpr int WY_MIN_T = 32;
+
+cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream);
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
 
 // Projections and the decoder pre-norm / residual (gdn_proj.cu).

@@ -1,0 +1,108 @@
+// gdn_umma.cuh -- tcgen05 (5th-generation tensor core) helpers for sm_100a:
+// shared-memory matrix descriptors for K-major bf16 tiles, the instruction
+// descriptor of kind::f16 (bf16 x bf16 -> f32), TMEM allocation, MMA issue,
+// commit to an mbarrier, and TMEM <-> register moves.
+//
+// Tile layout used by every operand (no swizzle, "interleaved" core matrices):
+// an R x KT bf16 tile, K-major, is stored as core matrices of 8 rows x 8 elements
+// (8 x 16 B, rows contiguous), ordered [row/8][k/8]:
+//     byte offset(r, k) = (r/8)*(KT/8)*128 + (k/8)*128 + (r%8)*16 + (k%8)*2
+// so the leading-dimension byte offset (between the two 16-byte K chunks of one
+// MMA k-step) is 128 and the stride byte offset (between 8-row groups) is KT*16.
+// One MMA consumes K = 16 elements; the next k-step starts 256 bytes further.
+//
+// Accumulator layout in TMEM (cta_group::1): for M = 128, row m is TMEM lane m;
+// for M = 64, row m is lane 32*(m/16) + m%16 (the first 16 lanes of each warp's
+// quarter).  Column n of the result is TMEM column base + n (32-bit).
+#pragma once
+
+#include <stdint.h>
+
+#include "gdn_ptx.cuh"
+
+namespace gdn {
+
+__device__ __forceinline__ uint32_t umma_tile_off(int r, int k, int KT) {
+    return (uint32_t)((r >> 3) * (KT >> 3) * 128 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+}
+
+// Shared-memory matrix descriptor (K-major, no swizzle) of a tile starting at `saddr`
+// (shared-space byte address), advanced by `kstep` MMA k-steps of 16 elements.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, int KT, int kstep) {
+    const uint32_t start = saddr + (uint32_t)kstep * 256u;
+    const uint32_t lbo = 128u, sbo = (uint32_t)KT * 16u;
+    uint64_t d = (uint64_t)((start >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version of sm_100; base offset 0, layout SWIZZLE_NONE
+    return d;
+}
+
+// kind::f16 instruction descriptor: A = B = bf16, D = f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (TMEM) (+)= A (smem) * B (smem)^T for one k-step; issued by a single thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// All MMAs issued so far by this thread arrive on `bar` when complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+}  // namespace gdn
