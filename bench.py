@@ -60,6 +60,7 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-mixer", action="store_true")
+    p.add_argument("--no-prefill", action="store_true")
     return p.parse_args()
 
 
@@ -328,6 +329,72 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
             "note": "30 x (pre-norm + in_proj GEMM + gdn_layer_step + out_proj GEMM + residual); GEMMs are cuBLASLt"}
 
 
+# Prefill (chunked WY) algorithmic flops per token per layer, chunk 64: 6*dk*dv + 2*C*(3*dk + 2*dv) per
+# v-head (state readout, state update, W S0^T, and the intra-chunk K K^T, Q K^T, T V, T K, P D), x 32 heads.
+WY_FLOPS_PER_TOKEN_LAYER = 32 * (6 * 128 * 128 + 2 * 64 * (3 * 128 + 2 * 128))
+assert WY_FLOPS_PER_TOKEN_LAYER == 5_767_168
+CONFIG4_LENS = [512, 1024, 2048, 3000, 4096, 5000, 6144, 8192]
+
+
+def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args, tc_peak):
+    """Config 4: 8 prompts packed in one call per layer, zero initial state, 30 layers (fused steps).
+    Segments of >= 32 tokens run the tcgen05 chunked kernel."""
+    lens = CONFIG4_LENS
+    cu_h = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    N = int(cu_h[-1])
+    pool.reserve_tokens(N)
+    proj = torch.randn((N, PROJ_LD), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty((N, cfg.z_dim), dtype=torch.bfloat16, device=dev)
+    slots = torch.arange(len(lens), dtype=torch.int32, device=dev)
+    cu = torch.from_numpy(cu_h).to(dev)
+    io = abi.GdnStepIOC(proj.data_ptr(), PROJ_LD, proj.data_ptr() + 8192 * 2, PROJ_LD,
+                        proj.data_ptr() + (8192 + 4096) * 2, PROJ_LD, out.data_ptr(), cfg.z_dim)
+    slots_h = np.arange(len(lens), dtype=np.int32)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def step():
+        pool.reset(slots_h, stream)                     # prompts start from a zero state
+        for l in range(N_LAYERS):
+            rc = lib.gdn_layer_step(pool.h, l, C.byref(lws[l].c), C.byref(io), C.c_void_p(slots.data_ptr()),
+                                    C.c_void_p(cu.data_ptr()), len(lens), N, sp)
+            if rc:
+                abi.check(rc, "gdn_layer_step")
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    steps = max(2, min(args.steps, 5))
+    with torch.cuda.stream(stream):
+        g.replay()
+    stream.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    ms_step = ms / steps
+    flops = N * N_LAYERS * WY_FLOPS_PER_TOKEN_LAYER
+    return {"workload": "config4: prompts %s packed in one call, zero state, 30 fused layer steps" % lens,
+            "tokens": N, "tok_s": world * N / (ms_step / 1e3), "ms_per_step": ms_step,
+            "algorithmic_tflops": flops / (ms_step / 1e3) / 1e12, "tensor_peak_tflops": tc_peak,
+            "tensor_frac_of_measured": flops / (ms_step / 1e3) / 1e12 / tc_peak,
+            "flops_per_token_layer": WY_FLOPS_PER_TOKEN_LAYER}
+
+
 def run_ours(args):
     import torch
     world, rank, local, dist, timedelta = dist_setup(args.gpus)
@@ -501,6 +568,14 @@ def run_ours(args):
     e2e = {"value": world * B * args.steps / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": in_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2}
 
+    # ---- config-4 prefill on the chunked tensor-core path
+    prefill = None
+    if not args.no_prefill:
+        tc_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+        prefill = run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args,
+                              tc_peak)
+
     # ---- the whole mixer stack (projections + pre-norm + residual) at the same B
     mixer = None
     if not args.no_mixer:
@@ -535,7 +610,7 @@ def run_ours(args):
                            "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
                                N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
-                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer}
+                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer, "prefill": prefill}
     if dist is not None:
         dist.barrier()
         del g

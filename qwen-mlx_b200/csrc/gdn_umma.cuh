@@ -4,12 +4,13 @@
 // commit to an mbarrier, and TMEM <-> register moves.
 //
 // Tile layout used by every operand (no swizzle, "interleaved" core matrices):
-// an R x KT bf16 tile, K-major, is stored as core matrices of 8 rows x 8 elements
-// (8 x 16 B, rows contiguous), ordered [row/8][k/8]:
-//     byte offset(r, k) = (r/8)*(KT/8)*128 + (k/8)*128 + (r%8)*16 + (k%8)*2
-// so the leading-dimension byte offset (between the two 16-byte K chunks of one
-// MMA k-step) is 128 and the stride byte offset (between 8-row groups) is KT*16.
-// One MMA consumes K = 16 elements; the next k-step starts 256 bytes further.
+// an R x COLS bf16 tile is stored as core matrices of 8 rows x 8 elements
+// (8 x 16 B, rows contiguous), ordered [row/8][col/8]:
+//     byte offset(r, c) = (r/8)*(COLS/8)*128 + (c/8)*128 + (r%8)*16 + (c%8)*2
+// The same tile serves an MMA either K-major (K along the columns: LBO 128 B
+// between the two 16-byte K chunks of a k-step, SBO COLS*16 B between 8-row
+// groups, next k-step +256 B) or MN-major (K along the rows: SBO 128 B between
+// 8-column groups, LBO COLS*16 B between 8-row groups, next k-step +2*LBO).
 //
 // Accumulator layout in TMEM (cta_group::1): for M = 128, row m is TMEM lane m;
 // for M = 64, row m is lane 32*(m/16) + m%16 (the first 16 lanes of each warp's
@@ -26,11 +27,7 @@ __device__ __forceinline__ uint32_t umma_tile_off(int r, int k, int KT) {
     return (uint32_t)((r >> 3) * (KT >> 3) * 128 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
 }
 
-// Shared-memory matrix descriptor (K-major, no swizzle) of a tile starting at `saddr`
-// (shared-space byte address), advanced by `kstep` MMA k-steps of 16 elements.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, int KT, int kstep) {
-    const uint32_t start = saddr + (uint32_t)kstep * 256u;
-    const uint32_t lbo = 128u, sbo = (uint32_t)KT * 16u;
+__device__ __forceinline__ uint64_t umma_desc_raw(uint32_t start, uint32_t lbo, uint32_t sbo) {
     uint64_t d = (uint64_t)((start >> 4) & 0x3FFFu);
     d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
@@ -38,9 +35,25 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, int KT, int kstep)
     return d;
 }
 
-// kind::f16 instruction descriptor: A = B = bf16, D = f32, both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Descriptor of a tile [R][KT] read K-major (the MMA's K runs along the tile's columns),
+// advanced by `kstep` k-steps of 16 elements: LBO 128 B, SBO KT*16 B, step 256 B.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, int KT, int kstep) {
+    return umma_desc_raw(saddr + (uint32_t)kstep * 256u, 128u, (uint32_t)KT * 16u);
+}
+
+// Descriptor of a tile [K rows][COLS] read MN-major (the MMA's K runs along the tile's rows,
+// M or N along its columns): SBO 128 B between 8-element column groups, LBO COLS*16 B between
+// 8-row groups, so one k-step of 16 rows advances 2 * LBO.
+__device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, int COLS, int kstep) {
+    const uint32_t lbo = (uint32_t)COLS * 16u;
+    return umma_desc_raw(saddr + (uint32_t)kstep * 2u * lbo, lbo, 128u);
+}
+
+// kind::f16 instruction descriptor: A = B = bf16, D = f32, M x N; a_mn / b_mn select an
+// MN-major operand (bits 15 / 16), K-major otherwise.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn = false, bool b_mn = false) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // D (TMEM) (+)= A (smem) * B (smem)^T for one k-step; issued by a single thread.
