@@ -66,7 +66,7 @@ struct gdn_pool {
     size_t conv_slot_elems;  // (K-1)*D
     float* rec;              // [n_layers][n_slots][Hv][dv][dk]
     uint16_t* conv;          // [n_layers][n_slots][K-1][D]
-    int32_t* err;            // device error word
+    int32_t* err;            // device words: [0] error flags, [1] chunked-kernel work ticket
     gdn::GemmCtx* gemm;      // cuBLASLt handle for the projections
     void* gemm_ws;           // its workspace
     uint16_t* proj;          // scratch [rec_cap][D + Hv*dv + 2*Hv]: projection outputs
@@ -76,6 +76,8 @@ struct gdn_pool {
     uint8_t* recs;           // scratch: per-(v-head, token) records of the layer step [Hv][rec_cap][REC_BYTES]
     long long rec_cap;       // tokens per call the scratch holds
 };
+
+static constexpr int kDeviceWords = 16;  // one 64-byte allocation
 
 static long long proj_ld(const gdn_pool* p) { return (long long)p->D + p->cfg.n_v_heads * 128 + 2 * p->cfg.n_v_heads; }
 
@@ -164,7 +166,7 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         delete p;
         return fail(GDN_E_NOMEM, "cudaMalloc of %zu B of conv state failed: %s", conv_bytes, cudaGetErrorString(e));
     }
-    e = cudaMalloc(&p->err, sizeof(int32_t));
+    e = cudaMalloc(&p->err, kDeviceWords * sizeof(int32_t));
     if (e != cudaSuccess) {
         cudaFree(p->rec);
         cudaFree(p->conv);
@@ -173,7 +175,7 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
     }
     e = cudaMemset(p->rec, 0, rec_bytes);
     if (e == cudaSuccess) e = cudaMemset(p->conv, 0, conv_bytes);
-    if (e == cudaSuccess) e = cudaMemset(p->err, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(p->err, 0, kDeviceWords * sizeof(int32_t));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(p->rec);
@@ -421,6 +423,7 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     // chunked tensor-core kernel after the streaming kernel has done the rest.
     const bool has_long = n_tokens > n_seq;
     ra.wy_min_t = has_long ? gdn::WY_MIN_T : 0;
+    ra.wy_counter = p->err + 1;
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
     if (e == cudaSuccess && has_long) e = gdn::launch_wy(ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");

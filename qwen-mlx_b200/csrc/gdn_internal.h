@@ -70,6 +70,7 @@ struct RecurArgs {
     int32_t hk, hv, D;
     int32_t* err;
     int32_t wy_min_t;            // > 0: segments of at least this many tokens go to the chunked kernel
+    int32_t* wy_counter;         // chunked kernel's work-ticket counter (zeroed by launch_wy)
 };
 
 // Sequences of at least this many tokens in one call run the chunked (WY) tensor-core kernel.

@@ -6,9 +6,9 @@
 // at a time.  With lg_t = sum_{j<=t} log g_j inside the chunk, gamma_t = exp(lg_t)
 // and S0 the state entering the chunk:
 //   G = K K^T, QK = Q K^T                                (tensor cores, exact bf16 inputs)
-//   M[t][s] = beta_t exp(lg_t - lg_s) G[t][s]  (s < t),  T = (I + M)^-1   (CUDA cores)
+//   M[t][s] = beta_t exp(lg_t - lg_s) G[t][s]  (s < t),  T = (I + M)^-1   (CUDA cores, blocked)
 //   U = T diag(beta) V,  W = T diag(beta gamma) K          (tensor cores)
-//   D = U - W S0^T                                        (the chunk's rank-1 update vectors)
+//   D = U - W S0^T                                        (accumulated onto U in TMEM)
 //   Y = diag(gamma) Q S0^T + P (.) QK D,  P[t][s] = exp(lg_t - lg_s) (s <= t)
 //   S_C = gamma_C S0 + D^T diag(exp(lg_C - lg_s)) K
 // f32 operands (T, W, S0, D, P (.) QK) enter the bf16 MMAs as hi + lo bf16 pairs
@@ -16,24 +16,28 @@
 // The f32 state S lives in TMEM for the whole sequence: each chunk scales it by
 // gamma_C in place and the state-update MMA accumulates onto it.  The epilogue
 // rounds y to bf16 (metal_gdn.rs:54) and applies silu(z) * rms_norm(y, norm_w, eps)
-// (qwen3_5.rs:660-665) on the row each thread owns.  Decays stay in log space, so
-// long chunks of strong decay cannot underflow into 0/0.
+// (qwen3_5.rs:660-665).  Decays stay in log space, so long chunks of strong decay
+// cannot underflow into 0/0.
 //
-// One CTA (128 threads, 4 warps) per (sequence, v-head) item at a time, persistent
-// over the items whose segment has at least WY_MIN_T tokens; shorter segments stay
-// on the token-sequential recurrence kernel.  Inputs are the prep kernel's records.
+// Every operand tile is stored token-major ([t][d], [t][v], [s][v]) in the core-matrix
+// layout of gdn_umma.cuh and read K-major or MN-major as each product needs, so no tile
+// is ever transposed and every shared-memory store is a 16-byte vector.
 //
-// Shared memory (bytes), K-major bf16 tiles in the layout of gdn_umma.cuh; regions are
-// reused once their last reader (an MMA waited on, or a barrier) is done:
-//   R_K   16K  K [64 t][128 d]            -> W_hi [64 t][128 d]
+// Work items are (sequence, v-head) pairs of the segments with at least wy_min_t
+// tokens.  Each CTA (256 threads, 8 warps, one per SM) first ranks those sequences
+// longest first, then takes items from a global ticket counter, so the longest
+// sequential chains start first.  Inputs are the prep kernel's records; the next
+// chunk's K, V and Q are prefetched with cp.async while the current one computes.
+//
+// Shared memory (bytes); bf16 tiles in the layout of gdn_umma.cuh:
 //   R_Q   16K  Q [64 t][128 d]
-//   R_KT  16K  K^T [128 d][64 s]
-//   R_VT  16K  V^T [128 v][64 s]          -> W_lo
-//   R_M   16K  M f32 [64][64]             -> D^T hi [128 v][64 s]
-//   R_T   16K  T f32 [64][64]             -> D^T lo
-//   R_P   16K  (P(.)QK) hi, lo [64 t][64 s]
-//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] -> Dd^T hi, lo [128 v][64 s]
-//   R_S   64K  S0 hi, lo [128 v][128 d]
+//   R_V   16K  V [64 s][128 v]
+//   R_K   32K  K [64 s][128 d], two buffers (chunk parity)
+//   R_X   64K  S0 hi, lo [128 v][128 d]  -> D hi, D lo, Dd hi, Dd lo [64 s][128 v]
+//   R_T   17K  M, then T = (I + M)^-1 in place (f32, row stride LDT)
+//   R_N    6K  N_ik = T_ii M_ik for the six blocks below the diagonal (f32 16 x 16)
+//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] -> -W hi, -W lo [64 t][128 d]
+//   R_P   16K  (P (.) QK) hi, lo [64 t][64 s]
 // TMEM (512 columns): S [0,128) (M=128 layout), A [128,256), B [256,384), C [384,512)
 // (M=64 accumulators: row t in lane 32*(t/16) + t%16).
 #include "gdn_device.cuh"
@@ -44,21 +48,65 @@
 namespace gdn {
 
 constexpr int WC = 64;                 // tokens per chunk
-constexpr int WY_THREADS = 128;
-constexpr int R_K = 0, R_Q = 16384, R_KT = 32768, R_VT = 49152, R_M = 65536, R_T = 81920, R_P = 98304,
-              R_TB = 114688, R_S = 147456, R_SMALL = 212992;
-constexpr int WY_SMEM = R_SMALL + 4 * 64 * 4 + 128 * 4 + 64;
+constexpr int WY_THREADS = 256;
+constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
+constexpr int WY_SORT_CAP = 1024;      // sequences ranked longest-first; more fall back to call order
+constexpr int R_Q = 0, R_V = 16384, R_K = 32768, R_X = 65536, R_T = 131072, R_N = R_T + WC * LDT * 4,
+              R_TB = 155648, R_P = 188416, R_SMALL = 204800;
+static_assert(R_N + 6 * 256 * 4 <= R_TB, "prefill shared memory layout");
+constexpr int SMALL_FLOATS = 2 * 64 + 2 * 64 + 3 * 64 + 128 + 128;
+constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + WY_SORT_CAP * 4 + 64;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
 constexpr uint32_t TM_S = 0, TM_A = 128, TM_B = 256, TM_C = 384;
 constexpr uint64_t WY_WAIT_NS = 2000000000ull;
 
-__device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
-    hi = f2bf(x);
-    lo = f2bf(x - bf2f(hi));
+__device__ __forceinline__ uint32_t pack_bf2(float lo_half, float hi_half) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo_half, hi_half);
+    return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void st_bf16(uint8_t* base, uint32_t off, uint16_t v) {
-    *reinterpret_cast<uint16_t*>(base + off) = v;
+// hi = bf16(x), lo = bf16(x - hi) for 8 consecutive values, packed as two 16-byte vectors.
+__device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[i] = pack_bf2(x[2 * i], x[2 * i + 1]);
+        l[i] = pack_bf2(x[2 * i] - __uint_as_float(h[i] << 16), x[2 * i + 1] - __uint_as_float(h[i] & 0xFFFF0000u));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// 16-byte vector at row r, column group c8 (8 columns) of a [rows][COLS] bf16 tile.
+template <int COLS>
+__device__ __forceinline__ void st_tile(uint8_t* base, int r, int c8, const uint4& v) {
+    *reinterpret_cast<uint4*>(base + (r >> 3) * (COLS / 8) * 128 + c8 * 128 + (r & 7) * 16) = v;
+}
+
+// Rows [0, 64) of one 256-byte record field into a [64][128] tile; rows >= nv zero-filled.
+// Eight consecutive lanes take eight consecutive rows of one 16-byte column group, so the
+// shared-memory writes of a quarter-warp hit distinct banks and each row's 32-byte sector
+// is read by one instruction.
+__device__ __forceinline__ void load_field(uint32_t dst, const uint8_t* rec0, int field, int nv, int tid) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int idx = tid + i * WY_THREADS;
+        const int t = (idx & 7) | ((idx >> 7) << 3), ch = (idx >> 3) & 15;
+        const bool ok = t < nv;
+        const uint8_t* src = rec0 + (ok ? (size_t)t * REC_BYTES + field + ch * 16 : 0);
+        cp_async16(dst + umma_tile_off(t, ch * 8, 128), src, ok ? 16u : 0u);
+    }
+}
+
+// beta and log g of the chunk's tokens (zero for rows >= nv).
+__device__ __forceinline__ void load_gates(float* s_beta, float* s_lgr, const uint8_t* rec0, int nv, int tid) {
+    if (tid < 2 * WC) {
+        const int t = tid & (WC - 1);
+        const bool ok = t < nv;
+        float* dst = tid < WC ? s_beta + t : s_lgr + t;
+        const uint8_t* src = rec0 + (ok ? (size_t)t * REC_BYTES + (tid < WC ? 1028 : 1032) : 0);
+        cp_async4(smem_u32(dst), src, ok ? 4u : 0u);
+    }
 }
 
 // Wait for the MMAs committed to `bar` (phase `ph`); false on timeout.
@@ -78,25 +126,40 @@ __device__ __forceinline__ void wy_sync_for_mma() {
     tc_fence_after();
 }
 
+__device__ __forceinline__ bool wy_qualifies(const RecurArgs& a, int seq, int& t0, int& T, int& slot) {
+    t0 = __ldg(a.cu_seqlens + seq);
+    T = __ldg(a.cu_seqlens + seq + 1) - t0;
+    slot = __ldg(a.slot_ids + seq);
+    return slot >= 0 && slot < a.n_slots && T >= a.wy_min_t && t0 >= 0 && t0 + T <= a.n_tokens;
+}
+
 __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* s_beta = reinterpret_cast<float*>(smem + R_SMALL);
-    float* s_lg = s_beta + 64;
-    float* s_gam = s_lg + 64;      // exp(lg_t)
-    float* s_tail = s_gam + 64;    // exp(lg_last - lg_t)
-    float* s_nw = s_tail + 64;     // norm_w [128]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(s_nw + 128);
+    float* s_beta = reinterpret_cast<float*>(smem + R_SMALL);  // [2][64] (chunk parity)
+    float* s_lgr = s_beta + 2 * WC;                               // [2][64] log g per token
+    float* s_lg = s_lgr + 2 * WC;                                 // [64] cumulative, log2 units
+    float* s_gam = s_lg + WC;                                     // exp(lg_t)
+    float* s_tail = s_gam + WC;                                   // exp(lg_last - lg_t)
+    float* s_nw = s_tail + WC;                                    // norm_w [128]
+    float* s_ss = s_nw + DV;                                      // [2][64] sum of squares halves
+    int* s_order = reinterpret_cast<int*>(s_ss + 2 * WC);         // sequences, longest first
+    uint64_t* bar = reinterpret_cast<uint64_t*>(s_order + WY_SORT_CAP);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* s_ticket = s_abort + 1;
+    int* s_cnt = const_cast<int*>(s_ticket + 1);
+    float* fT = reinterpret_cast<float*>(smem + R_T);
+    float* fN = reinterpret_cast<float*>(smem + R_N);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t sbase = smem_u32(smem);
-    const int n_items = a.n_seq * a.hv;
+    const int quarter = warp & 3, hh = warp >> 2;   // TMEM lane quarter, column half
+    const uint32_t sb = smem_u32(smem);
     const int ratio = a.hv / a.hk;
 
     if (tid == 0) {
         mbar_init(bar, 1);
         *s_abort = 0;
+        *s_cnt = 0;
         fence_mbar_init();
     }
     for (int i = tid; i < DV; i += WY_THREADS) s_nw[i] = bf2f(a.norm_w[i]);
@@ -105,89 +168,129 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     uint32_t ph = 0;
     pdl_wait();
 
-    // M=64 accumulator row owned by this thread (lanes 0..15 of each warp)
-    const bool row_thread = lane < 16;
-    const int trow = warp * 16 + (lane & 15);
+    // ---- the qualifying sequences, ranked longest first (ties: call order)
+    {
+        int* l_seq = reinterpret_cast<int*>(smem + R_X);
+        int* l_len = l_seq + WY_SORT_CAP;
+        for (int i = tid; i < a.n_seq; i += WY_THREADS) {
+            int t0, T, slot;
+            if (wy_qualifies(a, i, t0, T, slot)) {
+                const int e = atomicAdd(s_cnt, 1);
+                if (e < WY_SORT_CAP) {
+                    l_seq[e] = i;
+                    l_len[e] = T;
+                }
+            }
+        }
+        __syncthreads();
+        const int m = *s_cnt;
+        if (m <= WY_SORT_CAP) {
+            for (int e = tid; e < m; e += WY_THREADS) {
+                const int le = l_len[e], se = l_seq[e];
+                int r = 0;
+                for (int f = 0; f < m; ++f) {
+                    const int lf = l_len[f];
+                    r += (lf > le) || (lf == le && l_seq[f] < se);
+                }
+                s_order[r] = se;
+            }
+        }
+        __syncthreads();
+    }
+    const int m_seq = *s_cnt;
+    const bool ranked = m_seq <= WY_SORT_CAP;
+    const int n_work = (ranked ? m_seq : a.n_seq) * a.hv;
 
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int seq = item / a.hv;
-        const int hv = item - seq * a.hv;
-        const int t0 = __ldg(a.cu_seqlens + seq);
-        const int T = __ldg(a.cu_seqlens + seq + 1) - t0;
-        const int slot = __ldg(a.slot_ids + seq);
-        if (slot < 0 || slot >= a.n_slots || T < a.wy_min_t || t0 < 0 || t0 + T > a.n_tokens) continue;
-        if (*s_abort) break;
+    // M=64 accumulator row owned by this thread (lanes 0..15 of each warp)
+    const bool rt = lane < 16;
+    const int trow = quarter * 16 + (lane & 15);
+    // M=128 row (state row v) owned by this thread
+    const int vrow = quarter * 32 + lane;
+
+    for (;;) {
+        if (tid == 0) *s_ticket = atomicAdd(a.wy_counter, 1);
+        __syncthreads();
+        const int k = *s_ticket;
+        const bool stop = k >= n_work || *s_abort;
+        __syncthreads();
+        if (stop) break;
+        const int si = k / a.hv;
+        const int hv = k - si * a.hv;
+        const int seq = ranked ? s_order[si] : si;
+        int t0, T, slot;
+        if (!wy_qualifies(a, seq, t0, T, slot)) continue;
         float* st = a.rec + ((size_t)slot * a.hv + hv) * (DV * DK);
         const float* st_in = (a.rec_in ? a.rec_in : a.rec) + ((size_t)slot * a.hv + hv) * (DV * DK);
+        const uint8_t* recb = a.recs + ((long long)hv * a.rec_cap + t0) * REC_BYTES;
+        const int n_chunks = (T + WC - 1) / WC;
 
-        // ---- state -> TMEM S (thread v owns row v)
+        // chunk 0's inputs
         {
-            const float* src = st_in + (size_t)tid * DK;
+            const int nv = T < WC ? T : WC;
+            load_field(sb + R_K, recb, 256, nv, tid);
+            load_field(sb + R_Q, recb, 0, nv, tid);
+            load_field(sb + R_V, recb, 512, nv, tid);
+            load_gates(s_beta, s_lgr, recb, nv, tid);
+            cp_async_commit();
+        }
+        // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
+        {
+            const float* src = st_in + (size_t)vrow * DK + hh * 64;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 4; ++j) {
                 float v[16];
 #pragma unroll
                 for (int e = 0; e < 16; e += 4) {
                     const float4 f = __ldcs(reinterpret_cast<const float4*>(src + j * 16 + e));
                     v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
                 }
-                tmem_st16(tmem + lane_base + TM_S + j * 16, v);
+                tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
             }
             tmem_st_wait();
         }
 
-        const int n_chunks = (T + WC - 1) / WC;
-        for (int c = 0; c < n_chunks && !*s_abort; ++c) {
-            const int n0 = t0 + c * WC;
+        for (int c = 0; c < n_chunks; ++c) {
+            const int kb = c & 1;
             const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
-            const uint8_t* rec0 = a.recs + ((long long)hv * a.rec_cap + n0) * REC_BYTES;
+            const uint8_t* rec0 = recb + (size_t)c * WC * REC_BYTES;
+            const bool has_next = c + 1 < n_chunks;
+            const uint8_t* rec1 = rec0 + (size_t)WC * REC_BYTES;
+            const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
+            const uint32_t sK = sb + R_K + kb * 16384;
 
-            // ---- phase A: the chunk's K, Q (K-major), K^T, V^T, beta, log-decay
-            for (int i = tid; i < WC * 16; i += WY_THREADS) {
-                const int t = i >> 4, ch = i & 15;
-                uint4 qv = make_uint4(0, 0, 0, 0), kv = qv, vv = qv;
-                if (t < nv) {
-                    const uint8_t* r = rec0 + (size_t)t * REC_BYTES;
-                    qv = *reinterpret_cast<const uint4*>(r + ch * 16);
-                    kv = *reinterpret_cast<const uint4*>(r + 256 + ch * 16);
-                    vv = *reinterpret_cast<const uint4*>(r + 512 + ch * 16);
-                }
-                *reinterpret_cast<uint4*>(smem + R_Q + umma_tile_off(t, ch * 8, 128)) = qv;
-                *reinterpret_cast<uint4*>(smem + R_K + umma_tile_off(t, ch * 8, 128)) = kv;
-                const uint16_t* k8 = reinterpret_cast<const uint16_t*>(&kv);
-                const uint16_t* v8 = reinterpret_cast<const uint16_t*>(&vv);
+            // ---- phase A: this chunk's inputs landed; next chunk's K and gates in flight
+            cp_async_wait_all();
+            __syncthreads();
+            if (*s_abort) break;
+            if (has_next) {
+                load_field(sb + R_K + (kb ^ 1) * 16384, rec1, 256, nv1, tid);
+                load_gates(s_beta + (kb ^ 1) * WC, s_lgr + (kb ^ 1) * WC, rec1, nv1, tid);
+            }
+            cp_async_commit();
+            if (warp == 0) {
+                // inclusive scan of log g over the chunk, in log2 units
+                float x0 = s_lgr[kb * WC + lane], x1 = s_lgr[kb * WC + 32 + lane];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    st_bf16(smem + R_KT, umma_tile_off(ch * 8 + e, t, 64), k8[e]);
-                    st_bf16(smem + R_VT, umma_tile_off(ch * 8 + e, t, 64), v8[e]);
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+                    const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+                    if (lane >= o) { x0 += y0; x1 += y1; }
                 }
-            }
-            if (tid < WC) {
-                float b = 0.f, ld = 0.f;
-                if (tid < nv) {
-                    const float* gb = reinterpret_cast<const float*>(rec0 + (size_t)tid * REC_BYTES + 1024);
-                    b = gb[1];
-                    ld = gb[2];
-                }
-                s_beta[tid] = b;
-                s_lg[tid] = ld;
-            }
-            __syncthreads();
-            if (tid == 0) {
-                float acc = 0.f;
-                for (int t = 0; t < WC; ++t) {
-                    acc += s_lg[t];
-                    s_lg[t] = acc;
-                }
-            }
-            __syncthreads();
-            if (tid < WC) {
-                s_gam[tid] = expf(s_lg[tid]);
-                s_tail[tid] = expf(s_lg[WC - 1] - s_lg[tid]);
+                x1 += __shfl_sync(0xffffffffu, x0, 31);
+                const float kLog2e = 1.4426950408889634f;
+                x0 *= kLog2e;
+                x1 *= kLog2e;
+                const float last = __shfl_sync(0xffffffffu, x1, 31);
+                s_lg[lane] = x0;
+                s_lg[32 + lane] = x1;
+                s_gam[lane] = exp2f(x0);
+                s_gam[32 + lane] = exp2f(x1);
+                s_tail[lane] = exp2f(last - x0);
+                s_tail[32 + lane] = exp2f(last - x1);
             }
             wy_sync_for_mma();
 
@@ -195,216 +298,320 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             if (tid == 0) {
                 const uint32_t id = umma_idesc_bf16(64, 64);
                 for (int ks = 0; ks < 8; ++ks)
-                    umma_bf16(tmem + TM_A, umma_desc(sbase + R_K, 128, ks), umma_desc(sbase + R_K, 128, ks), id, ks > 0);
+                    umma_bf16(tmem + TM_A, umma_desc(sK, 128, ks), umma_desc(sK, 128, ks), id, ks > 0);
                 for (int ks = 0; ks < 8; ++ks)
-                    umma_bf16(tmem + TM_A + 64, umma_desc(sbase + R_Q, 128, ks), umma_desc(sbase + R_K, 128, ks), id,
-                              ks > 0);
+                    umma_bf16(tmem + TM_A + 64, umma_desc(sb + R_Q, 128, ks), umma_desc(sK, 128, ks), id, ks > 0);
                 umma_commit(bar);
             }
-            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-
-            // ---- phase C1: M (f32) and P (.) QK (hi/lo) from this thread's row
-            {
-                float* fM = reinterpret_cast<float*>(smem + R_M);
-                const float lg_t = s_lg[trow];
-                const float b_t = s_beta[trow];
-                for (int j = 0; j < 4; ++j) {
-                    float gv[16], qv[16];
-                    tmem_ld16(tmem + lane_base + TM_A + j * 16, gv);
-                    tmem_ld16(tmem + lane_base + TM_A + 64 + j * 16, qv);
-                    if (row_thread) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const int s = j * 16 + e;
-                            const float dec = expf(lg_t - s_lg[s]);
-                            fM[trow * 64 + s] = s < trow ? b_t * dec * gv[e] : 0.f;
-                            uint16_t hi, lo;
-                            split_bf16(s <= trow ? dec * qv[e] : 0.f, hi, lo);
-                            st_bf16(smem + R_P, umma_tile_off(trow, s, 64), hi);
-                            st_bf16(smem + R_P + 8192, umma_tile_off(trow, s, 64), lo);
-                        }
-                    }
-                }
-            }
-            // ---- phase C2: S0 hi/lo from TMEM (row v = tid); S *= gamma_last in place
+            // ---- phase C2 (overlaps B): S0 hi/lo tiles [v][d]; S *= gamma_last in place
             {
                 const float g_last = s_gam[WC - 1];
-                for (int j = 0; j < 8; ++j) {
-                    float sv[16];
-                    tmem_ld16(tmem + lane_base + TM_S + j * 16, sv);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        uint16_t hi, lo;
-                        split_bf16(sv[e], hi, lo);
-                        st_bf16(smem + R_S, umma_tile_off(tid, j * 16 + e, 128), hi);
-                        st_bf16(smem + R_S + 32768, umma_tile_off(tid, j * 16 + e, 128), lo);
-                        sv[e] *= g_last;
+                for (int j = 0; j < 4; ++j) {
+                    float sv[16];
+                    tmem_ld16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        uint4 hi, lo;
+                        split8(sv + 8 * u, hi, lo);
+                        st_tile<128>(smem + R_X, vrow, hh * 8 + j * 2 + u, hi);
+                        st_tile<128>(smem + R_X + 32768, vrow, hh * 8 + j * 2 + u, lo);
                     }
-                    tmem_st16(tmem + lane_base + TM_S + j * 16, sv);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) sv[e] *= g_last;
+                    tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
                 }
                 tmem_st_wait();
             }
-            __syncthreads();
+            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
-            // ---- phase C3: T = (I + M)^-1, column s by the lane pair (2s, 2s+1)
+            // ---- phase C1: M (f32 rows) and P (.) QK (hi/lo tiles) of row trow, columns [32 hh, +32)
             {
-                const float* fM = reinterpret_cast<const float*>(smem + R_M);
-                float* fT = reinterpret_cast<float*>(smem + R_T);
-                const int s = tid >> 1, p = tid & 1;
-                if (p == 0) fT[s * 64 + s] = 1.f;
-                __syncwarp();
-                for (int t = 1; t < WC; ++t) {
-                    float acc = 0.f;
-                    if (t > s)
-                        for (int j = s + p; j < t; j += 2) acc += fM[t * 64 + j] * fT[j * 64 + s];
-                    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                    if (t > s && p == 0) fT[t * 64 + s] = -acc;
-                    __syncwarp();
+                const float lg_t = s_lg[trow];
+                const float b_t = s_beta[kb * WC + trow];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    float gv[16], qv[16];
+                    tmem_ld16(tmem + lane_base + TM_A + hh * 32 + j * 16, gv);
+                    tmem_ld16(tmem + lane_base + TM_A + 64 + hh * 32 + j * 16, qv);
+                    if (rt) {
+                        float mv[16], pv[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const int s = hh * 32 + j * 16 + e;
+                            const float dec = exp2f(lg_t - s_lg[s]);
+                            mv[e] = s < trow ? b_t * dec * gv[e] : 0.f;
+                            pv[e] = s <= trow ? dec * qv[e] : 0.f;
+                        }
+                        float* mrow = fT + trow * LDT + hh * 32 + j * 16;
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            *reinterpret_cast<float4*>(mrow + e) = make_float4(mv[e], mv[e + 1], mv[e + 2], mv[e + 3]);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint4 hi, lo;
+                            split8(pv + 8 * u, hi, lo);
+                            st_tile<64>(smem + R_P, trow, hh * 4 + j * 2 + u, hi);
+                            st_tile<64>(smem + R_P + 8192, trow, hh * 4 + j * 2 + u, lo);
+                        }
+                    }
                 }
             }
             __syncthreads();
-            // ---- phase C4: (T beta) and (T beta gamma) as hi/lo bf16 tiles
+
+            // ---- phase C3: T = (I + M)^-1 by 16 x 16 blocks, in place over M
+            // diagonal blocks by forward substitution: lane (block 2 warp + lane/16, column s)
+            if (warp < 2) {
+                const int b = 2 * warp + (lane >> 4), s = lane & 15;
+                float* Mb = fT + 16 * b * LDT + 16 * b;
+                float col[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) col[j] = j == s ? 1.f : 0.f;
+#pragma unroll
+                for (int t = 1; t < 16; ++t) {
+                    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                    for (int j4 = 0; j4 < t; j4 += 4) {
+                        const float4 mv = *reinterpret_cast<const float4*>(Mb + t * LDT + j4);
+                        a0 = fmaf(mv.x, col[j4], a0);
+                        a1 = fmaf(mv.y, col[j4 + 1], a1);
+                        a0 = fmaf(mv.z, col[j4 + 2], a0);
+                        a1 = fmaf(mv.w, col[j4 + 3], a1);
+                    }
+                    if (t > s) col[t] = -(a0 + a1);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) Mb[j * LDT + s] = col[j];
+            }
+            __syncthreads();
             {
-                const float* fT = reinterpret_cast<const float*>(smem + R_T);
-                for (int i = tid; i < WC * WC; i += WY_THREADS) {
-                    const int t = i >> 6, s = i & 63;
-                    const float x = s <= t ? fT[t * 64 + s] : 0.f;
-                    const float tb = x * s_beta[s];
-                    uint16_t hi, lo;
-                    split_bf16(tb, hi, lo);
-                    st_bf16(smem + R_TB, umma_tile_off(t, s, 64), hi);
-                    st_bf16(smem + R_TB + 8192, umma_tile_off(t, s, 64), lo);
-                    split_bf16(tb * s_gam[s], hi, lo);
-                    st_bf16(smem + R_TB + 16384, umma_tile_off(t, s, 64), hi);
-                    st_bf16(smem + R_TB + 24576, umma_tile_off(t, s, 64), lo);
+                const int r = tid >> 4, cc = tid & 15;
+                // N_ik = T_ii M_ik for the six blocks below the diagonal (pair index i(i-1)/2 + k)
+#pragma unroll
+                for (int p = 0; p < 6; ++p) {
+                    const int i = p < 1 ? 1 : (p < 3 ? 2 : 3);
+                    const int kk = p - i * (i - 1) / 2;
+                    const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
+                    const float* Mk = fT + 16 * i * LDT + 16 * kk + cc;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int m4 = 0; m4 < 16; m4 += 4) {
+                        const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
+                        acc = fmaf(tr.x, Mk[(m4 + 0) * LDT], acc);
+                        acc = fmaf(tr.y, Mk[(m4 + 1) * LDT], acc);
+                        acc = fmaf(tr.z, Mk[(m4 + 2) * LDT], acc);
+                        acc = fmaf(tr.w, Mk[(m4 + 3) * LDT], acc);
+                    }
+                    fN[p * 256 + r * 16 + cc] = acc;
+                }
+                __syncthreads();
+                // block rows 1..3: T_ij = -sum_{k=j}^{i-1} N_ik T_kj
+#pragma unroll
+                for (int i = 1; i < 4; ++i) {
+#pragma unroll
+                    for (int j = 0; j < i; ++j) {
+                        float acc = 0.f;
+#pragma unroll
+                        for (int kk = j; kk < i; ++kk) {
+                            const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
+                            const float* Tc = fT + 16 * kk * LDT + 16 * j + cc;
+#pragma unroll
+                            for (int m4 = 0; m4 < 16; m4 += 4) {
+                                const float4 nr = *reinterpret_cast<const float4*>(Nr + m4);
+                                acc = fmaf(nr.x, Tc[(m4 + 0) * LDT], acc);
+                                acc = fmaf(nr.y, Tc[(m4 + 1) * LDT], acc);
+                                acc = fmaf(nr.z, Tc[(m4 + 2) * LDT], acc);
+                                acc = fmaf(nr.w, Tc[(m4 + 3) * LDT], acc);
+                            }
+                        }
+                        fT[(16 * i + r) * LDT + 16 * j + cc] = -acc;
+                    }
+                    __syncthreads();
+                }
+            }
+
+            // ---- phase C4: (T beta) and (T beta gamma) hi/lo tiles; thread (row t, columns [16 cq, +16))
+            {
+                const int t = tid & 63, cq = tid >> 6;
+                const float* Tr = fT + t * LDT + 16 * cq;
+                float tb[16], tg[16];
+#pragma unroll
+                for (int e4 = 0; e4 < 16; e4 += 4) {
+                    const float4 x = *reinterpret_cast<const float4*>(Tr + e4);
+                    tb[e4] = x.x; tb[e4 + 1] = x.y; tb[e4 + 2] = x.z; tb[e4 + 3] = x.w;
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int s = 16 * cq + e;
+                    const float x = s <= t ? tb[e] * s_beta[kb * WC + s] : 0.f;
+                    tb[e] = x;
+                    tg[e] = x * s_gam[s];
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    uint4 hi, lo;
+                    split8(tb + 8 * u, hi, lo);
+                    st_tile<64>(smem + R_TB, t, 2 * cq + u, hi);
+                    st_tile<64>(smem + R_TB + 8192, t, 2 * cq + u, lo);
+                    split8(tg + 8 * u, hi, lo);
+                    st_tile<64>(smem + R_TB + 16384, t, 2 * cq + u, hi);
+                    st_tile<64>(smem + R_TB + 24576, t, 2 * cq + u, lo);
                 }
             }
             wy_sync_for_mma();
 
-            // ---- phase D: U = (T beta) V -> B;  W = (T beta gamma) K -> C
+            // ---- phase D: U = (T beta) V -> B;  W = (T beta gamma) K -> C   (V, K read MN-major)
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(64, 128);
+                const uint32_t id = umma_idesc_bf16(64, 128, false, true);
                 for (int h = 0; h < 2; ++h)
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_B, umma_desc(sbase + R_TB + h * 8192, 64, ks), umma_desc(sbase + R_VT, 64, ks),
+                        umma_bf16(tmem + TM_B, umma_desc(sb + R_TB + h * 8192, 64, ks), umma_desc_mn(sb + R_V, 128, ks),
                                   id, (h | ks) != 0);
                 for (int h = 0; h < 2; ++h)
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_C, umma_desc(sbase + R_TB + 16384 + h * 8192, 64, ks),
-                                  umma_desc(sbase + R_KT, 64, ks), id, (h | ks) != 0);
+                        umma_bf16(tmem + TM_C, umma_desc(sb + R_TB + 16384 + h * 8192, 64, ks), umma_desc_mn(sK, 128, ks),
+                                  id, (h | ks) != 0);
                 umma_commit(bar);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            if (has_next) load_field(sb + R_V, rec1, 512, nv1, tid);   // V is free
+            cp_async_commit();
 
-            // ---- phase E: W hi/lo tiles; then W S0^T -> A and Q S0^T -> C
-            for (int j = 0; j < 8; ++j) {
-                float wv[16];
-                tmem_ld16(tmem + lane_base + TM_C + j * 16, wv);
-                if (row_thread) {
+            // ---- phase E: -W hi/lo tiles [t][d]; then D = U - W S0^T onto B, Q S0^T -> C
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        uint16_t hi, lo;
-                        split_bf16(wv[e], hi, lo);
-                        st_bf16(smem + R_K, umma_tile_off(trow, j * 16 + e, 128), hi);
-                        st_bf16(smem + R_VT, umma_tile_off(trow, j * 16 + e, 128), lo);
+            for (int j = 0; j < 4; ++j) {
+                float wv[16];
+                tmem_ld16(tmem + lane_base + TM_C + hh * 64 + j * 16, wv);
+                if (rt) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) wv[e] = -wv[e];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        uint4 hi, lo;
+                        split8(wv + 8 * u, hi, lo);
+                        st_tile<128>(smem + R_TB, trow, hh * 8 + j * 2 + u, hi);
+                        st_tile<128>(smem + R_TB + 16384, trow, hh * 8 + j * 2 + u, lo);
                     }
                 }
             }
             wy_sync_for_mma();
             if (tid == 0) {
                 const uint32_t id = umma_idesc_bf16(64, 128);
-                const uint32_t aw[3] = {R_K, R_K, R_VT}, bs[3] = {R_S, R_S + 32768, R_S};
+                const uint32_t aw[3] = {R_TB, R_TB, R_TB + 16384}, bs[3] = {R_X, R_X + 32768, R_X};
                 for (int p = 0; p < 3; ++p)
                     for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_A, umma_desc(sbase + aw[p], 128, ks), umma_desc(sbase + bs[p], 128, ks), id,
-                                  (p | ks) != 0);
+                        umma_bf16(tmem + TM_B, umma_desc(sb + aw[p], 128, ks), umma_desc(sb + bs[p], 128, ks), id, 1u);
                 for (int h = 0; h < 2; ++h)
                     for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_C, umma_desc(sbase + R_Q, 128, ks), umma_desc(sbase + R_S + h * 32768, 128, ks),
-                                  id, (h | ks) != 0);
+                        umma_bf16(tmem + TM_C, umma_desc(sb + R_Q, 128, ks), umma_desc(sb + R_X + h * 32768, 128, ks), id,
+                                  (h | ks) != 0);
                 umma_commit(bar);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            if (has_next) load_field(sb + R_Q, rec1, 0, nv1, tid);     // Q is free
+            cp_async_commit();
 
-            // ---- phase F: D = U - W S0^T; D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles
+            // ---- phase F: D and Dd = diag(exp(lg_last - lg_s)) D as hi/lo tiles [s][v]
             {
                 const float tail = s_tail[trow];
-                for (int j = 0; j < 8; ++j) {
-                    float uv[16], wsv[16];
-                    tmem_ld16(tmem + lane_base + TM_B + j * 16, uv);
-                    tmem_ld16(tmem + lane_base + TM_A + j * 16, wsv);
-                    if (row_thread) {
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const int v = j * 16 + e;
-                            const float d = uv[e] - wsv[e];
-                            uint16_t hi, lo;
-                            split_bf16(d, hi, lo);
-                            st_bf16(smem + R_M, umma_tile_off(v, trow, 64), hi);
-                            st_bf16(smem + R_T, umma_tile_off(v, trow, 64), lo);
-                            split_bf16(d * tail, hi, lo);
-                            st_bf16(smem + R_TB, umma_tile_off(v, trow, 64), hi);
-                            st_bf16(smem + R_TB + 16384, umma_tile_off(v, trow, 64), lo);
+                for (int j = 0; j < 4; ++j) {
+                    float dv[16];
+                    tmem_ld16(tmem + lane_base + TM_B + hh * 64 + j * 16, dv);
+                    if (rt) {
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint4 hi, lo;
+                            split8(dv + 8 * u, hi, lo);
+                            st_tile<128>(smem + R_X, trow, hh * 8 + j * 2 + u, hi);
+                            st_tile<128>(smem + R_X + 16384, trow, hh * 8 + j * 2 + u, lo);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) dv[e] *= tail;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint4 hi, lo;
+                            split8(dv + 8 * u, hi, lo);
+                            st_tile<128>(smem + R_X + 32768, trow, hh * 8 + j * 2 + u, hi);
+                            st_tile<128>(smem + R_X + 49152, trow, hh * 8 + j * 2 + u, lo);
                         }
                     }
                 }
             }
             wy_sync_for_mma();
-            // ---- phase G: (P (.) QK) D -> B;  S += Dd^T K -> S
+            // ---- phase G: (P (.) QK) D -> A;  S += Dd^T K -> S   (D, Dd, K read MN-major)
             if (tid == 0) {
-                const uint32_t id64 = umma_idesc_bf16(64, 128);
-                const uint32_t ap[3] = {R_P, R_P, R_P + 8192}, bd[3] = {R_M, R_T, R_M};
+                const uint32_t id64 = umma_idesc_bf16(64, 128, false, true);
+                const uint32_t ap[3] = {R_P, R_P, R_P + 8192}, bd[3] = {R_X, R_X + 16384, R_X};
                 for (int p = 0; p < 3; ++p)
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_B, umma_desc(sbase + ap[p], 64, ks), umma_desc(sbase + bd[p], 64, ks), id64,
+                        umma_bf16(tmem + TM_A, umma_desc(sb + ap[p], 64, ks), umma_desc_mn(sb + bd[p], 128, ks), id64,
                                   (p | ks) != 0);
-                const uint32_t id128 = umma_idesc_bf16(128, 128);
+                const uint32_t id128 = umma_idesc_bf16(128, 128, true, true);
                 for (int h = 0; h < 2; ++h)
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_S, umma_desc(sbase + R_TB + h * 16384, 64, ks), umma_desc(sbase + R_KT, 64, ks),
-                                  id128, 1u);
+                        umma_bf16(tmem + TM_S, umma_desc_mn(sb + R_X + 32768 + h * 16384, 128, ks),
+                                  umma_desc_mn(sK, 128, ks), id128, 1u);
                 umma_commit(bar);
+            }
+            // silu(z) of this row's 64 columns, loaded while the MMAs run
+            const bool valid = rt && trow < nv;
+            uint4 zr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) zr[i] = make_uint4(0, 0, 0, 0);
+            if (valid) {
+                const uint8_t* zp = rec0 + (size_t)trow * REC_BYTES + 768 + hh * 128;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
             // ---- phase H: y = gamma_t Q S0^T + (P (.) QK) D, rounded to bf16; gated RMSNorm
             {
-                const bool valid = row_thread && trow < nv;
                 const float gam = s_gam[trow];
+                float y[64];
                 float ss = 0.f;
-                for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
                     float qs[16], pd[16];
-                    tmem_ld16(tmem + lane_base + TM_C + j * 16, qs);
-                    tmem_ld16(tmem + lane_base + TM_B + j * 16, pd);
+                    tmem_ld16(tmem + lane_base + TM_C + hh * 64 + j * 16, qs);
+                    tmem_ld16(tmem + lane_base + TM_A + hh * 64 + j * 16, pd);
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const float y = rbf(gam * qs[e] + pd[e]);
-                        ss += y * y;
+                        const float yy = rbf(gam * qs[e] + pd[e]);
+                        y[j * 16 + e] = yy;
+                        ss += yy * yy;
                     }
                 }
-                const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
-                const long long n = (long long)n0 + trow;
-                const uint8_t* rec = rec0 + (size_t)trow * REC_BYTES;
-                for (int j = 0; j < 8; ++j) {
-                    float qs[16], pd[16];
-                    tmem_ld16(tmem + lane_base + TM_C + j * 16, qs);
-                    tmem_ld16(tmem + lane_base + TM_B + j * 16, pd);
-                    if (valid) {
-                        const uint4 z0 = *reinterpret_cast<const uint4*>(rec + 768 + j * 32);
-                        const uint4 z1 = *reinterpret_cast<const uint4*>(rec + 768 + j * 32 + 16);
-                        const uint16_t* zz0 = reinterpret_cast<const uint16_t*>(&z0);
-                        const uint16_t* zz1 = reinterpret_cast<const uint16_t*>(&z1);
-                        uint16_t o[16];
+                if (rt) s_ss[hh * WC + trow] = ss;
+                __syncthreads();
+                if (valid) {
+                    const float tot = s_ss[trow] + s_ss[WC + trow];
+                    const float nrm = 1.0f / sqrtf(tot / (float)DV + a.eps);
+                    uint16_t* dst = a.out + (long long)(t0 + c * WC + trow) * a.ld_out + (long long)hv * DV + hh * 64;
+                    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const float y = rbf(gam * qs[e] + pd[e]);
-                            const float yn = rbf(rbf(y * nrm) * s_nw[j * 16 + e]);
-                            const float zs = bf2f(e < 8 ? zz0[e] : zz1[e - 8]);
-                            o[e] = f2bf(zs * yn);
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t zw[4] = {zr[i].x, zr[i].y, zr[i].z, zr[i].w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            const int col = i * 8 + 2 * e2;
+                            const float yn0 = rbf(rbf(y[col] * nrm) * s_nw[hh * 64 + col]);
+                            const float yn1 = rbf(rbf(y[col + 1] * nrm) * s_nw[hh * 64 + col + 1]);
+                            const float z0 = __uint_as_float(zw[e2] << 16), z1 = __uint_as_float(zw[e2] & 0xFFFF0000u);
+                            o[e2] = (uint32_t)f2bf(z0 * yn0) | ((uint32_t)f2bf(z1 * yn1) << 16);
                         }
-                        uint16_t* dst = a.out + n * a.ld_out + (long long)hv * DV + j * 16;
+                        if (vec) {
+                            *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+                        } else {
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) dst[e] = o[e];
+                            for (int e2 = 0; e2 < 4; ++e2) {
+                                dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
+                                dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
+                            }
+                        }
                     }
                 }
             }
@@ -412,13 +619,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             __syncthreads();
             tc_fence_after();
         }
+        cp_async_wait_all();
 
-        // ---- state back to the pool (row v = tid)
+        // ---- state back to the pool (row v, columns [64 half, +64))
         {
-            float* dst = st + (size_t)tid * DK;
-            for (int j = 0; j < 8; ++j) {
+            float* dst = st + (size_t)vrow * DK + hh * 64;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
                 float v[16];
-                tmem_ld16(tmem + lane_base + TM_S + j * 16, v);
+                tmem_ld16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
 #pragma unroll
                 for (int e = 0; e < 16; e += 4)
                     __stcs(reinterpret_cast<float4*>(dst + j * 16 + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
@@ -446,6 +655,7 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         tc_fence_after();
     }
 
+    cp_async_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
@@ -458,6 +668,7 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!r.wy_counter) return cudaErrorInvalidValue;
     if (g_wy_sms[dev] == 0) {
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -468,6 +679,8 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     }
     const int n_items = r.n_seq * r.hv;
     if (n_items == 0) return cudaSuccess;
+    e = cudaMemsetAsync(r.wy_counter, 0, sizeof(int32_t), stream);
+    if (e != cudaSuccess) return e;
     const int grid = n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev];
     gdn_wy_kernel<<<grid, WY_THREADS, WY_SMEM, stream>>>(r);
     return cudaGetLastError();
