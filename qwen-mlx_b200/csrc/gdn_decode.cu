@@ -1,7 +1,8 @@
 // gdn_decode.cu -- the fused GDN layer step as two kernels chained with
 // programmatic dependent launch (sm_100a).
 //
-// K1 gdn_prep_kernel (token-parallel, small): for every packed token and
+// K1 gdn_prep_kernel (token-parallel, small; gdn_prep_tile_kernel, its tiled form, serves
+//    calls with multi-token segments): for every packed token and
 //    k-head group, the causal depthwise conv + SiLU of its q, k and v channels
 //    (reference rounding: S=1 -> bf16 products and bf16 sum, qwen3_5.rs:602-610;
 //    S>1 -> f32 conv1d, qwen3_5.rs:617-623), q/k RMSNorm with gains 1/dk and
@@ -222,6 +223,215 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
         gb[0] = expf(logdecay);
         gb[1] = rbf(sigmoid_f32(gb_b));
         gb[2] = logdecay;  // log g, for the chunked prefill kernel
+    }
+}
+
+// ------------------------------------------------------------------ K1, tiled
+
+constexpr int PT_TOK = 16;  // packed tokens per tiled-prep CTA
+
+__device__ __forceinline__ void unpack_pair(uint32_t u, float& lo, float& hi) {
+    lo = __uint_as_float(u << 16);
+    hi = __uint_as_float(u & 0xffff0000u);
+}
+
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+    return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+
+// Token loop of the tiled prep.  SIMPLE: every token of the tile sits at position >= 3 of a
+// multi-token sequence, so no tap comes from the conv window and no token takes the decode
+// rounding (nearly every prefill tile).
+template <bool SIMPLE>
+__device__ __forceinline__ void prep_tile_tokens(const PrepArgs& a, int ch, bool is_qk, bool has_pair, bool z_ok,
+                                                 uint8_t* vrec, uint8_t* zrec, const float (&w)[2][4],
+                                                 uint32_t (*s_x)[256], const uint32_t (*s_z)[128], const int* s_seq,
+                                                 const int* s_t, const int* s_T, const int* s_slot,
+                                                 float (*s_red)[PT_TOK]) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t win[KC - 1] = {s_x[0][tid], s_x[1][tid], s_x[2][tid]};
+#pragma unroll 1
+    for (int j = 0; j < PT_TOK; ++j) {
+        const uint32_t cur = s_x[j + KC - 1][tid];
+        const bool valid = s_seq[j] >= 0;
+        float o0 = 0.f, o1 = 0.f;
+        if (valid) {
+            if (has_pair) {
+                uint32_t tap[KC] = {win[0], win[1], win[2], cur};
+                bool decode = false;
+                if (!SIMPLE) {
+                    const int t = s_t[j];
+                    decode = s_T[j] == 1;
+                    uint16_t* cs = a.conv + (size_t)s_slot[j] * (KC - 1) * a.D;
+#pragma unroll
+                    for (int p = 0; p < KC - 1; ++p)
+                        if (t + p < KC - 1) tap[p] = *reinterpret_cast<const uint32_t*>(cs + (size_t)(t + p) * a.D + ch);
+                    if (decode) {
+#pragma unroll
+                        for (int p = 0; p < KC - 1; ++p)
+                            *reinterpret_cast<uint32_t*>(cs + (size_t)p * a.D + ch) = tap[p + 1];
+                    }
+                }
+                float x0[4], x1[4];
+#pragma unroll
+                for (int p = 0; p < KC; ++p) unpack_pair(tap[p], x0[p], x1[p]);
+                o0 = conv_silu(x0, w[0], decode);
+                o1 = conv_silu(x1, w[1], decode);
+                if (!is_qk) *reinterpret_cast<uint32_t*>(vrec + (size_t)j * REC_BYTES) = pack_pair(o0, o1);
+            }
+            if (z_ok) {
+                const uint32_t zp = s_z[j][tid >> 1];
+                const float zv = __uint_as_float((tid & 1) ? (zp & 0xffff0000u) : (zp << 16));
+                *reinterpret_cast<uint16_t*>(zrec + (size_t)j * REC_BYTES) = f2bf(silu_bf(zv));
+            }
+        }
+        if (is_qk) {
+            // o0, o1 are bf16 values: park them exactly in this thread's spent row j
+            s_x[j][tid] = pack_pair(o0, o1);
+            const float ss = warp_sum(o0 * o0 + o1 * o1);
+            if (lane == 0) s_red[warp][j] = ss;
+        }
+        win[0] = win[1];
+        win[1] = win[2];
+        win[2] = cur;
+    }
+}
+
+// Tiled K1 for calls that carry multi-token segments: one CTA per (16 consecutive packed
+// tokens, k-head), same records and rounding as gdn_prep_kernel.  Thread tid owns one bf16
+// channel pair: threads 0..63 q pairs, 64..127 k pairs, 128..255 the v pairs of the k-head's
+// v-heads (Hv/Hk <= 2); and z column tid of those heads.  The pair's 19 tap rows (3 before the
+// tile) and the z pairs are fetched up front with cp.async into shared columns; a rolled
+// token loop then slides a 3-row window through registers, so a tap row is read once per
+// tile and the loop body stays small.  q / k outputs wait in the thread's own spent tap rows
+// until the RMSNorm sums are known.  Needs qkv / z rows at 4-byte alignment.
+__global__ void __launch_bounds__(256) gdn_prep_tile_kernel(const PrepArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ uint32_t s_x[PT_TOK + KC - 1][256];  // [row][thread]: rows n0-3 .. n0+15 of the pair
+    __shared__ uint32_t s_z[PT_TOK][128];           // z pairs of the group, loaded by the v threads
+    __shared__ int s_seq[PT_TOK], s_t[PT_TOK], s_T[PT_TOK], s_slot[PT_TOK];
+    __shared__ float s_red[4][PT_TOK];
+
+    const int n0 = blockIdx.x * PT_TOK;
+    const int hk = blockIdx.y;
+    const int tid = threadIdx.x;
+    const int ratio = a.hv / a.hk;
+    const bool is_qk = tid < 128, is_q = tid < 64;
+    // this thread's channel pair
+    int ch, v_hv = 0, v_c = 0;
+    bool has_pair = true;
+    if (is_qk) {
+        ch = (is_q ? 0 : a.hk * DK) + hk * DK + 2 * (tid & 63);
+    } else {
+        const int vi = 2 * (tid - 128);
+        has_pair = vi < ratio * DV;
+        v_hv = hk * ratio + vi / DV;
+        v_c = vi % DV;
+        ch = 2 * a.hk * DK + v_hv * DV + v_c;
+    }
+
+    // ---- inputs of the pair: tap rows and z, asynchronously
+    if (has_pair) {
+#pragma unroll
+        for (int r = 0; r < PT_TOK + KC - 1; ++r) {
+            const int row = n0 - (KC - 1) + r;
+            const bool ok = row >= 0 && row < a.n_tokens;
+            cp_async4(smem_u32(&s_x[r][tid]), a.qkv + (ok ? (long long)row * a.ld_qkv + ch : 0), ok ? 4u : 0u);
+        }
+        if (!is_qk) {
+#pragma unroll
+            for (int j = 0; j < PT_TOK; ++j) {
+                const bool ok = n0 + j < a.n_tokens;
+                cp_async4(smem_u32(&s_z[j][tid - 128]),
+                          a.z + (ok ? (long long)(n0 + j) * a.ld_z + (long long)v_hv * DV + v_c : 0), ok ? 4u : 0u);
+            }
+        }
+    }
+    cp_async_commit();
+
+    // ---- routing of the tile's tokens (s_seq < 0: no such token, or a rejected sequence)
+    bool simple_tok = true;
+    if (tid < PT_TOK) {
+        const int n = n0 + tid;
+        int seq = -1, t = 0, T = 0, slot = -1;
+        if (n < a.n_tokens) {
+            const int guess = n < a.n_seq ? n : a.n_seq - 1;
+            if (__ldg(a.cu_seqlens + guess) <= n && n < __ldg(a.cu_seqlens + guess + 1))
+                seq = guess;
+            else
+                seq = find_seq(a.cu_seqlens, a.n_seq, n);
+            if (seq < 0) {
+                if (hk == 0) atomicOr(a.err, ERR_BAD_SEQLENS);
+            } else {
+                const int t0 = __ldg(a.cu_seqlens + seq);
+                T = __ldg(a.cu_seqlens + seq + 1) - t0;
+                slot = __ldg(a.slot_ids + seq);
+                t = n - t0;
+                if (slot < 0 || slot >= a.n_slots || t0 + T > a.n_tokens) {
+                    if (hk == 0 && t == 0) atomicOr(a.err, slot < 0 || slot >= a.n_slots ? ERR_BAD_SLOT : ERR_BAD_SEQLENS);
+                    seq = -1;
+                }
+            }
+        }
+        s_seq[tid] = seq;
+        s_t[tid] = t;
+        s_T[tid] = T;
+        s_slot[tid] = slot;
+        simple_tok = seq < 0 || (t >= KC - 1 && T > 1);
+    }
+    cp_async_wait_all();
+    const bool simple = __syncthreads_and(simple_tok) != 0;
+
+    float w[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (has_pair) {
+        unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)ch * KC)), w[0]);
+        unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)(ch + 1) * KC)), w[1]);
+    }
+    const bool z_ok = tid < ratio * DV;
+    uint8_t* vrec = a.rec + ((long long)v_hv * a.rec_cap + n0) * REC_BYTES + 512 + 2 * v_c;
+    uint8_t* zrec = a.rec + ((long long)(hk * ratio + tid / DV) * a.rec_cap + n0) * REC_BYTES + 768 + 2 * (tid % DV);
+
+    // ---- conv + SiLU over the tile's tokens; v and silu(z) go straight to the records
+    if (simple)
+        prep_tile_tokens<true>(a, ch, is_qk, has_pair, z_ok, vrec, zrec, w, s_x, s_z, s_seq, s_t, s_T, s_slot, s_red);
+    else
+        prep_tile_tokens<false>(a, ch, is_qk, has_pair, z_ok, vrec, zrec, w, s_x, s_z, s_seq, s_t, s_T, s_slot, s_red);
+
+    // ---- q / k RMSNorm with the scale folded into the gain
+    if (is_qk) {
+        named_bar_sync(1, 128);
+        const float gain = is_q ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
+        const int w0 = is_q ? 0 : 2;
+        const int off = (is_q ? 0 : 256) + 4 * (tid & 63);
+#pragma unroll 1
+        for (int j = 0; j < PT_TOK; ++j) {
+            if (s_seq[j] < 0) continue;
+            const float tot = s_red[w0][j] + s_red[w0 + 1][j];
+            const float nrm = 1.0f / sqrtf(tot / (float)DK + 1e-6f);
+            float o0, o1;
+            unpack_pair(s_x[j][tid], o0, o1);
+            const uint32_t val = pack_pair(rbf(o0 * nrm) * gain, rbf(o1 * nrm) * gain);
+            for (int r = 0; r < ratio; ++r) {
+                uint8_t* rec = a.rec + ((long long)(hk * ratio + r) * a.rec_cap + n0 + j) * REC_BYTES;
+                *reinterpret_cast<uint32_t*>(rec + off) = val;
+            }
+        }
+    }
+    // ---- gates (compiled_beta_g)
+    for (int idx = tid; idx < PT_TOK * ratio; idx += 256) {
+        const int j = idx / ratio;
+        if (s_seq[j] < 0) continue;
+        const int n = n0 + j;
+        const int hv = hk * ratio + idx % ratio;
+        const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
+        const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
+        const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+        const float logdecay = -(expf(a.A_log[hv]) * sp);
+        float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
+        gb[0] = expf(logdecay);
+        gb[1] = rbf(sigmoid_f32(b));
+        gb[2] = logdecay;
     }
 }
 
@@ -492,13 +702,18 @@ cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStre
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
 
+    // Calls with multi-token segments take the tiled prep when the bf16 pair loads are aligned.
+    const bool pairs_aligned = ((reinterpret_cast<uintptr_t>(p.qkv) | reinterpret_cast<uintptr_t>(p.z)) & 3u) == 0 &&
+                               (p.ld_qkv & 1) == 0 && (p.ld_z & 1) == 0;
+    const bool tiled = p.n_tokens > p.n_seq && pairs_aligned && p.hv <= 2 * p.hk;
     cudaLaunchConfig_t c1 = {};
-    c1.gridDim = dim3((unsigned)p.n_tokens, (unsigned)p.hk, 1);
+    c1.gridDim = tiled ? dim3((unsigned)((p.n_tokens + PT_TOK - 1) / PT_TOK), (unsigned)p.hk, 1)
+                       : dim3((unsigned)p.n_tokens, (unsigned)p.hk, 1);
     c1.blockDim = dim3(256, 1, 1);
     c1.stream = stream;
     c1.attrs = attr;
     c1.numAttrs = 1;
-    e = cudaLaunchKernelEx(&c1, gdn_prep_kernel, p);
+    e = tiled ? cudaLaunchKernelEx(&c1, gdn_prep_tile_kernel, p) : cudaLaunchKernelEx(&c1, gdn_prep_kernel, p);
     if (e != cudaSuccess) return e;
 
     const int n_items = r.n_seq * r.hv;

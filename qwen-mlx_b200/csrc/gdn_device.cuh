@@ -24,7 +24,8 @@ __device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(
 // Round an f32 value to bf16 precision (round-to-nearest-even) and widen back.
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 
-__device__ __forceinline__ float sigmoid_f32(float x) { return 1.0f / (1.0f + expf(-x)); }
+// 1 / (1 + exp(-x)); the correctly rounded reciprocal equals the correctly rounded quotient 1 / y.
+__device__ __forceinline__ float sigmoid_f32(float x) { return __frcp_rn(1.0f + expf(-x)); }
 // nn::silu on a bf16 value: computed in f32, rounded once to bf16.
 __device__ __forceinline__ float silu_bf(float x) { return rbf(x * sigmoid_f32(x)); }
 
