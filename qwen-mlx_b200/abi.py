@@ -1,4 +1,4 @@
-"""ctypes declarations of include/gdn.h for libgdn_b200.so.
+"""ctypes declarations of include/gdn.h and include/gdn_host.h for libgdn_b200.so.
 
 The library is the product; this module only binds it.  Loading fails loudly
 when the library has not been built: there is no fallback implementation.
@@ -19,6 +19,12 @@ GDN_E_BAD_SEQLENS = 4
 GDN_E_CUDA = 5
 GDN_E_NOMEM = 6
 GDN_E_DEVICE = 7
+
+GDN_ENTRY_DECODE = 0
+GDN_ENTRY_PREFILL_FIRST = 1
+GDN_ENTRY_PREFILL_CONT = 2
+GDN_FINISH_EOS = 0
+GDN_FINISH_MAX_TOKENS = 1
 
 # Every function declared in include/gdn.h, with (restype, argtypes).
 _vp = C.c_void_p
@@ -43,6 +49,20 @@ class GdnStepIOC(C.Structure):
 
 class GdnMixerWeightsC(C.Structure):
     _fields_ = [("step", GdnLayerWeightsC), ("w_in", _vp), ("w_out", _vp), ("pre_norm_w", _vp)]
+
+
+class GdnStepEntryC(C.Structure):
+    _fields_ = [("seq_id", C.c_uint64), ("slot", _i32), ("n_tokens", _i32), ("kind", _i32), ("pos", _i32)]
+
+
+class GdnSchedConfigC(C.Structure):
+    _fields_ = [("n_shards", _i32), ("slots_per_shard", _i32), ("max_batch", _i32), ("prefill_budget", _i32),
+                ("prefill_chunk", _i32)]
+
+
+class GdnSchedStatsC(C.Structure):
+    _fields_ = [("total_requests", C.c_uint64), ("tokens_generated", C.c_uint64), ("iterations", C.c_uint64),
+                ("active", _i32), ("waiting", _i32), ("prefilling", _i32), ("free_slots", _i32)]
 
 
 SIGNATURES = {
@@ -71,6 +91,17 @@ SIGNATURES = {
     "gdn_beta_g": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gdn_layer_step_noalloc": (_int, [C.POINTER(GdnConfigC), _i32, _vp, _vp, C.POINTER(GdnLayerWeightsC),
                                       C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32, _vp]),
+    # include/gdn_host.h
+    "gdn_pack_step": (_int, [C.POINTER(GdnStepEntryC), _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gdn_sched_create": (_int, [C.POINTER(GdnSchedConfigC), C.POINTER(_vp)]),
+    "gdn_sched_destroy": (_int, [_vp]),
+    "gdn_sched_enqueue": (_int, [_vp, _i32, _i32, C.POINTER(C.c_uint64)]),
+    "gdn_sched_plan": (_int, [_vp, C.POINTER(GdnStepEntryC), _i32, C.POINTER(_i32)]),
+    "gdn_sched_complete": (_int, [_vp, _vp]),
+    "gdn_sched_drain_finished": (_int, [_vp, C.POINTER(C.c_uint64), C.POINTER(_i32), _i32, C.POINTER(_i32)]),
+    "gdn_sched_stats_get": (_int, [_vp, C.POINTER(GdnSchedStatsC)]),
+    "gdn_sched_active_ids": (_int, [_vp, C.POINTER(C.c_uint64), _i32, C.POINTER(_i32)]),
+    "gdn_sched_free_slots": (_int, [_vp, _i32, C.POINTER(_i32)]),
 }
 
 

@@ -2,9 +2,9 @@
 
     python qwen-mlx_b200/build.py [--force] [--verbose]
 
-Compiles every CUDA source under csrc/ with nvcc for sm_100a
+Compiles every CUDA source (and the host-only C++ sources) under csrc/ with nvcc for sm_100a
 (-gencode arch=compute_100a,code=sm_100a) into qwen-mlx_b200/libgdn_b200.so,
-which exports the C ABI declared in include/gdn.h.  The CUDA runtime is linked
+which exports the C ABI declared in include/gdn.h and include/gdn_host.h.  The CUDA runtime is linked
 statically; cuBLASLt (the projection GEMMs) dynamically, with an rpath to the
 toolkit.
 """
@@ -28,7 +28,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
 
 
 def sources():
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _stale() -> bool:

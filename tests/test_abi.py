@@ -9,18 +9,19 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "gdn.h"
+INCLUDE = Path(__file__).resolve().parents[1] / "include"
 
 
 def declared_functions():
-    text = HEADER.read_text()
+    text = "".join(h.read_text() for h in sorted(INCLUDE.glob("*.h")))
     return sorted(set(re.findall(r"GDN_API\s+[\w\s\*]*?\b(gdn_\w+)\s*\(", text)))
 
 
 def test_header_declares_functions():
     names = declared_functions()
     assert "gdn_layer_step" in names and "gdn_gated_delta_kernel" in names
-    assert len(names) >= 15
+    assert "gdn_sched_plan" in names and "gdn_pack_step" in names
+    assert len(names) >= 30
 
 
 def test_library_exports_every_declared_symbol(abi):

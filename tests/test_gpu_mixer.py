@@ -24,7 +24,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import rel_l2
+from conftest import ALT_ORDERS, order_noise as _order_noise, rel_l2, with_order as _with_order
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
@@ -35,20 +35,6 @@ def _cu(lens):
     return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
 
 
-ALT_ORDERS = (1, 2, 3)
-
-
-def _with_order(oracle, order, fn):
-    oracle.set_linear_order(order)
-    try:
-        return fn()
-    finally:
-        oracle.set_linear_order(0)
-
-
-def _order_noise(ref, alts, conv=lambda a: a):
-    """Largest distance between the default-order oracle and the other-order runs."""
-    return max(rel_l2(conv(a), conv(ref)) for a in alts)
 
 
 def test_linear_within_one_ulp_of_exact(gdn, synth):
