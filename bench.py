@@ -61,6 +61,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-mixer", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="run only the chunked-prefill leg and print its result (profiling of that leg)")
+    p.add_argument("--prefill-lens", default=None,
+                   help="comma-separated prompt lengths for the prefill leg (default: config 4)")
     return p.parse_args()
 
 
@@ -70,6 +74,14 @@ def measured_peaks():
         d = json.loads(f.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 tensor-core peak (TFLOP/s): the burst figure of MEASURED_PEAKS.json, else the fallback."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        return float(json.loads(f.read_text())["bf16_tflops"])
+    return 1590.0
 
 
 def profiled_traffic():
@@ -339,7 +351,7 @@ CONFIG4_LENS = [512, 1024, 2048, 3000, 4096, 5000, 6144, 8192]
 def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args, tc_peak):
     """Config 4: 8 prompts packed in one call per layer, zero initial state, 30 layers (fused steps).
     Segments of >= 32 tokens run the tcgen05 chunked kernel."""
-    lens = CONFIG4_LENS
+    lens = [int(x) for x in args.prefill_lens.split(",")] if args.prefill_lens else CONFIG4_LENS
     cu_h = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     N = int(cu_h[-1])
     pool.reserve_tokens(N)
@@ -388,7 +400,8 @@ def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier,
     del g
     ms_step = ms / steps
     flops = N * N_LAYERS * WY_FLOPS_PER_TOKEN_LAYER
-    return {"workload": "config4: prompts %s packed in one call, zero state, 30 fused layer steps" % lens,
+    name = "config4" if lens == CONFIG4_LENS else "custom"
+    return {"workload": "%s: prompts %s packed in one call, zero state, 30 fused layer steps" % (name, lens),
             "tokens": N, "tok_s": world * N / (ms_step / 1e3), "ms_per_step": ms_step,
             "algorithmic_tflops": flops / (ms_step / 1e3) / 1e12, "tensor_peak_tflops": tc_peak,
             "tensor_frac_of_measured": flops / (ms_step / 1e3) / 1e12 / tc_peak,
@@ -413,8 +426,10 @@ def run_ours(args):
 
     cfg = synth.GdnConfig(n_layers=N_LAYERS)
     B = args.batch
-    sweep_bs = [] if (args.no_sweep or world > 1) else [1, 2, 4, 8, 16, 32, 64, 256, 1024, 2048]
+    sweep_bs = [] if (args.no_sweep or world > 1 or args.prefill_only) else [1, 2, 4, 8, 16, 32, 64, 256, 1024, 2048]
     n_slots = max([B] + sweep_bs)
+    if args.prefill_only:
+        n_slots = max(n_slots, len(args.prefill_lens.split(",")) if args.prefill_lens else len(CONFIG4_LENS))
     pool = gdn.StatePool(cfg, n_slots=n_slots, device=local)
     cudart = _cudart()
     cudart.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
@@ -505,6 +520,16 @@ def run_ours(args):
 
     hbm_peak, peak_kind = measured_peaks()
 
+    if args.prefill_only:
+        res = run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args,
+                          measured_tensor_peak())
+        if rank == 0:
+            print(json.dumps({"prefill": res}), flush=True)
+        pool.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
     # ---- headline: B sequences per GPU
     proj_h, out_h = buffers(B)
     g = capture(B, proj_h, out_h)
@@ -571,10 +596,8 @@ def run_ours(args):
     # ---- config-4 prefill on the chunked tensor-core path
     prefill = None
     if not args.no_prefill:
-        tc_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) \
-            if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
         prefill = run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args,
-                              tc_peak)
+                              measured_tensor_peak())
 
     # ---- the whole mixer stack (projections + pre-norm + residual) at the same B
     mixer = None
