@@ -697,6 +697,9 @@ cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStre
         g_num_sms[dev] = sms;
     }
     if (p.n_tokens == 0 || r.n_seq == 0) return cudaSuccess;
+    // one token per sequence on average, and enough sequences that (sequence, k-head) items balance over
+    // the SMs: the fused one-kernel decode step (below that the finer (sequence, v-head) items of K2 win)
+    if (p.n_tokens == p.n_seq && r.wy_min_t == 0 && r.n_seq >= FUSED_MIN_SEQ) return launch_decode_fused(p, r, stream);
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

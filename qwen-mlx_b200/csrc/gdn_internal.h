@@ -78,6 +78,10 @@ constexpr int WY_MIN_T = 32;
 
 cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream);
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
+// Decode-only calls (n_tokens == n_seq) with at least FUSED_MIN_SEQ sequences: prep and recurrence in
+// one persistent kernel (gdn_fused.cu).
+constexpr int FUSED_MIN_SEQ = 64;
+cudaError_t launch_decode_fused(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
 
 // Projections and the decoder pre-norm / residual (gdn_proj.cu).
 struct GemmCtx;

@@ -83,6 +83,23 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("barrier.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier `id` over `nthreads` threads that also ORs `pred` over them: every thread
+// gets the same answer, so a decision taken on it is uniform (non-.aligned form).
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n"
+        " .reg .pred p, q;\n"
+        " setp.ne.u32 p, %1, 0;\n"
+        " barrier.red.or.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n"
+        "}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ float4 lds128(const float* p) {
     float4 v;
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n"

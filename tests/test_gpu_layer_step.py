@@ -88,8 +88,9 @@ def _compare(synth, got_out, ref_out, got_states, ref_states, lens=None):
     assert np.array_equal(gc, rc), "conv state"
 
 
-@pytest.mark.parametrize("B", [1, 8, 33])
+@pytest.mark.parametrize("B", [1, 8, 33, 64, 129])
 def test_decode_batch(H, synth, oracle, B):
+    """B < 64: prep kernel + recurrence kernel; B >= 64: the fused one-kernel decode step."""
     h = H(n_slots=max(B, 16) + 3)
     cfg = h.cfg
     lens = [1] * B
@@ -103,6 +104,32 @@ def test_decode_batch(H, synth, oracle, B):
     assert h.pool.check() == 0
     ref = oracle.layer_step(cfg, h.w, inp["qkv"], inp["z"], inp["ab"], conv0, rec0, cu)
     _compare(synth, out, ref[0], h.states(1, slots), (ref[1], ref[2]))
+
+
+@pytest.mark.parametrize("lens", [[0, 2, 1, 1], [6, 0, 0, 0, 0, 0], [1, 0, 9, 0, 1, 0, 0, 0, 0, 1, 0, 0],
+                                  [1] * 60 + [0, 2, 0, 6, 0, 0, 0, 0], [0] * 40 + [1] * 23 + [41]])
+def test_decode_call_with_uneven_segments(H, synth, oracle, lens):
+    """Calls with n_tokens == n_seq take a decode path (the fused kernel from 64 sequences on); it must
+    also handle empty segments and multi-token segments (past the 4th token their records go through
+    the scratch)."""
+    n_slots = max(16, len(lens) + 3)
+    h = H(n_slots=n_slots)
+    cfg = h.cfg
+    assert sum(lens) == len(lens)
+    cu = _cu(lens)
+    slots = np.array([(5 * i + 3) % n_slots for i in range(len(lens))], np.int32)
+    assert len(set(slots.tolist())) == len(lens)
+    inp = synth.step_inputs(cfg, int(cu[-1]), seed=4, tag=f"uneven{len(lens)}")
+    conv0, rec0 = synth.random_states(cfg, len(lens), seed=4, tag=f"uneven{len(lens)}")
+    h.load_states(1, slots, conv0, rec0)
+    out = h.step(1, inp, slots, cu)
+    assert h.pool.check() == 0
+    ref = oracle.layer_step(cfg, h.w, inp["qkv"], inp["z"], inp["ab"], conv0, rec0, cu)
+    _compare(synth, out, ref[0], h.states(1, slots), (ref[1], ref[2]), lens)
+    for i, n in enumerate(lens):
+        if n == 0:
+            r, c = h.pool.export(int(slots[i]), 1)
+            assert np.array_equal(r, rec0[i]) and np.array_equal(c, conv0[i])
 
 
 def test_ragged_prefill_and_decode_scrambled(H, synth, oracle):
