@@ -29,17 +29,22 @@
 // sequential chains start first.  Inputs are the prep kernel's records; the next
 // chunk's K, V and Q are prefetched with cp.async while the current one computes.
 //
+// Every product but the intra-chunk inverse is an M=128 tcgen05 MMA whose 128 rows are v, d or
+// [Q; K] stacked, so every TMEM lane carries data: G and QK come out of one [Q; K] K^T product, and U, W,
+// D, Q S0^T and P D are formed transposed (U^T = V^T (T beta)^T, W^T = K^T (T beta gamma)^T,
+// D^T = U^T - S0 W^T, (Q S0^T)^T = S0 Q^T, (P D)^T = D^T P^T), each operand being a token-major tile read
+// K-major or MN-major.  The epilogue transposes y once through shared memory for the per-token norm.
+//
 // Shared memory (bytes); bf16 tiles in the layout of gdn_umma.cuh:
-//   R_Q   16K  Q [64 t][128 d]
+//   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity)
 //   R_V   16K  V [64 s][128 v]
-//   R_K   32K  K [64 s][128 d], two buffers (chunk parity)
-//   R_X   64K  S0 hi, lo [128 v][128 d]  -> D hi, D lo, Dd hi, Dd lo [64 s][128 v]
-//   R_T   17K  M, then T = (I + M)^-1 in place (f32, row stride LDT)
+//   R_X   64K  S0 hi, lo [128 v][128 d]  -> D^T hi, D^T lo, Dd^T hi, Dd^T lo [128 v][64 s]
+//   R_T   17K  M, then T = (I + M)^-1 in place (f32, row stride LDT)  -> y [64 t][128 v] bf16 (row stride LDY)
 //   R_N    6K  N_ik = T_ii M_ik for the six blocks below the diagonal (f32 16 x 16)
-//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] -> -W hi, -W lo [64 t][128 d]
+//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] -> -W^T hi, -W^T lo [128 d][64 t]
 //   R_P   16K  (P (.) QK) hi, lo [64 t][64 s]
-// TMEM (512 columns): S [0,128) (M=128 layout), A [128,256), B [256,384), C [384,512)
-// (M=64 accumulators: row t in lane 32*(t/16) + t%16).
+// TMEM (cta_group::1, all 128 lanes): S [0,128) = state [v][d]; GQ [128,192) = [QK; G]; U [192,256) = U^T
+// then D^T; W [256,320) = W^T; QS [320,384) = (Q S0^T)^T; PD [384,448) = (P D)^T.
 #include "gdn_device.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
@@ -51,13 +56,15 @@ constexpr int WC = 64;                 // tokens per chunk
 constexpr int WY_THREADS = 256;
 constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
 constexpr int WY_SORT_CAP = 1024;      // sequences ranked longest-first; more fall back to call order
-constexpr int R_Q = 0, R_V = 16384, R_K = 32768, R_X = 65536, R_T = 131072, R_N = R_T + WC * LDT * 4,
-              R_TB = 155648, R_P = 188416, R_SMALL = 204800;
+constexpr int R_QK = 0, R_V = 65536, R_X = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
+              R_P = 204800, R_SMALL = 221184;
 static_assert(R_N + 6 * 256 * 4 <= R_TB, "prefill shared memory layout");
-constexpr int SMALL_FLOATS = 2 * 64 + 2 * 64 + 3 * 64 + 128 + 128;
-constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + WY_SORT_CAP * 4 + 64;
+constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
+static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
+constexpr int SMALL_FLOATS = 2 * 64 + 2 * 64 + 3 * 2 * 64 + 128;
+constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + WY_SORT_CAP * 4 + 80;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
-constexpr uint32_t TM_S = 0, TM_A = 128, TM_B = 256, TM_C = 384;
+constexpr uint32_t TM_S = 0, TM_GQ = 128, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
 constexpr uint64_t WY_WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t pack_bf2(float lo_half, float hi_half) {
@@ -126,6 +133,28 @@ __device__ __forceinline__ void wy_sync_for_mma() {
     tc_fence_after();
 }
 
+// Inclusive scan of one chunk's log g (log2 units), gamma_t = exp(lg_t) and exp(lg_last - lg_t) (one warp).
+__device__ __forceinline__ void wy_scan(const float* lgr, float* lg, float* gam, float* tail, int lane) {
+    float x0 = lgr[lane], x1 = lgr[32 + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+        const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+        if (lane >= o) { x0 += y0; x1 += y1; }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    const float kLog2e = 1.4426950408889634f;
+    x0 *= kLog2e;
+    x1 *= kLog2e;
+    const float last = __shfl_sync(0xffffffffu, x1, 31);
+    lg[lane] = x0;
+    lg[32 + lane] = x1;
+    gam[lane] = exp2f(x0);
+    gam[32 + lane] = exp2f(x1);
+    tail[lane] = exp2f(last - x0);
+    tail[32 + lane] = exp2f(last - x1);
+}
+
 __device__ __forceinline__ bool wy_qualifies(const RecurArgs& a, int seq, int& t0, int& T, int& slot) {
     t0 = __ldg(a.cu_seqlens + seq);
     T = __ldg(a.cu_seqlens + seq + 1) - t0;
@@ -137,27 +166,32 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     extern __shared__ __align__(1024) uint8_t smem[];
     float* s_beta = reinterpret_cast<float*>(smem + R_SMALL);  // [2][64] (chunk parity)
     float* s_lgr = s_beta + 2 * WC;                               // [2][64] log g per token
-    float* s_lg = s_lgr + 2 * WC;                                 // [64] cumulative, log2 units
-    float* s_gam = s_lg + WC;                                     // exp(lg_t)
-    float* s_tail = s_gam + WC;                                   // exp(lg_last - lg_t)
-    float* s_nw = s_tail + WC;                                    // norm_w [128]
-    float* s_ss = s_nw + DV;                                      // [2][64] sum of squares halves
-    int* s_order = reinterpret_cast<int*>(s_ss + 2 * WC);         // sequences, longest first
-    uint64_t* bar = reinterpret_cast<uint64_t*>(s_order + WY_SORT_CAP);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+    float* s_lg = s_lgr + 2 * WC;                                 // [2][64] cumulative, log2 units
+    float* s_gam = s_lg + 2 * WC;                                 // [2][64] exp(lg_t)
+    float* s_tail = s_gam + 2 * WC;                               // [2][64] exp(lg_last - lg_t)
+    float* s_nw = s_tail + 2 * WC;                                // norm_w [128]
+    int* s_order = reinterpret_cast<int*>(s_nw + DV);             // sequences, longest first
+    uint64_t* bar = reinterpret_cast<uint64_t*>(s_order + WY_SORT_CAP);   // MMA batches waited in order
+    uint64_t* bar_qs = bar + 1;                                   // (Q S0^T)^T, issued early
+    uint64_t* bar_s = bar + 2;                                    // state update, waited when S is next used
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 3);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     int* s_cnt = const_cast<int*>(s_ticket + 1);
     float* fT = reinterpret_cast<float*>(smem + R_T);
     float* fN = reinterpret_cast<float*>(smem + R_N);
+    uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, hh = warp >> 2;   // TMEM lane quarter, column half
+    const int L = quarter * 32 + lane;              // TMEM lane = MMA row owned by this thread
     const uint32_t sb = smem_u32(smem);
     const int ratio = a.hv / a.hk;
 
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(bar_qs, 1);
+        mbar_init(bar_s, 1);
         *s_abort = 0;
         *s_cnt = 0;
         fence_mbar_init();
@@ -169,7 +203,7 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    uint32_t ph = 0;
+    uint32_t ph = 0, ph_qs = 0, ph_s = 0;
     pdl_wait();
 
     // ---- the qualifying sequences, ranked longest first (ties: call order)
@@ -205,12 +239,6 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     const bool ranked = m_seq <= WY_SORT_CAP;
     const int n_work = (ranked ? m_seq : a.n_seq) * a.hv;
 
-    // M=64 accumulator row owned by this thread (lanes 0..15 of each warp)
-    const bool rt = lane < 16;
-    const int trow = quarter * 16 + (lane & 15);
-    // M=128 row (state row v) owned by this thread
-    const int vrow = quarter * 32 + lane;
-
     for (;;) {
         if (tid == 0) *s_ticket = atomicAdd(a.wy_counter, 1);
         __syncthreads();
@@ -231,15 +259,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         // chunk 0's inputs
         {
             const int nv = T < WC ? T : WC;
-            load_field(sb + R_K, recb, 256, nv, tid);
-            load_field(sb + R_Q, recb, 0, nv, tid);
+            load_field(sb + R_QK, recb, 0, nv, tid);
+            load_field(sb + R_QK + 16384, recb, 256, nv, tid);
             load_field(sb + R_V, recb, 512, nv, tid);
             load_gates(s_beta, s_lgr, recb, nv, tid);
             cp_async_commit();
         }
         // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
         {
-            const float* src = st_in + (size_t)vrow * DK + hh * 64;
+            const float* src = st_in + (size_t)L * DK + hh * 64;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 float v[16];
@@ -260,52 +288,41 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             const bool has_next = c + 1 < n_chunks;
             const uint8_t* rec1 = rec0 + (size_t)WC * REC_BYTES;
             const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
-            const uint32_t sK = sb + R_K + kb * 16384;
+            const uint32_t sQ = sb + R_QK + kb * 32768;    // Q [64][128], then K [64][128] at +16384
+            const uint32_t sK = sQ + 16384;
+            const float* lgc = s_lg + kb * WC;
+            const float* gamc = s_gam + kb * WC;
+            const float* tailc = s_tail + kb * WC;
 
-            // ---- phase A: this chunk's inputs landed; next chunk's K and gates in flight
+            // ---- phase A: this chunk's inputs landed; next chunk's Q, K and gates in flight
             cp_async_wait_all();
+            if (c > 0) {
+                // the previous chunk's state update still reads the K buffer refilled below
+                if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                ph_s ^= 1u;
+                tc_fence_after();
+            }
             __syncthreads();
             if (*s_abort) break;
             if (has_next) {
-                load_field(sb + R_K + (kb ^ 1) * 16384, rec1, 256, nv1, tid);
+                load_field(sb + R_QK + (kb ^ 1) * 32768, rec1, 0, nv1, tid);
+                load_field(sb + R_QK + (kb ^ 1) * 32768 + 16384, rec1, 256, nv1, tid);
                 load_gates(s_beta + (kb ^ 1) * WC, s_lgr + (kb ^ 1) * WC, rec1, nv1, tid);
             }
             cp_async_commit();
-            if (warp == 0) {
-                // inclusive scan of log g over the chunk, in log2 units
-                float x0 = s_lgr[kb * WC + lane], x1 = s_lgr[kb * WC + 32 + lane];
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
-                    const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
-                    if (lane >= o) { x0 += y0; x1 += y1; }
-                }
-                x1 += __shfl_sync(0xffffffffu, x0, 31);
-                const float kLog2e = 1.4426950408889634f;
-                x0 *= kLog2e;
-                x1 *= kLog2e;
-                const float last = __shfl_sync(0xffffffffu, x1, 31);
-                s_lg[lane] = x0;
-                s_lg[32 + lane] = x1;
-                s_gam[lane] = exp2f(x0);
-                s_gam[32 + lane] = exp2f(x1);
-                s_tail[lane] = exp2f(last - x0);
-                s_tail[32 + lane] = exp2f(last - x1);
-            }
+            if (c == 0 && warp == 0) wy_scan(s_lgr, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
             wy_sync_for_mma();
 
-            // ---- phase B: G = K K^T -> A[0,64), QK = Q K^T -> A[64,128)
+            // ---- phase B: [QK; G] = [Q; K] K^T -> GQ (rows 0..63 QK, rows 64..127 G)
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(64, 64);
-                for (int ks = 0; ks < 8; ++ks)
-                    umma_bf16(tmem + TM_A, umma_desc(sK, 128, ks), umma_desc(sK, 128, ks), id, ks > 0);
-                for (int ks = 0; ks < 8; ++ks)
-                    umma_bf16(tmem + TM_A + 64, umma_desc(sb + R_Q, 128, ks), umma_desc(sK, 128, ks), id, ks > 0);
+                const uint32_t id = umma_idesc_bf16(128, 64);
+                const uint64_t da = umma_desc(sQ, 128, 0), db = umma_desc(sK, 128, 0);
+                for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem + TM_GQ, da + ks * KSTEP_K, db + ks * KSTEP_K, id, ks > 0);
                 umma_commit(bar);
             }
             // ---- phase C2 (overlaps B): S0 hi/lo tiles [v][d]; S *= gamma_last in place
             {
-                const float g_last = s_gam[WC - 1];
+                const float g_last = gamc[WC - 1];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     float sv[16];
@@ -314,8 +331,8 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                     for (int u = 0; u < 2; ++u) {
                         uint4 hi, lo;
                         split8(sv + 8 * u, hi, lo);
-                        st_tile<128>(smem + R_X, vrow, hh * 8 + j * 2 + u, hi);
-                        st_tile<128>(smem + R_X + 32768, vrow, hh * 8 + j * 2 + u, lo);
+                        st_tile<128>(smem + R_X, L, hh * 8 + j * 2 + u, hi);
+                        st_tile<128>(smem + R_X + 32768, L, hh * 8 + j * 2 + u, lo);
                     }
 #pragma unroll
                     for (int e = 0; e < 16; ++e) sv[e] *= g_last;
@@ -323,112 +340,143 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                 }
                 tmem_st_wait();
             }
+            wy_sync_for_mma();
+            // (Q S0^T)^T = S0 Q^T -> QS, off the critical path (read in H)
+            if (tid == 0) {
+                const uint32_t idq = umma_idesc_bf16(128, 64);
+                const uint64_t dq = umma_desc(sQ, 128, 0);
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t ds = umma_desc(sb + R_X + h * 32768, 128, 0);
+                    for (int ks = 0; ks < 8; ++ks)
+                        umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * KSTEP_K, idq, (h | ks) != 0);
+                }
+                umma_commit(bar_qs);
+            }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
-            // ---- phase C1: M (f32 rows) and P (.) QK (hi/lo tiles) of row trow, columns [32 hh, +32)
+            // ---- phase C1: lanes 0..63 hold QK row t -> P (.) QK hi/lo tiles; lanes 64..127 hold G row t -> M (f32)
             {
-                const float lg_t = s_lg[trow];
-                const float b_t = s_beta[kb * WC + trow];
+                const bool is_g = L >= WC;
+                const int t = L & (WC - 1);
+                const float lg_t = lgc[t];
+                const float b_t = s_beta[kb * WC + t];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    float gv[16], qv[16];
-                    tmem_ld16(tmem + lane_base + TM_A + hh * 32 + j * 16, gv);
-                    tmem_ld16(tmem + lane_base + TM_A + 64 + hh * 32 + j * 16, qv);
-                    if (rt) {
-                        float mv[16], pv[16];
+                    float x[16];
+                    tmem_ld16(tmem + lane_base + TM_GQ + hh * 32 + j * 16, x);
+                    if (is_g) {
+                        float mv[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) {
                             const int s = hh * 32 + j * 16 + e;
-                            const float dec = exp2f(lg_t - s_lg[s]);
-                            mv[e] = s < trow ? b_t * dec * gv[e] : 0.f;
-                            pv[e] = s <= trow ? dec * qv[e] : 0.f;
+                            mv[e] = s < t ? b_t * exp2f(lg_t - lgc[s]) * x[e] : 0.f;
                         }
-                        float* mrow = fT + trow * LDT + hh * 32 + j * 16;
+                        float* mrow = fT + t * LDT + hh * 32 + j * 16;
 #pragma unroll
                         for (int e = 0; e < 16; e += 4)
                             *reinterpret_cast<float4*>(mrow + e) = make_float4(mv[e], mv[e + 1], mv[e + 2], mv[e + 3]);
+                    } else {
+                        float pv[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const int s = hh * 32 + j * 16 + e;
+                            pv[e] = s <= t ? exp2f(lg_t - lgc[s]) * x[e] : 0.f;
+                        }
 #pragma unroll
                         for (int u = 0; u < 2; ++u) {
                             uint4 hi, lo;
                             split8(pv + 8 * u, hi, lo);
-                            st_tile<64>(smem + R_P, trow, hh * 4 + j * 2 + u, hi);
-                            st_tile<64>(smem + R_P + 8192, trow, hh * 4 + j * 2 + u, lo);
+                            st_tile<64>(smem + R_P, t, hh * 4 + j * 2 + u, hi);
+                            st_tile<64>(smem + R_P + 8192, t, hh * 4 + j * 2 + u, lo);
                         }
                     }
                 }
             }
-            __syncthreads();
 
-            // ---- phase C3: T = (I + M)^-1 by 16 x 16 blocks, in place over M
-            // diagonal blocks by forward substitution: lane (block 2 warp + lane/16, column s)
-            if (warp < 2) {
-                const int b = 2 * warp + (lane >> 4), s = lane & 15;
-                float* Mb = fT + 16 * b * LDT + 16 * b;
-                float col[16];
+            // ---- phase C3: T = (I + M)^-1 by 16 x 16 blocks, in place over M.  The warps that wrote M (2, 3, 6,
+            // 7) meet first; warps 2 and 3 invert the diagonal blocks by forward substitution (lane: block
+            // 2 (warp - 2) + lane/16, column s) while the P writers finish.
+            if (quarter >= 2) {
+                named_bar_sync(1, 128);
+                if (warp < 4) {
+                    const int b = 2 * (warp - 2) + (lane >> 4), s = lane & 15;
+                    float* Mb = fT + 16 * b * LDT + 16 * b;
+                    float col[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) col[j] = j == s ? 1.f : 0.f;
+                    for (int j = 0; j < 16; ++j) col[j] = j == s ? 1.f : 0.f;
 #pragma unroll
-                for (int t = 1; t < 16; ++t) {
-                    float a0 = 0.f, a1 = 0.f;
+                    for (int t = 1; t < 16; ++t) {
+                        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-                    for (int j4 = 0; j4 < t; j4 += 4) {
-                        const float4 mv = *reinterpret_cast<const float4*>(Mb + t * LDT + j4);
-                        a0 = fmaf(mv.x, col[j4], a0);
-                        a1 = fmaf(mv.y, col[j4 + 1], a1);
-                        a0 = fmaf(mv.z, col[j4 + 2], a0);
-                        a1 = fmaf(mv.w, col[j4 + 3], a1);
+                        for (int j4 = 0; j4 < t; j4 += 4) {
+                            const float4 mv = *reinterpret_cast<const float4*>(Mb + t * LDT + j4);
+                            a0 = fmaf(mv.x, col[j4], a0);
+                            a1 = fmaf(mv.y, col[j4 + 1], a1);
+                            a0 = fmaf(mv.z, col[j4 + 2], a0);
+                            a1 = fmaf(mv.w, col[j4 + 3], a1);
+                        }
+                        if (t > s) col[t] = -(a0 + a1);
                     }
-                    if (t > s) col[t] = -(a0 + a1);
-                }
-                __syncwarp();
+                    __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) Mb[j * LDT + s] = col[j];
+                    for (int j = 0; j < 16; ++j) Mb[j * LDT + s] = col[j];
+                }
             }
             __syncthreads();
-            {
-                const int r = tid >> 4, cc = tid & 15;
-                // N_ik = T_ii M_ik for the six blocks below the diagonal (pair index i(i-1)/2 + k)
+            // N_ik = T_ii M_ik for the six blocks below the diagonal (pair index i(i-1)/2 + k); each task
+            // is 4 consecutive outputs of one row: 384 tasks
+            for (int task = tid; task < 6 * 64; task += WY_THREADS) {
+                const int p = task >> 6, rem = task & 63;
+                const int r = rem >> 2, c4 = (rem & 3) * 4;
+                const int i = p < 1 ? 1 : (p < 3 ? 2 : 3);
+                const int kk = p - i * (i - 1) / 2;
+                const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
+                const float* Mk = fT + 16 * i * LDT + 16 * kk + c4;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int p = 0; p < 6; ++p) {
-                    const int i = p < 1 ? 1 : (p < 3 ? 2 : 3);
-                    const int kk = p - i * (i - 1) / 2;
-                    const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
-                    const float* Mk = fT + 16 * i * LDT + 16 * kk + cc;
-                    float acc = 0.f;
+                for (int m4 = 0; m4 < 16; m4 += 4) {
+                    const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
+                    const float tv[4] = {tr.x, tr.y, tr.z, tr.w};
 #pragma unroll
-                    for (int m4 = 0; m4 < 16; m4 += 4) {
-                        const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
-                        acc = fmaf(tr.x, Mk[(m4 + 0) * LDT], acc);
-                        acc = fmaf(tr.y, Mk[(m4 + 1) * LDT], acc);
-                        acc = fmaf(tr.z, Mk[(m4 + 2) * LDT], acc);
-                        acc = fmaf(tr.w, Mk[(m4 + 3) * LDT], acc);
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 mr = *reinterpret_cast<const float4*>(Mk + (m4 + q) * LDT);
+                        acc.x = fmaf(tv[q], mr.x, acc.x);
+                        acc.y = fmaf(tv[q], mr.y, acc.y);
+                        acc.z = fmaf(tv[q], mr.z, acc.z);
+                        acc.w = fmaf(tv[q], mr.w, acc.w);
                     }
-                    fN[p * 256 + r * 16 + cc] = acc;
                 }
-                __syncthreads();
-                // block rows 1..3: T_ij = -sum_{k=j}^{i-1} N_ik T_kj
+                *reinterpret_cast<float4*>(fN + p * 256 + r * 16 + c4) = acc;
+            }
+            __syncthreads();
+            // block rows 1..3: T_ij = -sum_{k=j}^{i-1} N_ik T_kj (4 outputs per task)
 #pragma unroll
-                for (int i = 1; i < 4; ++i) {
+            for (int i = 1; i < 4; ++i) {
+                if (tid < 64 * i) {
+                    const int j = tid >> 6, rem = tid & 63;
+                    const int r = rem >> 2, c4 = (rem & 3) * 4;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int kk = j; kk < i; ++kk) {
+                        const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
+                        const float* Tc = fT + 16 * kk * LDT + 16 * j + c4;
 #pragma unroll
-                    for (int j = 0; j < i; ++j) {
-                        float acc = 0.f;
+                        for (int m4 = 0; m4 < 16; m4 += 4) {
+                            const float4 nr = *reinterpret_cast<const float4*>(Nr + m4);
+                            const float nv4[4] = {nr.x, nr.y, nr.z, nr.w};
 #pragma unroll
-                        for (int kk = j; kk < i; ++kk) {
-                            const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
-                            const float* Tc = fT + 16 * kk * LDT + 16 * j + cc;
-#pragma unroll
-                            for (int m4 = 0; m4 < 16; m4 += 4) {
-                                const float4 nr = *reinterpret_cast<const float4*>(Nr + m4);
-                                acc = fmaf(nr.x, Tc[(m4 + 0) * LDT], acc);
-                                acc = fmaf(nr.y, Tc[(m4 + 1) * LDT], acc);
-                                acc = fmaf(nr.z, Tc[(m4 + 2) * LDT], acc);
-                                acc = fmaf(nr.w, Tc[(m4 + 3) * LDT], acc);
+                            for (int q = 0; q < 4; ++q) {
+                                const float4 tr = *reinterpret_cast<const float4*>(Tc + (m4 + q) * LDT);
+                                acc.x = fmaf(nv4[q], tr.x, acc.x);
+                                acc.y = fmaf(nv4[q], tr.y, acc.y);
+                                acc.z = fmaf(nv4[q], tr.z, acc.z);
+                                acc.w = fmaf(nv4[q], tr.w, acc.w);
                             }
                         }
-                        fT[(16 * i + r) * LDT + 16 * j + cc] = -acc;
                     }
-                    __syncthreads();
+                    *reinterpret_cast<float4*>(fT + (16 * i + r) * LDT + 16 * j + c4) =
+                        make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
                 }
+                __syncthreads();
             }
 
             // ---- phase C4: (T beta) and (T beta gamma) hi/lo tiles; thread (row t, columns [16 cq, +16))
@@ -446,7 +494,7 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                     const int s = 16 * cq + e;
                     const float x = s <= t ? tb[e] * s_beta[kb * WC + s] : 0.f;
                     tb[e] = x;
-                    tg[e] = x * s_gam[s];
+                    tg[e] = x * gamc[s];
                 }
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
@@ -461,145 +509,160 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             }
             wy_sync_for_mma();
 
-            // ---- phase D: U = (T beta) V -> B;  W = (T beta gamma) K -> C   (V, K read MN-major)
+            // ---- phase D: U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major)
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(64, 128, false, true);
-                for (int h = 0; h < 2; ++h)
+                const uint32_t id = umma_idesc_bf16(128, 64, true, false);
+                const uint64_t dv = umma_desc_mn(sb + R_V, 128, 0), dk = umma_desc_mn(sK, 128, 0);
+                constexpr uint64_t kmn = umma_kstep_mn(128);
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_B, umma_desc(sb + R_TB + h * 8192, 64, ks), umma_desc_mn(sb + R_V, 128, ks),
-                                  id, (h | ks) != 0);
-                for (int h = 0; h < 2; ++h)
+                        umma_bf16(tmem + TM_U, dv + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                }
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_C, umma_desc(sb + R_TB + 16384 + h * 8192, 64, ks), umma_desc_mn(sK, 128, ks),
-                                  id, (h | ks) != 0);
+                        umma_bf16(tmem + TM_W, dk + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                }
                 umma_commit(bar);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
             if (has_next) load_field(sb + R_V, rec1, 512, nv1, tid);   // V is free
             cp_async_commit();
 
-            // ---- phase E: -W hi/lo tiles [t][d]; then D = U - W S0^T onto B, Q S0^T -> C
+            // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U, (Q S0^T)^T = S0 Q^T -> QS
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 2; ++j) {
                 float wv[16];
-                tmem_ld16(tmem + lane_base + TM_C + hh * 64 + j * 16, wv);
-                if (rt) {
+                tmem_ld16(tmem + lane_base + TM_W + hh * 32 + j * 16, wv);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) wv[e] = -wv[e];
+                for (int e = 0; e < 16; ++e) wv[e] = -wv[e];
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        uint4 hi, lo;
-                        split8(wv + 8 * u, hi, lo);
-                        st_tile<128>(smem + R_TB, trow, hh * 8 + j * 2 + u, hi);
-                        st_tile<128>(smem + R_TB + 16384, trow, hh * 8 + j * 2 + u, lo);
-                    }
+                for (int u = 0; u < 2; ++u) {
+                    uint4 hi, lo;
+                    split8(wv + 8 * u, hi, lo);
+                    st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, hi);
+                    st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
                 }
             }
             wy_sync_for_mma();
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(64, 128);
-                const uint32_t aw[3] = {R_TB, R_TB, R_TB + 16384}, bs[3] = {R_X, R_X + 32768, R_X};
-                for (int p = 0; p < 3; ++p)
-                    for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_B, umma_desc(sb + aw[p], 128, ks), umma_desc(sb + bs[p], 128, ks), id, 1u);
-                for (int h = 0; h < 2; ++h)
-                    for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_C, umma_desc(sb + R_Q, 128, ks), umma_desc(sb + R_X + h * 32768, 128, ks), id,
-                                  (h | ks) != 0);
+                const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
+                const uint32_t as0[3] = {R_X, R_X + 32768, R_X}, bw[3] = {R_TB, R_TB, R_TB + 16384};
+                constexpr uint64_t kmn = umma_kstep_mn(64);
+                for (int p = 0; p < 3; ++p) {
+                    const uint64_t da = umma_desc(sb + as0[p], 128, 0), db = umma_desc_mn(sb + bw[p], 64, 0);
+                    for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem + TM_U, da + ks * KSTEP_K, db + ks * kmn, idd, 1u);
+                }
                 umma_commit(bar);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            if (has_next) load_field(sb + R_Q, rec1, 0, nv1, tid);     // Q is free
-            cp_async_commit();
+            if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
-            // ---- phase F: D and Dd = diag(exp(lg_last - lg_s)) D as hi/lo tiles [s][v]
-            {
-                const float tail = s_tail[trow];
+            // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float dv[16];
-                    tmem_ld16(tmem + lane_base + TM_B + hh * 64 + j * 16, dv);
-                    if (rt) {
+            for (int j = 0; j < 2; ++j) {
+                float dv[16];
+                tmem_ld16(tmem + lane_base + TM_U + hh * 32 + j * 16, dv);
 #pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            uint4 hi, lo;
-                            split8(dv + 8 * u, hi, lo);
-                            st_tile<128>(smem + R_X, trow, hh * 8 + j * 2 + u, hi);
-                            st_tile<128>(smem + R_X + 16384, trow, hh * 8 + j * 2 + u, lo);
-                        }
+                for (int u = 0; u < 2; ++u) {
+                    uint4 hi, lo;
+                    split8(dv + 8 * u, hi, lo);
+                    st_tile<64>(smem + R_X, L, hh * 4 + j * 2 + u, hi);
+                    st_tile<64>(smem + R_X + 16384, L, hh * 4 + j * 2 + u, lo);
+                }
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) dv[e] *= tail;
+                for (int e = 0; e < 16; ++e) dv[e] *= tailc[hh * 32 + j * 16 + e];
 #pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            uint4 hi, lo;
-                            split8(dv + 8 * u, hi, lo);
-                            st_tile<128>(smem + R_X + 32768, trow, hh * 8 + j * 2 + u, hi);
-                            st_tile<128>(smem + R_X + 49152, trow, hh * 8 + j * 2 + u, lo);
-                        }
-                    }
+                for (int u = 0; u < 2; ++u) {
+                    uint4 hi, lo;
+                    split8(dv + 8 * u, hi, lo);
+                    st_tile<64>(smem + R_X + 32768, L, hh * 4 + j * 2 + u, hi);
+                    st_tile<64>(smem + R_X + 49152, L, hh * 4 + j * 2 + u, lo);
                 }
             }
             wy_sync_for_mma();
-            // ---- phase G: (P (.) QK) D -> A;  S += Dd^T K -> S   (D, Dd, K read MN-major)
+            // ---- phase G: (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (K read MN-major; waited
+            // when the state or the K buffer is next touched)
             if (tid == 0) {
-                const uint32_t id64 = umma_idesc_bf16(64, 128, false, true);
-                const uint32_t ap[3] = {R_P, R_P, R_P + 8192}, bd[3] = {R_X, R_X + 16384, R_X};
-                for (int p = 0; p < 3; ++p)
+                const uint32_t idp = umma_idesc_bf16(128, 64);
+                const uint32_t ad[3] = {R_X, R_X + 16384, R_X}, bp[3] = {R_P, R_P, R_P + 8192};
+                for (int p = 0; p < 3; ++p) {
+                    const uint64_t da = umma_desc(sb + ad[p], 64, 0), db = umma_desc(sb + bp[p], 64, 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_A, umma_desc(sb + ap[p], 64, ks), umma_desc_mn(sb + bd[p], 128, ks), id64,
-                                  (p | ks) != 0);
-                const uint32_t id128 = umma_idesc_bf16(128, 128, true, true);
-                for (int h = 0; h < 2; ++h)
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_S, umma_desc_mn(sb + R_X + 32768 + h * 16384, 128, ks),
-                                  umma_desc_mn(sK, 128, ks), id128, 1u);
+                        umma_bf16(tmem + TM_PD, da + ks * KSTEP_K, db + ks * KSTEP_K, idp, (p | ks) != 0);
+                }
                 umma_commit(bar);
+                const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
+                const uint64_t dk = umma_desc_mn(sK, 128, 0);
+                constexpr uint64_t kmn = umma_kstep_mn(128);
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t dd = umma_desc(sb + R_X + 32768 + h * 16384, 64, 0);
+                    for (int ks = 0; ks < 4; ++ks) umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * kmn, ids, 1u);
+                }
+                umma_commit(bar_s);
             }
-            // silu(z) of this row's 64 columns, loaded while the MMAs run
-            const bool valid = rt && trow < nv;
-            uint4 zr[8];
+            // silu(z) of the epilogue's row and quarter, loaded while the MMAs run
+            const int yt = tid >> 2, yq = tid & 3;
+            const bool valid = yt < nv;
+            uint4 zr[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) zr[i] = make_uint4(0, 0, 0, 0);
+            for (int i = 0; i < 4; ++i) zr[i] = make_uint4(0, 0, 0, 0);
             if (valid) {
-                const uint8_t* zp = rec0 + (size_t)trow * REC_BYTES + 768 + hh * 128;
+                const uint8_t* zp = rec0 + (size_t)yt * REC_BYTES + 768 + yq * 64;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
+                for (int i = 0; i < 4; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
-            // ---- phase H: y = gamma_t Q S0^T + (P (.) QK) D, rounded to bf16; gated RMSNorm
+            // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
+            // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float qs[16], pd[16];
+                tmem_ld16(tmem + lane_base + TM_QS + hh * 32 + j * 16, qs);
+                tmem_ld16(tmem + lane_base + TM_PD + hh * 32 + j * 16, pd);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int t = hh * 32 + j * 16 + e;
+                    s_yt[t * LDY + L] = f2bf(gamc[t] * qs[e] + pd[e]);
+                }
+            }
+            cp_async_wait_group1();   // the next chunk's Q, K and gates (only its V may still be in flight)
+            __syncthreads();
+            if (has_next && warp == 7)
+                wy_scan(s_lgr + (kb ^ 1) * WC, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC, s_tail + (kb ^ 1) * WC, lane);
             {
-                const float gam = s_gam[trow];
-                float y[64];
+                const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
+                uint32_t yw[16];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 q = yr[i];
+                    yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
+                }
                 float ss = 0.f;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float qs[16], pd[16];
-                    tmem_ld16(tmem + lane_base + TM_C + hh * 64 + j * 16, qs);
-                    tmem_ld16(tmem + lane_base + TM_A + hh * 64 + j * 16, pd);
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const float yy = rbf(gam * qs[e] + pd[e]);
-                        y[j * 16 + e] = yy;
-                        ss += yy * yy;
-                    }
+                for (int i = 0; i < 16; ++i) {
+                    const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
+                    ss += y0 * y0 + y1 * y1;
                 }
-                if (rt) s_ss[hh * WC + trow] = ss;
-                __syncthreads();
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                 if (valid) {
-                    const float tot = s_ss[trow] + s_ss[WC + trow];
-                    const float nrm = 1.0f / sqrtf(tot / (float)DV + a.eps);
-                    uint16_t* dst = a.out + (long long)(t0 + c * WC + trow) * a.ld_out + (long long)hv * DV + hh * 64;
+                    const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
+                    uint16_t* dst = a.out + (long long)(t0 + c * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
                     const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+                    const float* nw = s_nw + yq * 32;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 4; ++i) {
                         const uint32_t zw[4] = {zr[i].x, zr[i].y, zr[i].z, zr[i].w};
                         uint32_t o[4];
 #pragma unroll
                         for (int e2 = 0; e2 < 4; ++e2) {
                             const int col = i * 8 + 2 * e2;
-                            const float yn0 = rbf(rbf(y[col] * nrm) * s_nw[hh * 64 + col]);
-                            const float yn1 = rbf(rbf(y[col + 1] * nrm) * s_nw[hh * 64 + col + 1]);
+                            const uint32_t yv = yw[col >> 1];
+                            const float yn0 = rbf(rbf(__uint_as_float(yv << 16) * nrm) * nw[col]);
+                            const float yn1 = rbf(rbf(__uint_as_float(yv & 0xFFFF0000u) * nrm) * nw[col + 1]);
                             const float z0 = __uint_as_float(zw[e2] << 16), z1 = __uint_as_float(zw[e2] & 0xFFFF0000u);
                             o[e2] = (uint32_t)f2bf(z0 * yn0) | ((uint32_t)f2bf(z1 * yn1) << 16);
                         }
@@ -620,10 +683,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             tc_fence_after();
         }
         cp_async_wait_all();
+        if (n_chunks > 0 && !*s_abort) {
+            if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            ph_s ^= 1u;
+            tc_fence_after();
+        }
 
         // ---- state back to the pool (row v, columns [64 half, +64))
         {
-            float* dst = st + (size_t)vrow * DK + hh * 64;
+            float* dst = st + (size_t)L * DK + hh * 64;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 float v[16];

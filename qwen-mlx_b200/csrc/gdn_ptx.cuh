@@ -118,5 +118,7 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+// Wait until at most one of this thread's committed cp.async groups is still pending.
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 }  // namespace gdn

@@ -49,6 +49,12 @@ __device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, int COLS, int k
     return umma_desc_raw(saddr + (uint32_t)kstep * 2u * lbo, lbo, 128u);
 }
 
+// One k-step of the descriptors above, in units of their 16-byte start-address field: adding
+// kstep * KSTEP_K (K-major) or kstep * umma_kstep_mn(COLS) (MN-major) to a kstep-0 descriptor gives
+// the kstep descriptor (shared-memory addresses stay below 2^18, so the field cannot carry over).
+constexpr uint64_t KSTEP_K = 256u >> 4;
+__host__ __device__ constexpr uint64_t umma_kstep_mn(int COLS) { return (uint64_t)(2 * COLS * 16) >> 4; }
+
 // kind::f16 instruction descriptor: A = B = bf16, D = f32, M x N; a_mn / b_mn select an
 // MN-major operand (bits 15 / 16), K-major otherwise.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn = false, bool b_mn = false) {
