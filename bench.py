@@ -62,6 +62,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-mixer", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
+    p.add_argument("--no-mixed", action="store_true")
     p.add_argument("--prefill-only", action="store_true",
                    help="run only the chunked-prefill leg and print its result (profiling of that leg)")
     p.add_argument("--prefill-lens", default=None,
@@ -347,6 +348,82 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
 WY_FLOPS_PER_TOKEN_LAYER = 32 * (6 * 128 * 128 + 2 * 64 * (3 * 128 + 2 * 128))
 assert WY_FLOPS_PER_TOKEN_LAYER == 5_767_168
 CONFIG4_LENS = [512, 1024, 2048, 3000, 4096, 5000, 6144, 8192]
+TOKEN_IO_BYTES = 8192 * 2 + 4096 * 2 + 64 * 2 + 4096 * 2    # qkv, z, a/b in; gated output out (per token, layer)
+STATE_BYTES_PER_SEQ_LAYER = BYTES_PER_SEQ_LAYER - TOKEN_IO_BYTES
+
+
+def run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, world, args, hbm_peak):
+    """Config 3 (ragged continuous batching): a 256-slot pool with 64 live sequences holding prior state;
+    every step a seeded 50-100% subset is active and ~10% of the active ones carry a prefill chunk of
+    U[1, 512] tokens, all packed in one call per layer (30 fused layer steps).  Token counts change every
+    step, so the steps are launched eagerly; the tables are uploaded inside the timed region."""
+    rng = np.random.default_rng(1234)
+    n_slots, n_live, n_steps, warm = 256, 64, 12, 3
+    slots_live = rng.permutation(n_slots)[:n_live].astype(np.int32)
+    plans = []
+    for _ in range(n_steps):
+        n_act = int(rng.integers(n_live // 2, n_live + 1))
+        act = rng.permutation(n_live)[:n_act]
+        n_pref = max(1, int(round(0.1 * n_act)))
+        lens = np.ones(n_act, np.int64)
+        lens[:n_pref] = rng.integers(1, 513, n_pref)
+        order = rng.permutation(n_act)
+        act, lens = act[order], lens[order]
+        plans.append((slots_live[act], np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)))
+    n_max = max(int(c[-1]) for _, c in plans)
+    mpool = gdn.StatePool(cfg, n_slots=n_slots, device=dev.index)
+    mpool.reserve_tokens(n_max)
+    proj = torch.randn((N_LAYERS, n_max, PROJ_LD), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty((N_LAYERS, n_max, cfg.z_dim), dtype=torch.bfloat16, device=dev)
+    tab_h = torch.empty(2 * (n_live + 1), dtype=torch.int32).pin_memory()
+    tab_d = torch.empty(2 * (n_live + 1), dtype=torch.int32, device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    ios = [abi.GdnStepIOC(proj[l].data_ptr(), PROJ_LD, proj[l].data_ptr() + 8192 * 2, PROJ_LD,
+                          proj[l].data_ptr() + (8192 + 4096) * 2, PROJ_LD, out[l].data_ptr(), cfg.z_dim)
+           for l in range(N_LAYERS)]
+
+    def step(k):
+        sl, cu = plans[k]
+        n = len(sl)
+        tab_h[:n] = torch.from_numpy(sl)
+        tab_h[n_live + 1:n_live + 2 + n] = torch.from_numpy(cu)
+        with torch.cuda.stream(stream):
+            tab_d.copy_(tab_h, non_blocking=True)
+            for l in range(N_LAYERS):
+                rc = lib.gdn_layer_step(mpool.h, l, C.byref(lws[l].c), C.byref(ios[l]), C.c_void_p(tab_d.data_ptr()),
+                                        C.c_void_p(tab_d.data_ptr() + (n_live + 1) * 4), n, int(cu[-1]), sp)
+                if rc:
+                    abi.check(rc, "gdn_layer_step")
+        stream.synchronize()   # the pinned table buffer is reused by the next step
+
+    for k in range(warm):
+        step(k)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(warm, n_steps):
+        step(k)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert mpool.check() == 0
+    timed = plans[warm:]
+    tokens = sum(int(c[-1]) for _, c in timed)
+    seqs = sum(len(sl) for sl, _ in timed)
+    step_bytes = sum(N_LAYERS * (len(sl) * STATE_BYTES_PER_SEQ_LAYER + int(c[-1]) * TOKEN_IO_BYTES
+                                 + BYTES_PER_LAUNCH_CONST) for sl, c in timed)
+    mpool.close()
+    del proj, out
+    return {"workload": "config3: 256-slot pool, 64 live, 50-100% active per step, ~10% of them with a prefill "
+                        "chunk U[1,512], 30 fused layer steps, eager launches",
+            "steps": len(timed), "tokens": tokens, "sequence_steps": seqs, "tok_s": world * tokens / (ms / 1e3),
+            "ms_per_step": ms / len(timed), "hbm_frac_of_measured": step_bytes / (ms / 1e3) / 1e9 / hbm_peak}
 
 
 def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args, tc_peak):
@@ -637,6 +714,11 @@ def run_ours(args):
         prefill = run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args,
                               measured_tensor_peak())
 
+    # ---- config-3 continuous batching (ragged prefill chunks mixed with decode)
+    mixed = None
+    if not args.no_mixed:
+        mixed = run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, world, args, hbm_peak)
+
     # ---- the whole mixer stack (projections + pre-norm + residual) at the same B
     mixer = None
     if not args.no_mixer:
@@ -671,7 +753,7 @@ def run_ours(args):
                            "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
                                N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
-                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer, "prefill": prefill}
+                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer, "prefill": prefill, "mixed": mixed}
     if dist is not None:
         dist.barrier()
         del g

@@ -7,6 +7,8 @@
 //   warps 0..15  consumers: per v-head, the state tile [dv][dk] in registers (warp w: rows
 //                8w..8w+7, lane l: columns 4l..4l+3), the gated delta rule per token
 //                (metal_gdn.rs:37-62) and the gated RMSNorm epilogue (qwen3_5.rs:660-665);
+//                the updated tile goes back into its stage and one bulk async store returns it
+//                to the pool while the warps move on;
 //   warp 16      producer (one lane): the v-heads' 64 KiB f32 state tiles into a 3-stage ring
 //                with bulk async copies completing on mbarriers;
 //   warps 17..20 prep: conv + SiLU of the q, k and v channels (decode rounding for a one-token
@@ -49,7 +51,7 @@ constexpr int FD_SMEM = FD_OFF_FLAGS + 16;
 static_assert(FD_STAGE % 16 == 0, "stage alignment");
 static_assert(FD_SMEM <= 232448, "shared memory budget");
 constexpr uint64_t FD_WAIT_NS = 2000000000ull;
-constexpr int FD_BAR_Y = 1, FD_BAR_PREP = 2, FD_BAR_DRAIN = 3;
+constexpr int FD_BAR_Y = 1, FD_BAR_PREP = 2, FD_BAR_DRAIN = 3, FD_BAR_STORE = 4;
 
 struct FdHdr {
     int slot, hv, t0, T;  // T < 0: end of this CTA's work
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
     if (tid == 0) {
         for (int s = 0; s < FD_NSTAGE; ++s) {
             mbar_init(&full[s], 2);           // producer (with the tile's bytes) + prep
-            mbar_init(&empty[s], FD_CWARPS);
+            mbar_init(&empty[s], 1);          // consumer thread 0, once the stage's state store has read it
         }
         *s_abort = 0;
         *s_issued = 0;
@@ -519,6 +521,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
     const float nw = bf2f(r.norm_w[oc]);
     int buf = 0;
     int k = 0;
+    int pend_s = -1;   // (thread 0) stage whose state store may still be reading it
     while (true) {
         const int s = k % FD_NSTAGE;
         const uint32_t ph = (uint32_t)(k / FD_NSTAGE) & 1u;
@@ -548,11 +551,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
             const float zs = bf2f(reinterpret_cast<const uint16_t*>(rec)[384 + oc]);
             const float gt = reinterpret_cast<const float*>(rec + 1024)[0];
             const float bt = reinterpret_cast<const float*>(rec + 1024)[1];
-            if (t == h.T - 1) {
-                // every read of this stage is done: hand it back
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-            }
             const float4 q4 = make_float4(__uint_as_float(qu.x << 16), __uint_as_float(qu.x & 0xffff0000u),
                                           __uint_as_float(qu.y << 16), __uint_as_float(qu.y & 0xffff0000u));
             const float4 k4 = make_float4(__uint_as_float(ku.x << 16), __uint_as_float(ku.x & 0xffff0000u),
@@ -587,12 +585,30 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
             buf ^= 1;
         }
 
-        // state tile back to the pool (evict-first: it is not re-read in this step)
-        float* dst = r.rec + ((size_t)h.slot * r.hv + h.hv) * (DV * DK) + row0 * DK + lane * 4;
+        // the previous item's state store has had this item's compute to read its stage: release it
+        if (tid == 0 && pend_s >= 0) {
+            bulk_wait_read_all();
+            mbar_arrive(&empty[pend_s]);
+            pend_s = -1;
+        }
+        // state tile back into its stage, then one bulk store to the pool (the copy engine drains it while
+        // the consumers go on)
+        float* tw = reinterpret_cast<float*>(smem + s * FD_STAGE);
 #pragma unroll
-        for (int j = 0; j < FD_RPW; ++j) __stcs(reinterpret_cast<float4*>(dst + j * DK), S[j]);
+        for (int j = 0; j < FD_RPW; ++j) *reinterpret_cast<float4*>(tw + (row0 + j) * DK + lane * 4) = S[j];
+        fence_async_shared();
+        named_bar_sync(FD_BAR_STORE, FD_CONSUMERS);
+        if (tid == 0) {
+            bulk_s2g(r.rec + ((size_t)h.slot * r.hv + h.hv) * (DV * DK), tw, FD_TILE);
+            bulk_commit();
+            pend_s = s;
+        }
     }
-    if (tid == 0) *s_consumed = k;
+    if (tid == 0) {
+        if (pend_s >= 0) mbar_arrive(&empty[pend_s]);
+        bulk_wait_all();   // every state store performed before the CTA ends
+        *s_consumed = k;
+    }
     fd_drain(full, s_issued, s_consumed, tid);
 }
 
