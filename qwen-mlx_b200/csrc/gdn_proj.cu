@@ -61,10 +61,20 @@ cudaError_t launch_add_rmsnorm(const uint16_t* h_in, long long ld_h, const uint1
 
 // ------------------------------------------------------------------ GEMM (cuBLASLt)
 
+// Per GEMM shape, the cuBLASLt algorithm that timed fastest among the heuristic's top candidates
+// (chosen on the first call made outside stream capture; calls during capture take the top one).
+struct GemmPlan {
+    int M, N, K;
+    long long ldx, ldo;
+    cublasLtMatmulAlgo_t algo;
+};
+
 struct GemmCtx {
     cublasLtHandle_t handle = nullptr;
     void* workspace = nullptr;
     size_t ws_bytes = 0;
+    GemmPlan plans[32];
+    int n_plans = 0;
 };
 
 GemmCtx* gemm_create(void* workspace, size_t ws_bytes) {
@@ -102,17 +112,57 @@ int gemm_bf16_nt(GemmCtx* g, int M, int N, int K, const uint16_t* x, long long l
         if (cublasLtMatrixLayoutCreate(&la, CUDA_R_16BF, K, N, K) != CUBLAS_STATUS_SUCCESS) break;
         if (cublasLtMatrixLayoutCreate(&lb, CUDA_R_16BF, K, M, ldx) != CUBLAS_STATUS_SUCCESS) break;
         if (cublasLtMatrixLayoutCreate(&lc, CUDA_R_16BF, N, M, ldo) != CUBLAS_STATUS_SUCCESS) break;
-        if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) break;
-        cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &g->ws_bytes,
-                                             sizeof g->ws_bytes);
-        cublasLtMatmulHeuristicResult_t heur;
-        int found = 0;
-        if (cublasLtMatmulAlgoGetHeuristic(g->handle, op, la, lb, lc, lc, pref, 1, &heur, &found) !=
-                CUBLAS_STATUS_SUCCESS ||
-            found == 0)
-            break;
         const float alpha = 1.0f, beta = 0.0f;
-        if (cublasLtMatmul(g->handle, op, &alpha, w, la, x, lb, &beta, out, lc, out, lc, &heur.algo, g->workspace,
+        const GemmPlan* plan = nullptr;
+        for (int i = 0; i < g->n_plans; ++i) {
+            const GemmPlan& q = g->plans[i];
+            if (q.M == M && q.N == N && q.K == K && q.ldx == ldx && q.ldo == ldo) plan = &q;
+        }
+        cublasLtMatmulAlgo_t algo;
+        if (plan) {
+            algo = plan->algo;
+        } else {
+            if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) break;
+            cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &g->ws_bytes,
+                                                 sizeof g->ws_bytes);
+            cublasLtMatmulHeuristicResult_t heur[8];
+            int found = 0;
+            if (cublasLtMatmulAlgoGetHeuristic(g->handle, op, la, lb, lc, lc, pref, 8, heur, &found) !=
+                    CUBLAS_STATUS_SUCCESS ||
+                found == 0)
+                break;
+            algo = heur[0].algo;
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            cudaStreamIsCapturing(stream, &cap);
+            if (cap == cudaStreamCaptureStatusNone && found > 1) {
+                // time every candidate on this call's operands (3 runs each, after one warm-up run)
+                cudaEvent_t e0, e1;
+                cudaEventCreate(&e0);
+                cudaEventCreate(&e1);
+                float best = 1e30f;
+                for (int i = 0; i < found; ++i) {
+                    if (cublasLtMatmul(g->handle, op, &alpha, w, la, x, lb, &beta, out, lc, out, lc, &heur[i].algo,
+                                       g->workspace, g->ws_bytes, stream) != CUBLAS_STATUS_SUCCESS)
+                        continue;
+                    cudaEventRecord(e0, stream);
+                    for (int r = 0; r < 3; ++r)
+                        cublasLtMatmul(g->handle, op, &alpha, w, la, x, lb, &beta, out, lc, out, lc, &heur[i].algo,
+                                       g->workspace, g->ws_bytes, stream);
+                    cudaEventRecord(e1, stream);
+                    cudaEventSynchronize(e1);
+                    float ms = 0.f;
+                    cudaEventElapsedTime(&ms, e0, e1);
+                    if (ms < best) {
+                        best = ms;
+                        algo = heur[i].algo;
+                    }
+                }
+                cudaEventDestroy(e0);
+                cudaEventDestroy(e1);
+                if (g->n_plans < 32) g->plans[g->n_plans++] = GemmPlan{M, N, K, ldx, ldo, algo};
+            }
+        }
+        if (cublasLtMatmul(g->handle, op, &alpha, w, la, x, lb, &beta, out, lc, out, lc, &algo, g->workspace,
                            g->ws_bytes, stream) != CUBLAS_STATUS_SUCCESS)
             break;
         rc = 0;
