@@ -260,25 +260,8 @@ MIXER_WEIGHT_BYTES = ((8192 + 4096 + 64) * 2048 + 2048 * 4096) * 2
 assert MIXER_WEIGHT_BYTES == 67_371_008
 
 
-def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrier, dist, world, args, hbm_peak):
-    """Config 2 through gdn_stack_step: h <- h + mixer_l(rms_norm(h)) over 30 layers (projections by
-    cuBLASLt).  Device tok/s, and e2e with the step's x copied in and h copied out."""
-    import importlib
-    synth = importlib.import_module("qwen_mlx_b200.synth")
-    mws = []
-    keep = []
-    for l in range(N_LAYERS):
-        w = synth.layer_weights(cfg, l, with_proj=False)
-        step = gdn.LayerWeights(w, dev)
-        w_in = (torch.randn((8192 + 4096 + 64, cfg.hidden), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
-        w_out = (torch.randn((cfg.hidden, cfg.z_dim), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
-        pre = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
-        keep.append((step, w_in, w_out, pre))
-        mws.append(abi.GdnMixerWeightsC(step.c, w_in.data_ptr(), w_out.data_ptr(), pre.data_ptr()))
-    arr = (abi.GdnMixerWeightsC * N_LAYERS)(*mws)
-    h = torch.randn((B, cfg.hidden), device=dev, generator=gen).to(torch.bfloat16)
-    slots = torch.arange(B, dtype=torch.int32, device=dev)
-    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+def _time_stack(torch, lib, abi, pool, arr, h, slots, cu, B, cfg, stream, barrier, dist, args):
+    """Device ms and e2e ms (x in from pinned host, h out) of `args.steps` graph-replayed stack steps."""
     sp = C.c_void_p(stream.cuda_stream)
 
     def step():
@@ -330,17 +313,68 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
     barrier()
     e2e_ms = e0.elapsed_time(e1)
     if dist is not None:
-        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms], device=h.device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = float(t[0].item()), float(t[1].item())
-    step_bytes = N_LAYERS * (MIXER_WEIGHT_BYTES + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
     del g
+    return ms, e2e_ms, x_host.numel() * 2, y_host.numel() * 2
+
+
+# 4-bit (MLX affine, group 64) bytes of one layer's projections: codes + bf16 scale and bias per group.
+MIXER_WEIGHT_BYTES_Q4 = ((8192 + 4096 + 64) * 2048 + 2048 * 4096) // 2 + \
+    ((8192 + 4096 + 64) * 2048 + 2048 * 4096) // 64 * 4
+assert MIXER_WEIGHT_BYTES_Q4 == 18_948_096
+
+
+def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrier, dist, world, args, hbm_peak):
+    """Config 2 through gdn_stack_step: h <- h + mixer_l(rms_norm(h)) over 30 layers, twice: with bf16
+    projections (cuBLASLt) and with MLX 4-bit projections (the reference's quantized checkpoint format;
+    the weight-streaming tcgen05 kernel, weights dequantized on chip).  Device tok/s, and e2e with the
+    step's x copied in and h copied out."""
+    import importlib
+    synth = importlib.import_module("qwen_mlx_b200.synth")
+    plain, q4 = [], []
+    keep = []
+    n_in = 8192 + 4096 + 64
+    for l in range(N_LAYERS):
+        w = synth.layer_weights(cfg, l, with_proj=False)
+        step = gdn.LayerWeights(w, dev)
+        w_in = (torch.randn((n_in, cfg.hidden), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w_out = (torch.randn((cfg.hidden, cfg.z_dim), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        pre = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
+        # synthetic 4-bit weights: random codes, scales U(0, 0.005), biases N(0, 0.005^2) (timing only)
+        qt = []
+        for rows, cols in ((n_in, cfg.hidden), (cfg.hidden, cfg.z_dim)):
+            wq = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, cols // 8), dtype=torch.int32, device=dev, generator=gen)
+            sc = (torch.rand((rows, cols // 64), device=dev, generator=gen) * 0.005).to(torch.bfloat16)
+            bi = (torch.randn((rows, cols // 64), device=dev, generator=gen) * 0.005).to(torch.bfloat16)
+            qt.append(gdn.tile_weight_q4(wq, sc, bi))
+        keep.append((step, w_in, w_out, pre, qt))
+        plain.append(abi.GdnMixerWeightsC(step.c, w_in.data_ptr(), w_out.data_ptr(), pre.data_ptr(),
+                                          None, None, None, None))
+        q4.append(abi.GdnMixerWeightsC(step.c, None, None, pre.data_ptr(), None, None, qt[0].data_ptr(),
+                                       qt[1].data_ptr()))
+    arr_p = (abi.GdnMixerWeightsC * N_LAYERS)(*plain)
+    arr_q = (abi.GdnMixerWeightsC * N_LAYERS)(*q4)
+    h = torch.randn((B, cfg.hidden), device=dev, generator=gen).to(torch.bfloat16)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    ms, e2e_ms, hb, db = _time_stack(torch, lib, abi, pool, arr_p, h, slots, cu, B, cfg, stream, barrier, dist, args)
+    ms_q, e2e_q, _, _ = _time_stack(torch, lib, abi, pool, arr_q, h, slots, cu, B, cfg, stream, barrier, dist, args)
+    step_bytes = N_LAYERS * (MIXER_WEIGHT_BYTES + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
+    step_bytes_q = N_LAYERS * (MIXER_WEIGHT_BYTES_Q4 + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
     return {"tok_s": world * B * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps,
             "hbm_frac_of_measured": step_bytes / (ms / args.steps / 1e3) / 1e9 / hbm_peak,
             "bytes_per_step": step_bytes,
-            "e2e_tok_s": world * B * args.steps / (e2e_ms / 1e3), "h2d_bytes_per_step": x_host.numel() * 2,
-            "d2h_bytes_per_step": y_host.numel() * 2,
-            "note": "30 x (pre-norm + in_proj GEMM + gdn_layer_step + out_proj GEMM + residual); GEMMs are cuBLASLt"}
+            "e2e_tok_s": world * B * args.steps / (e2e_ms / 1e3), "h2d_bytes_per_step": hb,
+            "d2h_bytes_per_step": db,
+            "note": "30 x (pre-norm + in_proj GEMM + gdn_layer_step + out_proj GEMM + residual); bf16 GEMMs "
+                    "are cuBLASLt",
+            "q4": {"tok_s": world * B * args.steps / (ms_q / 1e3), "ms_per_step": ms_q / args.steps,
+                   "hbm_frac_of_measured": step_bytes_q / (ms_q / args.steps / 1e3) / 1e9 / hbm_peak,
+                   "bytes_per_step": step_bytes_q, "e2e_tok_s": world * B * args.steps / (e2e_q / 1e3),
+                   "note": "same stack, MLX 4-bit (group 64) projections on the weight-streaming tcgen05 "
+                           "kernel; synthetic random codes"}}
 
 
 # Prefill (chunked WY) algorithmic flops per token per layer, chunk 64: 6*dk*dv + 2*C*(3*dk + 2*dv) per

@@ -160,12 +160,23 @@ GDN_API int gdn_layer_step(gdn_pool* pool, int32_t layer, const gdn_layer_weight
 /* Parameters of a whole mixer layer (GatedDeltaNet, qwen3_5.rs:466-503) and of its
  * decoder-layer input norm.  Device pointers.  w_in holds the four input
  * projections stacked by rows in the reference's merged order (qwen3_5.rs:1038-1047):
- * in_proj_qkv (D rows) | in_proj_z (Hv*dv) | in_proj_b (Hv) | in_proj_a (Hv). */
+ * in_proj_qkv (D rows) | in_proj_z (Hv*dv) | in_proj_b (Hv) | in_proj_a (Hv).
+ * Each projection may also (or instead) be given in a tiled form:
+ *   *_q4    gdn_weight_tile_q4 tiles of the MLX 4-bit quantized weight (the reference's
+ *           4-bit checkpoint, qwen3_5.rs:929-935): used for every call when present;
+ *   *_tiles gdn_weight_tile tiles of the bf16 weight: used for calls of at most 64 tokens.
+ * Otherwise (and for longer calls without 4-bit tiles) the row-major bf16 weight runs on
+ * cuBLASLt, so a row-major weight may be NULL only when one of the tiled forms covers
+ * every call made. */
 typedef struct gdn_mixer_weights {
     gdn_layer_weights step;      /* conv_w, A_log, dt_bias, norm_w */
-    const gdn_bf16* w_in;        /* [D + Hv*dv + 2*Hv][hidden] */
-    const gdn_bf16* w_out;       /* [hidden][Hv*dv]  out_proj */
+    const gdn_bf16* w_in;        /* [D + Hv*dv + 2*Hv][hidden] or NULL */
+    const gdn_bf16* w_out;       /* [hidden][Hv*dv]  out_proj, or NULL */
     const gdn_bf16* pre_norm_w;  /* [hidden] input_layernorm gain (used by gdn_stack_step) */
+    const void* w_in_tiles;      /* gdn_weight_tile(D + Hv*dv + 2*Hv, hidden) of w_in, or NULL */
+    const void* w_out_tiles;     /* gdn_weight_tile(hidden, Hv*dv) of w_out, or NULL */
+    const void* w_in_q4;         /* gdn_weight_tile_q4 of the quantized w_in, or NULL */
+    const void* w_out_q4;        /* gdn_weight_tile_q4 of the quantized w_out, or NULL */
 } gdn_mixer_weights;
 
 /* One projection (nn::Linear without bias, qwen3_5.rs:572-586, :668):
@@ -175,10 +186,54 @@ typedef struct gdn_mixer_weights {
 GDN_API int gdn_linear(gdn_pool* pool, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x,
                        int64_t ld_x, const gdn_bf16* w, gdn_bf16* y, int64_t ld_y, void* stream);
 
+/* Bytes of the tiled copy of a bf16 projection weight w [n_out][n_in] (0 for a bad shape). */
+GDN_API int64_t gdn_weight_tile_bytes(int32_t n_out, int32_t n_in);
+
+/* Write the tiled copy of w [n_out][n_in] bf16 (row-major, device) into `tiles`
+ * (gdn_weight_tile_bytes bytes, 16-byte aligned, device): the layout the
+ * weight-streaming tensor-core kernel reads.  Blocks of 8 rows x 64 columns, 1 KB
+ * each, block (kt, rg) (columns [64 kt, +64), rows [8 rg, +8)) at
+ * (kt * ceil(n_out/8) + rg) * 1024; inside it element (8 rg + r, 64 kt + 8 c + e) at
+ * byte c*128 + r*16 + e*2; rows >= n_out and columns >= n_in are zero.  Done once
+ * when weights are loaded.  Asynchronous. */
+GDN_API int gdn_weight_tile(int32_t n_out, int32_t n_in, const gdn_bf16* w, void* tiles, void* stream);
+
+/* Bytes of the tiled copy of an MLX 4-bit weight of logical shape [n_out][n_in]
+ * (n_in a multiple of 64; 0 otherwise). */
+GDN_API int64_t gdn_weight_tile_q4_bytes(int32_t n_out, int32_t n_in);
+
+/* Tile an MLX affine 4-bit weight (bits 4, group size 64, as nn::QuantizedLinear holds it after
+ * quantize, qwen3_5.rs:929-935): w_q [n_out][n_in/8] uint32 (column k in bits 4*(k%8) of word
+ * k/8), scales and biases [n_out][n_in/64] bf16; weight = scale * q + bias.  Blocks of 8 rows x
+ * one group, 288 B each, block (kt, rg) at (kt * ceil(n_out/8) + rg) * 288: word (c, r) at
+ * c*32 + r*4 holds the codes of row 8 rg + r, columns 64 kt + 8c .. +7 (column 8c+e in nibble
+ * e/2 for even e, 4 + e/2 for odd e), then the 8 scales at 256 and the 8 biases at 272; rows
+ * >= n_out are zero.  Device pointers, 16-byte aligned tiles.  Asynchronous. */
+GDN_API int gdn_weight_tile_q4(int32_t n_out, int32_t n_in, const uint32_t* w_q, const gdn_bf16* scales,
+                               const gdn_bf16* biases, void* tiles, void* stream);
+
+/* gdn_linear on a bf16 tiled weight, on the weight-streaming tensor-core kernel
+ * (tokens in blocks of 64, each block streams the weight once):
+ * y[m][n] = bf16(sum_k x[m][k] * w[n][k]), f32 accumulation.  n_in % 8 == 0, x rows
+ * 16-byte aligned (ld_x % 8 == 0).  The sum order is fixed per shape and device, so
+ * results repeat bit for bit.  Asynchronous. */
+GDN_API int gdn_linear_tiled(gdn_pool* pool, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x,
+                             int64_t ld_x, const void* w_tiles, gdn_bf16* y, int64_t ld_y, void* stream);
+
+/* The 4-bit quantized projection (MLX quantized_matmul with transpose, bits 4, group 64,
+ * qwen3_5.rs:572-586 / :668 on the quantized checkpoint): each weight is dequantized once to
+ * bf16 (scale * q + bias, one rounding), then y[m][n] = bf16(sum_k x[m][k] * w[n][k]) with
+ * f32 accumulation on the tensor cores.  w_q4_tiles from gdn_weight_tile_q4; n_in % 64 == 0,
+ * x rows 16-byte aligned.  Tokens in blocks of 64.  Deterministic.  Asynchronous. */
+GDN_API int gdn_linear_q4(gdn_pool* pool, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x,
+                          int64_t ld_x, const void* w_q4_tiles, gdn_bf16* y, int64_t ld_y, void* stream);
+
 /* A whole mixer layer (GatedDeltaNet::forward_with_cache, qwen3_5.rs:559-669):
  * y = out_proj(gdn_layer_step(in_proj(x))) over a packed ragged batch.
- * x [n_tokens][ld_x], y [n_tokens][ld_y] bf16, hidden columns.  The projections are
- * bf16 GEMMs with f32 accumulation run by cuBLASLt (library GEMM).  Asynchronous. */
+ * x [n_tokens][ld_x], y [n_tokens][ld_y] bf16, hidden columns.  The projections run as
+ * gdn_mixer_weights says: 4-bit tiles on the weight-streaming kernel, bf16 tiles on it for
+ * calls of at most 64 tokens, otherwise cuBLASLt (library GEMM), all with f32 accumulation.
+ * Asynchronous. */
 GDN_API int gdn_mixer_step(gdn_pool* pool, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x,
                            int64_t ld_x, gdn_bf16* y, int64_t ld_y, const int32_t* slot_ids,
                            const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens, void* stream);

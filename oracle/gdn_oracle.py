@@ -187,6 +187,41 @@ def linear(x, w):
     return out
 
 
+def _f64_to_bf16(x):
+    """Round float64 to bf16 once (round-to-nearest-even): via float32 rounded to odd, which keeps the
+    information a second rounding to bf16 needs."""
+    x = np.asarray(x, np.float64)
+    t = x.astype(np.float32)
+    over = np.abs(t.astype(np.float64)) > np.abs(x)
+    t = np.where(over, np.nextafter(t, np.float32(0)), t).astype(np.float32)
+    inexact = t.astype(np.float64) != x
+    u = t.view(np.uint32) | inexact.astype(np.uint32)
+    u32 = u.astype(np.uint32)
+    return ((u32 + np.uint32(0x7FFF) + ((u32 >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+
+
+def q4_dequantize(w_q, scales, biases, group: int = 64):
+    """MLX affine 4-bit dequantization (bits 4, groups of `group` columns; mlx quantized_matmul with
+    transpose, called for the quantized projections at qwen3_5.rs:572-586, :668): column k of row n is
+    scale[n][k/group] * q + bias[n][k/group], q = bits 4*(k%8) of word k/8, rounded once to the
+    activation type (bf16), as MLX's quantized matmul tile loader writes it.  Returns bf16 [N, K]."""
+    w_q = np.asarray(w_q, np.uint32)
+    N, K = w_q.shape[0], w_q.shape[1] * 8
+    shifts = (np.arange(8, dtype=np.uint32) * 4)[None, None, :]
+    q = ((w_q[:, :, None] >> shifts) & np.uint32(0xF)).reshape(N, K).astype(np.float64)
+    s = np.repeat((np.asarray(scales, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64),
+                  group, axis=1)
+    b = np.repeat((np.asarray(biases, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64),
+                  group, axis=1)
+    return _f64_to_bf16(s * q + b)
+
+
+def q4_linear(x, w_q, scales, biases):
+    """The 4-bit projection: bf16(x @ dequant(w)^T) with f32 accumulation (linear() on the
+    dequantized weight)."""
+    return linear(x, q4_dequantize(w_q, scales, biases))
+
+
 def conv(cfg, x, conv_state, conv_w):
     """Causal conv + SiLU over one sequence x [T, >=D]; returns (out [T, D], new conv state)."""
     x = _c(x, np.uint16)

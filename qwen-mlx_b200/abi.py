@@ -48,7 +48,8 @@ class GdnStepIOC(C.Structure):
 
 
 class GdnMixerWeightsC(C.Structure):
-    _fields_ = [("step", GdnLayerWeightsC), ("w_in", _vp), ("w_out", _vp), ("pre_norm_w", _vp)]
+    _fields_ = [("step", GdnLayerWeightsC), ("w_in", _vp), ("w_out", _vp), ("pre_norm_w", _vp),
+                ("w_in_tiles", _vp), ("w_out_tiles", _vp), ("w_in_q4", _vp), ("w_out_q4", _vp)]
 
 
 class GdnStepEntryC(C.Structure):
@@ -82,6 +83,12 @@ SIGNATURES = {
     "gdn_layer_step": (_int, [_vp, _i32, C.POINTER(GdnLayerWeightsC), C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32,
                               _vp]),
     "gdn_linear": (_int, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp]),
+    "gdn_weight_tile_bytes": (_i64, [_i32, _i32]),
+    "gdn_weight_tile": (_int, [_i32, _i32, _vp, _vp, _vp]),
+    "gdn_weight_tile_q4_bytes": (_i64, [_i32, _i32]),
+    "gdn_weight_tile_q4": (_int, [_i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gdn_linear_tiled": (_int, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp]),
+    "gdn_linear_q4": (_int, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp]),
     "gdn_mixer_step": (_int, [_vp, _i32, C.POINTER(GdnMixerWeightsC), _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32,
                               _vp]),
     "gdn_stack_step": (_int, [_vp, C.POINTER(GdnMixerWeightsC), _vp, _i64, _vp, _vp, _i32, _i32, _vp]),

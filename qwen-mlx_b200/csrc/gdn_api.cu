@@ -69,6 +69,9 @@ struct gdn_pool {
     int32_t* err;            // device words: [0] error flags, [1] chunked-kernel work ticket
     gdn::GemmCtx* gemm;      // cuBLASLt handle for the projections
     void* gemm_ws;           // its workspace
+    int n_sm;                // multiprocessors of the pool's device
+    int* wg_cnt;             // weight-streaming GEMM: per-row-tile arrival counters [kWgMaxTiles] (zero at rest)
+    float* wg_ws;            // weight-streaming GEMM: partial sums [wg_workspace_floats(n_sm)]
     uint16_t* proj;          // scratch [rec_cap][D + Hv*dv + 2*Hv]: projection outputs
     uint16_t* gated;         // scratch [rec_cap][Hv*dv]: layer-step output (out_proj input)
     uint16_t* hn;            // scratch [rec_cap][hidden]: normed stack input
@@ -78,6 +81,7 @@ struct gdn_pool {
 };
 
 static constexpr int kDeviceWords = 16;  // one 64-byte allocation
+static constexpr int kWgMaxTiles = 4096;  // arrival counters: weight-streaming GEMMs of up to 4096 row slabs
 
 static long long proj_ld(const gdn_pool* p) { return (long long)p->D + p->cfg.n_v_heads * 128 + 2 * p->cfg.n_v_heads; }
 
@@ -189,6 +193,9 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
     p->rec_cap = 0;
     p->gemm = nullptr;
     p->gemm_ws = nullptr;
+    p->wg_cnt = nullptr;
+    p->wg_ws = nullptr;
+    p->n_sm = 0;
     rc = reserve_records(p, n_slots > 1024 ? n_slots : 1024);
     if (rc == GDN_OK) {
         const size_t ws = 32u << 20;
@@ -196,12 +203,23 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         if (e == cudaSuccess) p->gemm = gdn::gemm_create(p->gemm_ws, ws);
         if (e != cudaSuccess || !p->gemm) rc = fail(GDN_E_NOMEM, "cuBLASLt handle / workspace creation failed");
     }
+    if (rc == GDN_OK) {
+        e = cudaDeviceGetAttribute(&p->n_sm, cudaDevAttrMultiProcessorCount, device);
+        if (e == cudaSuccess) e = cudaMalloc(&p->wg_cnt, kWgMaxTiles * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&p->wg_ws, gdn::wg_workspace_floats(p->n_sm) * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(p->wg_cnt, 0, kWgMaxTiles * sizeof(int));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) rc = fail(GDN_E_NOMEM, "projection GEMM workspace: %s", cudaGetErrorString(e));
+    }
     if (rc) {
         cudaFree(p->rec);
         cudaFree(p->conv);
         cudaFree(p->err);
         cudaFree(p->recs); cudaFree(p->proj); cudaFree(p->gated); cudaFree(p->hn); cudaFree(p->mix);
         cudaFree(p->gemm_ws);
+        cudaFree(p->wg_cnt);
+        cudaFree(p->wg_ws);
+        gdn::gemm_destroy(p->gemm);
         delete p;
         return rc;
     }
@@ -231,6 +249,8 @@ int gdn_pool_destroy(gdn_pool* p) {
     cudaFree(p->mix);
     gdn::gemm_destroy(p->gemm);
     cudaFree(p->gemm_ws);
+    cudaFree(p->wg_cnt);
+    cudaFree(p->wg_ws);
     delete p;
     return ok();
 }
@@ -249,7 +269,8 @@ int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
     *bytes = (sizeof(float) * p->rec_slot_elems + sizeof(uint16_t) * p->conv_slot_elems) * (size_t)p->n_slots *
                  p->cfg.n_layers +
              sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES +
-             (size_t)p->rec_cap * 2 * (proj_ld(p) + p->cfg.n_v_heads * 128 + 2 * p->cfg.hidden) + (32u << 20);
+             (size_t)p->rec_cap * 2 * (proj_ld(p) + p->cfg.n_v_heads * 128 + 2 * p->cfg.hidden) + (32u << 20) +
+             kWgMaxTiles * sizeof(int) + (size_t)gdn::wg_workspace_floats(p->n_sm) * sizeof(float);
     return ok();
 }
 
@@ -431,7 +452,53 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
 }
 
 static bool mixer_weights_ok(const gdn_mixer_weights* w) {
-    return w && w->w_in && w->w_out && w->step.conv_w && w->step.A_log && w->step.dt_bias && w->step.norm_w;
+    return w && (w->w_in || w->w_in_tiles || w->w_in_q4) && (w->w_out || w->w_out_tiles || w->w_out_q4) &&
+           w->step.conv_w && w->step.A_log && w->step.dt_bias && w->step.norm_w;
+}
+
+// The weight-streaming kernel reads x rows that start on 16-byte boundaries, in whole 8-column chunks.
+static bool wg_rows_ok(int K, const void* x, long long ldx, const void* tiles) {
+    return K % 8 == 0 && ldx % 8 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)tiles & 15u) == 0;
+}
+
+// y = x w^T on the weight-streaming kernel, in token blocks of WG_MAX_M (each block streams the weight).
+static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, long long ldx, const void* tiles,
+                  uint16_t* y, long long ldy, cudaStream_t s, const char* what) {
+    for (int m0 = 0; m0 < M; m0 += gdn::WG_MAX_M) {
+        gdn::WgGemm g;
+        g.tiles = reinterpret_cast<const uint8_t*>(tiles);
+        g.q4 = q4;
+        g.x = x + (long long)m0 * ldx; g.ldx = ldx;
+        g.y = y + (long long)m0 * ldy; g.ldy = ldy;
+        g.M = M - m0 < gdn::WG_MAX_M ? M - m0 : gdn::WG_MAX_M;
+        g.N = N; g.K = K;
+        g.n_sm = p->n_sm; g.ws = p->wg_ws; g.cnt = p->wg_cnt; g.err = p->err;
+        const cudaError_t e = gdn::launch_wg_gemm(g, s);
+        if (e != cudaSuccess)
+            return fail(GDN_E_CUDA, "%s: weight-streaming GEMM launch failed (M=%d N=%d K=%d): %s", what, g.M, N, K,
+                        cudaGetErrorString(e));
+    }
+    return GDN_OK;
+}
+
+// One projection y = x w^T: 4-bit tiles when given (any token count), else bf16 tiles for calls of at
+// most WG_MAX_M tokens, else cuBLASLt on the row-major weight.
+static int projection(gdn_pool* p, int M, int N, int K, const uint16_t* x, long long ldx, const uint16_t* w,
+                      const void* w_tiles, const void* w_q4, uint16_t* y, long long ldy, cudaStream_t s,
+                      const char* what) {
+    if (w_q4) {
+        if (!wg_rows_ok(K, x, ldx, w_q4) || K % 64 != 0)
+            return fail(GDN_E_INVALID, "%s: 4-bit projection needs K %% 64 == 0 and 16-byte aligned rows", what);
+        return wg_run(p, true, M, N, K, x, ldx, w_q4, y, ldy, s, what);
+    }
+    if (w_tiles && M <= gdn::WG_MAX_M && wg_rows_ok(K, x, ldx, w_tiles))
+        return wg_run(p, false, M, N, K, x, ldx, w_tiles, y, ldy, s, what);
+    if (!w)
+        return fail(GDN_E_INVALID, "%s: M=%d tokens needs the row-major weight (tiled path: 1..%d tokens, "
+                    "16-byte aligned rows)", what, M, gdn::WG_MAX_M);
+    if (gdn::gemm_bf16_nt(p->gemm, M, N, K, x, ldx, w, y, ldy, s))
+        return fail(GDN_E_CUDA, "%s: cuBLASLt GEMM failed (M=%d N=%d K=%d)", what, M, N, K);
+    return GDN_OK;
 }
 
 // One mixer layer on the pool's scratch: x -> proj -> fused step -> gated -> y.
@@ -442,18 +509,18 @@ static int mixer_layer(gdn_pool* p, int32_t layer, const gdn_mixer_weights* w, c
     const int zd = p->cfg.n_v_heads * 128;
     const long long ldp = proj_ld(p);
     cudaStream_t s = (cudaStream_t)stream;
-    if (gdn::gemm_bf16_nt(p->gemm, n_tokens, (int)ldp, H, x, ld_x, w->w_in, p->proj, ldp, s))
-        return fail(GDN_E_CUDA, "cuBLASLt in-projection GEMM failed (M=%d N=%lld K=%d)", n_tokens, ldp, H);
+    int rc = projection(p, n_tokens, (int)ldp, H, x, ld_x, w->w_in, w->w_in_tiles, w->w_in_q4, p->proj, ldp, s,
+                        "in-projection");
+    if (rc) return rc;
     gdn_step_io io;
     io.qkv = p->proj; io.ld_qkv = ldp;
     io.z = p->proj + p->D; io.ld_z = ldp;
     io.ab = p->proj + p->D + zd; io.ld_ab = ldp;
     io.out = p->gated; io.ld_out = zd;
-    int rc = gdn_layer_step(p, layer, &w->step, &io, slot_ids, cu, n_seq, n_tokens, stream);
+    rc = gdn_layer_step(p, layer, &w->step, &io, slot_ids, cu, n_seq, n_tokens, stream);
     if (rc) return rc;
-    if (gdn::gemm_bf16_nt(p->gemm, n_tokens, H, zd, p->gated, zd, w->w_out, y, ld_y, s))
-        return fail(GDN_E_CUDA, "cuBLASLt out-projection GEMM failed (M=%d N=%d K=%d)", n_tokens, H, zd);
-    return GDN_OK;
+    return projection(p, n_tokens, H, zd, p->gated, zd, w->w_out, w->w_out_tiles, w->w_out_q4, y, ld_y, s,
+                      "out-projection");
 }
 
 int gdn_linear(gdn_pool* p, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x, int64_t ld_x,
@@ -469,6 +536,69 @@ int gdn_linear(gdn_pool* p, int32_t n_tokens, int32_t n_out, int32_t n_in, const
     if (gdn::gemm_bf16_nt(p->gemm, n_tokens, n_out, n_in, x, ld_x, w, y, ld_y, (cudaStream_t)stream))
         return fail(GDN_E_CUDA, "cuBLASLt GEMM failed (M=%d N=%d K=%d)", n_tokens, n_out, n_in);
     return ok();
+}
+
+int64_t gdn_weight_tile_bytes(int32_t n_out, int32_t n_in) {
+    if (n_out <= 0 || n_in <= 0) return 0;
+    return gdn::wg_tile_bytes(n_out, n_in);
+}
+
+int gdn_weight_tile(int32_t n_out, int32_t n_in, const gdn_bf16* w, void* tiles, void* stream) {
+    if (n_out <= 0 || n_in <= 0) return fail(GDN_E_INVALID, "bad weight shape [%d][%d]", n_out, n_in);
+    if (!w || !tiles) return fail(GDN_E_INVALID, "NULL tensor");
+    if (((uintptr_t)tiles & 15u) != 0) return fail(GDN_E_INVALID, "tiled weight buffer must be 16-byte aligned");
+    const cudaError_t e = gdn::launch_wg_tile(w, n_out, n_in, reinterpret_cast<uint8_t*>(tiles), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "weight tiling kernel launch");
+    return ok();
+}
+
+int64_t gdn_weight_tile_q4_bytes(int32_t n_out, int32_t n_in) {
+    if (n_out <= 0 || n_in <= 0 || n_in % 64 != 0) return 0;
+    return gdn::wq_tile_bytes(n_out, n_in);
+}
+
+int gdn_weight_tile_q4(int32_t n_out, int32_t n_in, const uint32_t* w_q, const gdn_bf16* scales,
+                       const gdn_bf16* biases, void* tiles, void* stream) {
+    if (n_out <= 0 || n_in <= 0 || n_in % 64 != 0)
+        return fail(GDN_E_INVALID, "bad 4-bit weight shape [%d][%d] (n_in must be a multiple of the group, 64)",
+                    n_out, n_in);
+    if (!w_q || !scales || !biases || !tiles) return fail(GDN_E_INVALID, "NULL tensor");
+    if (((uintptr_t)tiles & 15u) != 0) return fail(GDN_E_INVALID, "tiled weight buffer must be 16-byte aligned");
+    const cudaError_t e = gdn::launch_wq_tile(w_q, scales, biases, n_out, n_in, reinterpret_cast<uint8_t*>(tiles),
+                                              (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "4-bit weight tiling kernel launch");
+    return ok();
+}
+
+static int linear_tiled_common(gdn_pool* p, bool q4, int32_t n_tokens, int32_t n_out, int32_t n_in,
+                               const gdn_bf16* x, int64_t ld_x, const void* tiles, gdn_bf16* y, int64_t ld_y,
+                               void* stream, const char* what) {
+    if (!p) return fail(GDN_E_INVALID, "pool is NULL");
+    if (n_tokens < 0 || n_out <= 0 || n_in <= 0 || ld_x < n_in || ld_y < n_out)
+        return fail(GDN_E_INVALID, "bad GEMM shape (M=%d N=%d K=%d ld_x=%lld ld_y=%lld)", n_tokens, n_out, n_in,
+                    (long long)ld_x, (long long)ld_y);
+    if (n_tokens == 0) return ok();
+    if (!x || !tiles || !y) return fail(GDN_E_INVALID, "NULL tensor");
+    if (!wg_rows_ok(n_in, x, ld_x, tiles) || (q4 && n_in % 64 != 0))
+        return fail(GDN_E_INVALID, "%s needs n_in %% %d == 0 and 16-byte aligned x rows and weight", what,
+                    q4 ? 64 : 8);
+    if (gdn::wg_num_slabs((n_out + 7) / 8, p->n_sm) > kWgMaxTiles)
+        return fail(GDN_E_INVALID, "n_out %d: more row slabs than the pool's %d counters", n_out, kWgMaxTiles);
+    DeviceGuard g(p->device);
+    if (g.status != cudaSuccess) return cuda_fail(g.status, "cudaSetDevice");
+    const int rc = wg_run(p, q4, n_tokens, n_out, n_in, x, ld_x, tiles, y, ld_y, (cudaStream_t)stream, what);
+    return rc ? rc : ok();
+}
+
+int gdn_linear_tiled(gdn_pool* p, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x, int64_t ld_x,
+                     const void* w_tiles, gdn_bf16* y, int64_t ld_y, void* stream) {
+    return linear_tiled_common(p, false, n_tokens, n_out, n_in, x, ld_x, w_tiles, y, ld_y, stream,
+                               "gdn_linear_tiled");
+}
+
+int gdn_linear_q4(gdn_pool* p, int32_t n_tokens, int32_t n_out, int32_t n_in, const gdn_bf16* x, int64_t ld_x,
+                  const void* w_q4_tiles, gdn_bf16* y, int64_t ld_y, void* stream) {
+    return linear_tiled_common(p, true, n_tokens, n_out, n_in, x, ld_x, w_q4_tiles, y, ld_y, stream, "gdn_linear_q4");
 }
 
 int gdn_mixer_step(gdn_pool* p, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x, int64_t ld_x,

@@ -93,6 +93,31 @@ cudaError_t launch_add_rmsnorm(const uint16_t* h_in, long long ld_h, const uint1
                                uint16_t* h_out, const uint16_t* w, uint16_t* hn, long long ld_hn, int rows, int H,
                                float eps, cudaStream_t stream);
 
+// Weight-streaming projection GEMM for calls of at most WG_MAX_M tokens on a tiled weight
+// (gdn_wgemm.cu): y[m][n] = bf16(sum_k x[m][k] w[n][k]).  x rows 16-byte aligned (ldx % 8 == 0,
+// K % 8 == 0; K % 64 == 0 for 4-bit tiles); ws holds wg_workspace_floats(n_sm) floats, cnt one
+// zeroed int per 128 rows of w.
+constexpr int WG_MAX_M = 64;
+struct WgGemm {
+    const uint8_t* tiles;        // bf16 tiles (wg_tile_bytes) or 4-bit tiles (wq_tile_bytes)
+    bool q4;
+    const uint16_t* x; long long ldx;
+    uint16_t* y; long long ldy;
+    int M, N, K;
+    int n_sm;
+    float* ws;
+    int* cnt;
+    int* err;
+};
+long long wg_tile_bytes(int N, int K);
+long long wq_tile_bytes(int N, int K);
+long long wg_workspace_floats(int n_sm);
+int wg_num_slabs(int NRG, int n_sm);  // row slabs of the weight-streaming GEMM (one arrival counter each)
+cudaError_t launch_wg_tile(const uint16_t* w, int N, int K, uint8_t* tiles, cudaStream_t stream);
+cudaError_t launch_wq_tile(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases, int N, int K,
+                           uint8_t* tiles, cudaStream_t stream);
+cudaError_t launch_wg_gemm(const WgGemm& g, cudaStream_t stream);
+
 // Set the calling thread's gdn_last_error() message and return `code` / GDN_OK.
 int record_error(int code, const char* msg);
 int record_ok();

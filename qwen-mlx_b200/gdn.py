@@ -92,18 +92,65 @@ class LayerWeights:
                                       self.norm_w.data_ptr())
 
 
+def tile_weight(w, stream=None):
+    """The tiled copy (gdn_weight_tile) of a row-major bf16 device weight w [n_out, n_in]: the layout
+    the weight-streaming projection kernel reads.  Returns a uint8 device tensor."""
+    n_out, n_in = w.shape
+    t = torch.empty(int(abi.lib().gdn_weight_tile_bytes(n_out, n_in)), dtype=torch.uint8, device=w.device)
+    abi.call("gdn_weight_tile", n_out, n_in, _ptr(w), _ptr(t), _stream(stream))
+    return t
+
+
+def tile_weight_q4(w_q, scales, biases, stream=None):
+    """The tiled copy (gdn_weight_tile_q4) of an MLX 4-bit weight given as device tensors w_q [n_out,
+    n_in/8] (int32 holding the uint32 words), scales and biases [n_out, n_in/64] bf16."""
+    n_out, n_in = w_q.shape[0], w_q.shape[1] * 8
+    t = torch.empty(int(abi.lib().gdn_weight_tile_q4_bytes(n_out, n_in)), dtype=torch.uint8, device=w_q.device)
+    abi.call("gdn_weight_tile_q4", n_out, n_in, _ptr(w_q), _ptr(scales), _ptr(biases), _ptr(t), _stream(stream))
+    return t
+
+
+def q4_to_device(w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray, device):
+    """Upload an MLX 4-bit weight (numpy uint32 words, bf16 bit patterns) and tile it."""
+    wq = torch.from_numpy(np.ascontiguousarray(w_q, np.uint32).view(np.int32)).to(device)
+    return tile_weight_q4(wq, bf16_to_device(scales, device), bf16_to_device(biases, device))
+
+
 class MixerWeights:
     """Device copies of one whole mixer layer: step parameters, merged in-projection
     [qkv | z | b | a] rows (the reference's merged order), out-projection and the
-    decoder input-norm gain."""
+    decoder input-norm gain.
 
-    def __init__(self, w: dict, device):
+    tiled=True adds the bf16 tiled copies (calls of at most 64 tokens run the projections on the
+    weight-streaming tensor-core kernel).  q4=(w_in_q, w_out_q), each a (w_q, scales, biases) MLX
+    4-bit weight (synth.quantize_q4 or a quantized checkpoint), makes the projections 4-bit for every
+    call; the row-major bf16 weights are then not uploaded."""
+
+    def __init__(self, w: dict, device, tiled: bool = False, q4=None):
         self.step = LayerWeights(w, device)
-        w_in = np.concatenate([w["w_qkv"], w["w_z"], w["w_b"], w["w_a"]], axis=0)
-        self.w_in = bf16_to_device(w_in, device)
-        self.w_out = bf16_to_device(w["w_out"], device)
         self.pre_w = bf16_to_device(w["pre_w"], device)
-        self.c = abi.GdnMixerWeightsC(self.step.c, self.w_in.data_ptr(), self.w_out.data_ptr(), self.pre_w.data_ptr())
+        self.w_in = self.w_out = self.w_in_tiles = self.w_out_tiles = self.w_in_q4 = self.w_out_q4 = None
+        if q4 is not None:
+            self.w_in_q4 = q4_to_device(*q4[0], device)
+            self.w_out_q4 = q4_to_device(*q4[1], device)
+        else:
+            w_in = np.concatenate([w["w_qkv"], w["w_z"], w["w_b"], w["w_a"]], axis=0)
+            self.w_in = bf16_to_device(w_in, device)
+            self.w_out = bf16_to_device(w["w_out"], device)
+            if tiled:
+                self.w_in_tiles = tile_weight(self.w_in)
+                self.w_out_tiles = tile_weight(self.w_out)
+
+        def p(t):
+            return t.data_ptr() if t is not None else None
+
+        self.c = abi.GdnMixerWeightsC(self.step.c, p(self.w_in), p(self.w_out), self.pre_w.data_ptr(),
+                                      p(self.w_in_tiles), p(self.w_out_tiles), p(self.w_in_q4), p(self.w_out_q4))
+
+
+def merged_in_proj(w: dict) -> np.ndarray:
+    """The merged in-projection rows [qkv | z | b | a] of a synthetic weight dict."""
+    return np.concatenate([w["w_qkv"], w["w_z"], w["w_b"], w["w_a"]], axis=0)
 
 
 class StatePool:
@@ -200,6 +247,17 @@ class StatePool:
         """y = x @ w.T (bf16, f32 accumulation): x [M, K], w [N, K], y [M, N] device tensors."""
         abi.call("gdn_linear", self.h, x.shape[0], w.shape[0], w.shape[1], _ptr(x), x.stride(0), _ptr(w), _ptr(y),
                  y.stride(0), _stream(stream))
+
+    def linear_tiled(self, x, w_tiles, n_out: int, y, stream=None):
+        """y = x @ w.T on the weight-streaming kernel, w given as its tiled copy (tile_weight):
+        x [M, K], y [M, n_out] device bf16."""
+        abi.call("gdn_linear_tiled", self.h, x.shape[0], n_out, x.shape[1], _ptr(x), x.stride(0), _ptr(w_tiles),
+                 _ptr(y), y.stride(0), _stream(stream))
+
+    def linear_q4(self, x, w_q4_tiles, n_out: int, y, stream=None):
+        """y = x @ dequant(w).T, w an MLX 4-bit weight given as its tiled copy (tile_weight_q4)."""
+        abi.call("gdn_linear_q4", self.h, x.shape[0], n_out, x.shape[1], _ptr(x), x.stride(0), _ptr(w_q4_tiles),
+                 _ptr(y), y.stride(0), _stream(stream))
 
     def mixer_step(self, layer: int, w: MixerWeights, x, y, slot_ids, cu_seqlens, n_tokens: int, stream=None):
         """Whole mixer layer: y = out_proj(step(in_proj(x))); x, y [N, hidden] device bf16."""

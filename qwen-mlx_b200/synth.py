@@ -149,6 +149,31 @@ def layer_weights(cfg: GdnConfig, layer: int, with_proj: bool = True) -> dict:
     return w
 
 
+def quantize_q4(w: np.ndarray, group: int = 64):
+    """Affine 4-bit quantization of a bf16 weight [N, K] in groups of `group` columns, in the format of
+    MLX's quantize (bits 4; the reference quantizes its projections this way, qwen3_5.rs:929-935):
+    weight ~= scale * q + bias with q in 0..15.  Per group: scale = (max - min) / 15 and bias = min,
+    both rounded to bf16, then q = clip(round((w - bias) / scale), 0, 15).  (Checkpoints arrive already
+    quantized; only the dequantization, scale * q + bias, has to agree with the reference.)
+
+    Returns (w_q [N, K/8] uint32 with column k in bits 4*(k%8) of word k/8, scales, biases [N, K/group]
+    bf16)."""
+    N, K = w.shape
+    assert K % group == 0 and group % 8 == 0
+    g = bf16_to_f32(w).astype(np.float64).reshape(N, K // group, group)
+    lo, hi = g.min(axis=2), g.max(axis=2)
+    scales = f32_to_bf16(((hi - lo) / 15.0).astype(np.float32))
+    biases = f32_to_bf16(lo.astype(np.float32))
+    s = bf16_to_f32(scales).astype(np.float64)[:, :, None]
+    b = bf16_to_f32(biases).astype(np.float64)[:, :, None]
+    q = np.where(s > 0, np.rint((g - b) / np.where(s > 0, s, 1.0)), 0.0)
+    q = np.clip(q, 0, 15).astype(np.uint32).reshape(N, K // 8, 8)
+    w_q = np.zeros((N, K // 8), np.uint32)
+    for e in range(8):
+        w_q |= q[:, :, e] << np.uint32(4 * e)
+    return w_q, scales, biases
+
+
 def step_inputs(cfg: GdnConfig, n_tokens: int, seed: int = 0, tag: str = "") -> dict:
     """Projection outputs feeding one fused layer step: qkv [N,D], z [N,Hv*dv], ab [N,2Hv] (b then a)."""
     return {
