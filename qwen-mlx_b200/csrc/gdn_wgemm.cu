@@ -34,7 +34,8 @@
 // Roles: warp 0 lane 0 streams the weight (bulk copies; the first ring's worth is issued before the
 // wait on the previous kernel, since the weight does not depend on it); warp 1 lane 0 issues the
 // MMAs; warps 2-5 drain the accumulator (TMEM lane quarter w%4) and store; the loader warps (4 groups
-// of 1 warp for bf16, of 2 warps for 4-bit below 64 tokens; group g takes units g, g+4, ...) copy each
+// of 1 warp for bf16; for 4-bit, 8 groups of 2 warps at 16 tokens, 4 of 2 at 32, 4 of 1 at 64; group g
+// takes units g, g+NG, ...) copy each
 // unit's token chunk into the stage with plain loads (and dequantize a 4-bit unit), fence the writes
 // for the tensor core and signal.
 // Every wait is bounded (2 s): a timeout sets ERR_TIMEOUT and the CTA winds down.
@@ -67,7 +68,7 @@ struct WgShape {
     // unit i - NQ of a slot was the same group's), and the ring depth a multiple of PL (a lane's last
     // DEPTH/PL copies never share a slot, so its drain waits the right phases).
     static constexpr int PL = Q4 ? 8 : 4;
-    static constexpr int NG = 4;
+    static constexpr int NG = (Q4 && MP == 16) ? 8 : 4;
     static constexpr int WPU = (Q4 && MP < 64) ? 2 : 1;
     static constexpr int NL = NG * WPU;                     // loader warps
     static constexpr int THREADS = 32 * (6 + NL);
@@ -76,7 +77,10 @@ struct WgShape {
     static constexpr int SMEM_MAX = 227 * 1024 - 1024;      // rings + barriers
     static constexpr int NQ = Q4 ? 16 : 0;                 // 4-bit staging ring (a multiple of PL and NG)
     static constexpr int NST_FIT = (SMEM_MAX - 1024 - NQ * WQ_TILE) / STG;
-    static constexpr int NST = Q4 ? (NST_FIT > 8 ? 8 : NST_FIT) : (NST_FIT > 12 ? 12 : NST_FIT) / PL * PL;
+    static constexpr int NST = Q4 ? (NST_FIT > 8 ? 8 : NST_FIT) / 2 * 2 : (NST_FIT > 12 ? 12 : NST_FIT) / PL * PL;
+    // One tcgen05.commit (hundreds of cycles) frees a group of G consecutive stages: stage s's "free"
+    // barrier is empty[s / G], completed once per pass over the ring.
+    static constexpr int G = (NST % 4 == 0) ? 4 : 2;
     static constexpr int OFF_Q = NST * STG;
     static constexpr int OFF_BARS = OFF_Q + NQ * WQ_TILE;
     // wfull/xfull/empty [NST], qfull/qempty [NQ], acc full x2, acc empty x2, done
@@ -91,6 +95,7 @@ struct WgShape {
     static_assert(!Q4 || NST >= 6, "4-bit stage ring too shallow");
     static_assert(NST >= 8 || Q4, "bf16 ring too shallow");
     static_assert(NG <= NST && (Q4 ? (NQ % NG == 0 && NQ % PL == 0) : (NST % PL == 0)), "ring sizes");
+    static_assert(NST % G == 0, "stage groups");
 };
 
 struct WgArgs {
@@ -152,31 +157,23 @@ __device__ __forceinline__ int wg_cta_of(int u, int U, int G) {
     return (int)((unsigned)((u + 1) * G + U - 1) / (unsigned)U) - 1;
 }
 
-// Bounded mbarrier wait whose polls let the hardware suspend the thread until the phase completes (up
-// to a 1 us hint per poll), so waiting warps do not compete for issue slots and the barrier unit.
-__device__ __forceinline__ bool wg_wait(uint64_t* bar, uint32_t parity) {
+// Bounded mbarrier wait: one plain test, then polls spaced by `sleep_ns` of __nanosleep, so waiting
+// warps leave the schedulers to the warps on the critical path (the MMA issuer polls without sleeping).
+__device__ __forceinline__ bool wg_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 0) {
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        uint32_t ok;
-        asm volatile(
-            "{\n"
-            " .reg .pred p;\n"
-            " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-            " selp.u32 %0, 1, 0, p;\n"
-            "}\n"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
-            : "memory");
-        if (ok) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if (global_timer_ns() - t0 > WG_WAIT_NS) return false;
+        if (sleep_ns) __nanosleep(sleep_ns);
     }
 }
 
 // The same wait for a whole warp: lane 0 polls, the warp gets its answer (one poller per warp keeps
 // the barrier unit free for the copies and arrivals on the critical path).  Warp-uniform call.
-__device__ __forceinline__ bool wg_wait_warp(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool wg_wait_warp(uint64_t* bar, uint32_t parity, uint32_t sleep_ns) {
     bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wg_wait(bar, parity);
+    if ((threadIdx.x & 31) == 0) ok = wg_wait(bar, parity, sleep_ns);
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
@@ -283,7 +280,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
         for (int s = 0; s < S::NST; ++s) {
             mbar_init(&wfull[s], 1);
             mbar_init(&xfull[s], S::WPU);
-            mbar_init(&empty[s], 1);
+            if (s % S::G == 0) mbar_init(&empty[s / S::G], 1);
         }
         for (int s = 0; s < S::NQ; ++s) {
             mbar_init(&qfull[s], 1);
@@ -314,7 +311,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
             int i = lane, last = -1;
             for (; i < (int)n_units; i += S::PL, pos.advance(S::PL, a)) {
                 const int s = i % DEPTH;
-                if (i >= DEPTH && !wg_wait(&freed[s], ((uint32_t)(i / DEPTH) & 1u) ^ 1u)) {
+                if (i >= DEPTH && !wg_wait(&freed[Q4 ? s : s / S::G], ((uint32_t)(i / DEPTH) & 1u) ^ 1u, 32)) {
                     atomicOr(a.err, ERR_TIMEOUT);
                     *s_abort = 1;
                 }
@@ -328,7 +325,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
             // No copy may still be landing when the CTA exits (only after a timeout can one be unconsumed):
             // this lane's last DEPTH/PL copies, whose slots no later copy has reused.
             for (int j = last; j >= 0 && j > last - DEPTH; j -= S::PL)
-                wg_wait(&landed[j % DEPTH], (uint32_t)(j / DEPTH) & 1u);
+                wg_wait(&landed[j % DEPTH], (uint32_t)(j / DEPTH) & 1u, 64);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -365,7 +362,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
                     for (int ks = 0; ks < 4; ++ks)
                         umma_bf16(d + (uint32_t)((ks % S::NCH) * MP), ad + (uint64_t)ks * (256u >> 4),
                                   bd + (uint64_t)ks * ((MP * 32u) >> 4), idesc, (j > 0 || ks >= S::NCH) ? 1u : 0u);
-                    umma_commit(&empty[s]);
+                    if (s % S::G == S::G - 1) umma_commit(&empty[s / S::G]);  // frees stages s-G+1 .. s
                 }
                 if (bad) {
                     atomicOr(a.err, ERR_TIMEOUT);
@@ -393,7 +390,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
             const int kt0 = (int)(u % KT);
             const int len = min(KT - kt0, ub - u);
             const int ab = seg & 1;
-            const bool bad = !wg_wait_warp(&accf[ab], (uint32_t)(seg >> 1) & 1u);
+            const bool bad = !wg_wait_warp(&accf[ab], (uint32_t)(seg >> 1) & 1u, 256);
             if (bad) {
                 atomicOr(a.err, ERR_TIMEOUT);
                 *s_abort = 1;
@@ -510,7 +507,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
         for (int i = grp; i < n_units; i += S::NG, pos.advance(S::NG, a)) {
             const int s = i % S::NST;
             bool bad = false;
-            if (i >= S::NST) bad = !wg_wait_warp(&empty[s], ((uint32_t)(i / S::NST) & 1u) ^ 1u);
+            if (i >= S::NST) bad = !wg_wait_warp(&empty[s / S::G], ((uint32_t)(i / S::NST) & 1u) ^ 1u, 64);
             if (bad) {
                 atomicOr(a.err, ERR_TIMEOUT);
                 *s_abort = 1;
@@ -519,7 +516,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
             uint8_t* stg = smem + s * S::STG;
             if constexpr (Q4) {
                 const int qs = i % S::NQ;
-                bad = !wg_wait_warp(&qfull[qs], (uint32_t)(i / S::NQ) & 1u);
+                bad = !wg_wait_warp(&qfull[qs], (uint32_t)(i / S::NQ) & 1u, 64);
                 if (bad) {
                     atomicOr(a.err, ERR_TIMEOUT);
                     *s_abort = 1;
