@@ -148,6 +148,15 @@ class MixerWeights:
                                       p(self.w_in_tiles), p(self.w_out_tiles), p(self.w_in_q4), p(self.w_out_q4))
 
 
+def load_mixer_weights(model_dir, device, tiled: bool = False):
+    """(GDN shapes, linear-layer indices, [MixerWeights]) of a checkpoint directory in the reference's layout
+    (loader.load_gdn_layers): 4-bit projections for a quantized checkpoint, bf16 otherwise."""
+    from . import loader
+    cfg, layers, ws = loader.load_gdn_layers(model_dir)
+    mws = [MixerWeights(w, device, tiled=tiled, q4=(w["q4_in"], w["q4_out"]) if "q4_in" in w else None) for w in ws]
+    return cfg, layers, mws
+
+
 def merged_in_proj(w: dict) -> np.ndarray:
     """The merged in-projection rows [qkv | z | b | a] of a synthetic weight dict."""
     return np.concatenate([w["w_qkv"], w["w_z"], w["w_b"], w["w_a"]], axis=0)
