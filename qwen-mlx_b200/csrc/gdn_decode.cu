@@ -64,6 +64,20 @@ __device__ __forceinline__ void unpack_w4(uint2 wu, float (&w)[4]) {
     w[3] = __uint_as_float(wu.y & 0xffff0000u);
 }
 
+// nn::silu for the prefill tiles: sigmoid from the fast exponential and divide intrinsics (a few ulp in f32).
+// The result is rounded to bf16, so it can differ from silu_bf only when the f32 value lies within a few ulp
+// of a bf16 rounding boundary (about 1 output in 10^4, by one bf16 ulp).
+__device__ __forceinline__ float silu_bf_fast(float x) { return rbf(x * __fdividef(1.0f, 1.0f + __expf(-x))); }
+
+// silu(sum_j w[j] * x[j]) with the conv1d (f32) rounding, fast SiLU (prefill tiles).
+__device__ __forceinline__ float conv_silu_fast(const float (&x)[4], const float (&w)[4]) {
+    float acc = x[0] * w[0];
+    acc = acc + x[1] * w[1];
+    acc = acc + x[2] * w[2];
+    acc = acc + x[3] * w[3];
+    return silu_bf_fast(rbf(acc));
+}
+
 // silu(sum_j w[j] * x[j]) with the reference's decode (bf16 products + bf16 sum) or conv1d (f32) rounding.
 __device__ __forceinline__ float conv_silu(const float (&x)[4], const float (&w)[4], bool decode) {
     float acc;
@@ -275,14 +289,19 @@ __device__ __forceinline__ void prep_tile_tokens(const PrepArgs& a, int ch, bool
                 float x0[4], x1[4];
 #pragma unroll
                 for (int p = 0; p < KC; ++p) unpack_pair(tap[p], x0[p], x1[p]);
-                o0 = conv_silu(x0, w[0], decode);
-                o1 = conv_silu(x1, w[1], decode);
+                if (SIMPLE) {
+                    o0 = conv_silu_fast(x0, w[0]);
+                    o1 = conv_silu_fast(x1, w[1]);
+                } else {
+                    o0 = conv_silu(x0, w[0], decode);
+                    o1 = conv_silu(x1, w[1], decode);
+                }
                 if (!is_qk) *reinterpret_cast<uint32_t*>(vrec + (size_t)j * REC_BYTES) = pack_pair(o0, o1);
             }
             if (z_ok) {
                 const uint32_t zp = s_z[j][tid >> 1];
                 const float zv = __uint_as_float((tid & 1) ? (zp & 0xffff0000u) : (zp << 16));
-                *reinterpret_cast<uint16_t*>(zrec + (size_t)j * REC_BYTES) = f2bf(silu_bf(zv));
+                *reinterpret_cast<uint16_t*>(zrec + (size_t)j * REC_BYTES) = f2bf(SIMPLE ? silu_bf_fast(zv) : silu_bf(zv));
             }
         }
         if (is_qk) {
