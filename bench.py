@@ -41,7 +41,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "GDN-stack decode tok/s at B=1..2048 over 1/2/4/8 B200; % HBM roofline"
 UNIT = "tok/s"
 N_LAYERS = 30
-E2E_GROUP = 5            # layers per host<->device copy in the e2e step
+E2E_GROUPS = "1,7,7,7,7,1"   # layers per host<->device copy group in the e2e step (sums to the layer count)
 # Algorithmic bytes of one fused decode layer step (per sequence, and per launch constant):
 #   state f32 r+w 2*32*128*128*4 + conv bf16 r+w 2*3*8192*2 + qkv 8192*2 + z 4096*2 + a,b 64*2 + out 4096*2
 BYTES_PER_SEQ_LAYER = 2 * 32 * 128 * 128 * 4 + 2 * 3 * 8192 * 2 + 8192 * 2 + 4096 * 2 + 64 * 2 + 4096 * 2
@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--no-mixer", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-mixed", action="store_true")
+    p.add_argument("--e2e-groups", default=E2E_GROUPS,
+                   help="layers per host<->device copy group of the e2e step, comma separated")
     p.add_argument("--prefill-only", action="store_true",
                    help="run only the chunked-prefill leg and print its result (profiling of that leg)")
     p.add_argument("--prefill-lens", default=None,
@@ -674,10 +676,11 @@ def run_ours(args):
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region.
     # Every step copies each layer's projection outputs in and each layer's output back.  The copies run on
-    # two copy streams in groups of E2E_GROUP layers: group g's input copy gates group g's steps and its output
-    # copy follows them, so the host link overlaps the compute (one CUDA graph per step).  Groups of 5 cost
-    # less than per-layer copies: each copy has a fixed cost of a few us and each cross-stream edge interrupts
-    # the programmatic launch overlap of consecutive steps.
+    # two copy streams in groups of layers (--e2e-groups): group g's input copy gates group g's steps and its
+    # output copy follows them, so the host link overlaps the compute (one CUDA graph per step).  A one-layer
+    # first group lets the compute start after one layer's input; a one-layer last group leaves one layer's
+    # output to drain; the groups in between are large because each copy has a fixed cost of a few us and each
+    # cross-stream edge interrupts the programmatic launch overlap of consecutive steps.
     in_host = torch.empty((N_LAYERS, B, PROJ_LD), dtype=torch.bfloat16).pin_memory()
     in_host.copy_(proj_h.cpu())
     out_host = torch.empty((N_LAYERS, B, cfg.z_dim), dtype=torch.bfloat16).pin_memory()
@@ -685,7 +688,11 @@ def run_ours(args):
     d2h = torch.cuda.Stream(device=dev)
     ios_e = [make_io(proj_h, out_h, l) for l in range(N_LAYERS)]
     wcs_e = [lw.c for lw in lws]
-    groups = [(a, min(a + E2E_GROUP, N_LAYERS)) for a in range(0, N_LAYERS, E2E_GROUP)]
+    sizes = [int(v) for v in args.e2e_groups.split(",")]
+    if sum(sizes) != N_LAYERS or min(sizes) < 1:
+        raise SystemExit(f"--e2e-groups must be positive sizes summing to {N_LAYERS}")
+    starts = np.cumsum([0] + sizes)
+    groups = [(int(starts[i]), int(starts[i + 1])) for i in range(len(sizes))]
 
     def e2e_body():
         ev_in = [torch.cuda.Event() for _ in groups]
