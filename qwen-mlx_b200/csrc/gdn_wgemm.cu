@@ -28,16 +28,15 @@
 //
 // MMA: tcgen05 kind::f16, the weight slab as A (M = 128; rows past the slab are ignored), the tokens
 // as B (N = MP = 16/32/64 padded tokens, K-major, column-first: LBO MP*16 B, SBO 128 B); the f32
-// accumulator [128 rows][MP tokens] lives in TMEM, split over 2-4 independent chains (so the small
-// MMAs of a unit do not serialise on one accumulator) and double-buffered.
+// accumulators [128 rows][MP tokens] (one set per issuer) live in TMEM, double-buffered.
 //
-// Roles: warp 0 lane 0 streams the weight (bulk copies; the first ring's worth is issued before the
-// wait on the previous kernel, since the weight does not depend on it); warp 1 lane 0 issues the
-// MMAs; warps 2-5 drain the accumulator (TMEM lane quarter w%4) and store; the loader warps (4 groups
-// of 1 warp for bf16; for 4-bit, 8 groups of 2 warps at 16 tokens, 4 of 2 at 32, 4 of 1 at 64; group g
-// takes units g, g+NG, ...) copy each
-// unit's token chunk into the stage with plain loads (and dequantize a 4-bit unit), fence the writes
-// for the tensor core and signal.
+// Roles: warp 0 streams the weight (bulk copies from several lanes; the first ring's worth is issued
+// before the wait on the previous kernel, since the weight does not depend on it); warps 1 and 6 (lane
+// 0) issue the MMAs of the even / odd units into two accumulator sets; warps 2-5 drain the accumulators
+// (TMEM lane quarter w%4) and store; the loader warps (from warp 7: 4 groups of 1 warp for bf16; for
+// 4-bit, 8 groups of 2 warps at 16 tokens, 4 of 2 at 32, 4 of 1 at 64; group g takes units g, g+NG, ...)
+// copy each unit's token chunk into the stage with plain loads (and dequantize a 4-bit unit), fence the
+// writes for the tensor core and signal.
 // Every wait is bounded (2 s): a timeout sets ERR_TIMEOUT and the CTA winds down.
 #include <cuda_runtime.h>
 
@@ -71,7 +70,7 @@ struct WgShape {
     static constexpr int NG = (Q4 && MP == 16) ? 8 : 4;
     static constexpr int WPU = (Q4 && MP < 64) ? 2 : 1;
     static constexpr int NL = NG * WPU;                     // loader warps
-    static constexpr int THREADS = 32 * (6 + NL);
+    static constexpr int THREADS = 32 * (7 + NL);           // + producer, 2 MMA issuers, 4 epilogue warps
     static constexpr int XB = MP * WG_K * 2;                // token chunk of one stage
     static constexpr int STG = WG_TILE + XB;                // one MMA stage (weight tile + tokens)
     static constexpr int SMEM_MAX = 227 * 1024 - 1024;      // rings + barriers
@@ -83,19 +82,18 @@ struct WgShape {
     static constexpr int G = (NST % 4 == 0) ? 4 : 2;
     static constexpr int OFF_Q = NST * STG;
     static constexpr int OFF_BARS = OFF_Q + NQ * WQ_TILE;
-    // wfull/xfull/empty [NST], qfull/qempty [NQ], acc full x2, acc empty x2, done
-    static constexpr int N_BARS = 3 * NST + 2 * NQ + 5;
+    // wfull/xfull/empty [NST], qfull/qempty [NQ], acc full x2, acc empty x2, done x2
+    static constexpr int N_BARS = 3 * NST + 2 * NQ + 6;
     static constexpr int SMEM = OFF_BARS + N_BARS * 8 + 16;
-    // The 4 k-steps of a unit accumulate into NCH independent TMEM accumulators (k-step ks into chain
-    // ks % NCH), so consecutive MMAs do not wait on each other's result; the epilogue adds the chains.
-    static constexpr int NCH = MP <= 32 ? 4 : 2;
-    static constexpr int ACC_COLS = NCH * MP;               // one accumulator buffer
-    static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double-buffered: 128 or 256 columns
+    // Two MMA issuers (units of even / odd index) accumulate into their own f32 set [128][MP]; one
+    // accumulator buffer holds both sets, double-buffered: 64 / 128 / 256 TMEM columns.
+    static constexpr int ACC_COLS = 2 * MP;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert(!Q4 || NST >= 6, "4-bit stage ring too shallow");
     static_assert(NST >= 8 || Q4, "bf16 ring too shallow");
     static_assert(NG <= NST && (Q4 ? (NQ % NG == 0 && NQ % PL == 0) : (NST % PL == 0)), "ring sizes");
-    static_assert(NST % G == 0, "stage groups");
+    static_assert(NST % G == 0 && G % 2 == 0, "stage groups (each issuer commits once per group)");
 };
 
 struct WgArgs {
@@ -266,7 +264,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
     uint64_t* accf = qempty + S::NQ;
     uint64_t* acce = accf + 2;
     uint64_t* done = acce + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_last = s_abort + 1;
 
@@ -280,17 +278,18 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
         for (int s = 0; s < S::NST; ++s) {
             mbar_init(&wfull[s], 1);
             mbar_init(&xfull[s], S::WPU);
-            if (s % S::G == 0) mbar_init(&empty[s / S::G], 1);
+            if (s % S::G == 0) mbar_init(&empty[s / S::G], 2);  // one commit per issuer
         }
         for (int s = 0; s < S::NQ; ++s) {
             mbar_init(&qfull[s], 1);
             mbar_init(&qempty[s], S::WPU);
         }
-        mbar_init(&accf[0], 1);
-        mbar_init(&accf[1], 1);
+        mbar_init(&accf[0], 2);
+        mbar_init(&accf[1], 2);
         mbar_init(&acce[0], 128);
         mbar_init(&acce[1], 128);
-        mbar_init(done, 1);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -328,14 +327,17 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
                 wg_wait(&landed[j % DEPTH], (uint32_t)(j / DEPTH) & 1u, 64);
         }
         __syncwarp();
-    } else if (warp == 1) {
-        // ---------------------------------------------------------------- MMA issue
+    } else if (warp == 1 || warp == 6) {
+        // ---------------------------------------------------------------- MMA issue: issuer p takes the
+        // units of index parity p (one thread's MMA issue and barrier tests cost more per unit than the
+        // tensor core needs, so two issuers share the stream) into its own accumulator set.
+        const int p = warp == 1 ? 0 : 1;
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_bf16(128, MP);
             int i = 0;
             int seg = 0;
             for (int u = ua; u < ub && !*s_abort; ++seg) {
-                const int kt0 = (int)(u % KT);
+                const int kt0 = u % KT;
                 const int len = min(KT - kt0, ub - u);
                 const int ab = seg & 1;
                 if (seg >= 2 && !wg_wait(&acce[ab], (uint32_t)((seg >> 1) - 1) & 1u)) {
@@ -344,13 +346,13 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(ab * S::ACC_COLS);
-                bool bad = false;
+                const uint32_t d = tmem + (uint32_t)(ab * S::ACC_COLS + p * MP);
+                bool bad = false, first = true;
                 for (int j = 0; j < len; ++j, ++i) {
+                    if ((i & 1) != p) continue;
                     const int s = i % S::NST;
                     const uint32_t ph = (uint32_t)(i / S::NST) & 1u;
-                    if ((!Q4 && !wg_wait(&wfull[s], ph)) ||
-                        !wg_wait(&xfull[s], ph)) {
+                    if ((!Q4 && !wg_wait(&wfull[s], ph)) || !wg_wait(&xfull[s], ph)) {
                         bad = true;
                         break;
                     }
@@ -360,9 +362,11 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
                     const uint64_t bd = umma_desc_raw(sw + WG_TILE, (uint32_t)(MP * 16), 128u);
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(d + (uint32_t)((ks % S::NCH) * MP), ad + (uint64_t)ks * (256u >> 4),
-                                  bd + (uint64_t)ks * ((MP * 32u) >> 4), idesc, (j > 0 || ks >= S::NCH) ? 1u : 0u);
-                    if (s % S::G == S::G - 1) umma_commit(&empty[s / S::G]);  // frees stages s-G+1 .. s
+                        umma_bf16(d, ad + (uint64_t)ks * (256u >> 4), bd + (uint64_t)ks * ((MP * 32u) >> 4), idesc,
+                                  (!first || ks > 0) ? 1u : 0u);
+                    first = false;
+                    // this issuer's last unit of the stage group: its share of freeing the group
+                    if (s % S::G == S::G - 2 + p) umma_commit(&empty[s / S::G]);
                 }
                 if (bad) {
                     atomicOr(a.err, ERR_TIMEOUT);
@@ -372,8 +376,8 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
                 umma_commit(&accf[ab]);
                 u += len;
             }
-            umma_commit(done);  // arrives once every MMA issued above has completed
-            if (!wg_wait(done, 0)) atomicOr(a.err, ERR_TIMEOUT);
+            umma_commit(&done[p]);  // arrives once every MMA this issuer issued has completed
+            if (!wg_wait(&done[p], 0)) atomicOr(a.err, ERR_TIMEOUT);
         }
         __syncwarp();
     } else if (warp < 6) {
@@ -397,20 +401,19 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
             }
             if (named_bar_or(1, 128, bad || *s_abort)) break;
             tc_fence_after();
+            // set p holds the units of index parity p; a one-unit segment has only one of them
+            const int i0 = u - ua;
+            const bool has0 = len >= 2 || (i0 & 1) == 0, has1 = len >= 2 || (i0 & 1) == 1;
             float acc[MP];
 #pragma unroll
-            for (int j = 0; j < MP; j += 16) {
-                float v[16];
-                tmem_ld16(trow + (uint32_t)(ab * S::ACC_COLS + j), v);
+            for (int m = 0; m < MP; ++m) acc[m] = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) acc[j + e] = v[e];
-            }
-#pragma unroll
-            for (int c = 1; c < S::NCH; ++c) {  // chains added in a fixed order
+            for (int p = 0; p < 2; ++p) {  // sets added in a fixed order
+                if (p == 0 ? !has0 : !has1) continue;
 #pragma unroll
                 for (int j = 0; j < MP; j += 16) {
                     float v[16];
-                    tmem_ld16(trow + (uint32_t)(ab * S::ACC_COLS + c * MP + j), v);
+                    tmem_ld16(trow + (uint32_t)(ab * S::ACC_COLS + p * MP + j), v);
 #pragma unroll
                     for (int e = 0; e < 16; ++e) acc[j + e] += v[e];
                 }
@@ -486,7 +489,7 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
         }
     } else {
         // ---------------------------------------------------------------- loader warps
-        const int lw = warp - 6, grp = lw / S::WPU, half = lw % S::WPU;
+        const int lw = warp - 7, grp = lw / S::WPU, half = lw % S::WPU;
         pdl_wait();  // the tokens are the previous kernel's output
         constexpr int XPL = MP / (4 * S::WPU);  // 16-byte token chunks per lane per unit
         // token chunk of this warp's share of unit (k-tile kt), loaded into registers one unit ahead
