@@ -41,6 +41,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "GDN-stack decode tok/s at B=1..2048 over 1/2/4/8 B200; % HBM roofline"
 UNIT = "tok/s"
 N_LAYERS = 30
+# The layers of a step share its routing tables: layers 2..30 tell the step so (GDN_STEP_TABLES_STABLE), and
+# it reads its routing and conv windows while the previous layer's kernel is still running.
+STABLE = 1
 E2E_GROUPS = "1,7,7,7,7,1"   # layers per host<->device copy group in the e2e step (sums to the layer count)
 # Algorithmic bytes of one fused decode layer step (per sequence, and per launch constant):
 #   state f32 r+w 2*32*128*128*4 + conv bf16 r+w 2*3*8192*2 + qkv 8192*2 + z 4096*2 + a,b 64*2 + out 4096*2
@@ -426,10 +429,11 @@ def run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, w
         with torch.cuda.stream(stream):
             tab_d.copy_(tab_h, non_blocking=True)
             for l in range(N_LAYERS):
-                rc = lib.gdn_layer_step(mpool.h, l, C.byref(lws[l].c), C.byref(ios[l]), C.c_void_p(tab_d.data_ptr()),
-                                        C.c_void_p(tab_d.data_ptr() + (n_live + 1) * 4), n, int(cu[-1]), sp)
+                rc = lib.gdn_layer_step_ex(mpool.h, l, C.byref(lws[l].c), C.byref(ios[l]),
+                                           C.c_void_p(tab_d.data_ptr()), C.c_void_p(tab_d.data_ptr() + (n_live + 1) * 4),
+                                           n, int(cu[-1]), STABLE if l else 0, sp)
                 if rc:
-                    abi.check(rc, "gdn_layer_step")
+                    abi.check(rc, "gdn_layer_step_ex")
         stream.synchronize()   # the pinned table buffer is reused by the next step
 
     for k in range(warm):
@@ -481,10 +485,10 @@ def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier,
     def step():
         pool.reset(slots_h, stream)                     # prompts start from a zero state
         for l in range(N_LAYERS):
-            rc = lib.gdn_layer_step(pool.h, l, C.byref(lws[l].c), C.byref(io), C.c_void_p(slots.data_ptr()),
-                                    C.c_void_p(cu.data_ptr()), len(lens), N, sp)
+            rc = lib.gdn_layer_step_ex(pool.h, l, C.byref(lws[l].c), C.byref(io), C.c_void_p(slots.data_ptr()),
+                                       C.c_void_p(cu.data_ptr()), len(lens), N, STABLE if l else 0, sp)
             if rc:
-                abi.check(rc, "gdn_layer_step")
+                abi.check(rc, "gdn_layer_step_ex")
 
     with torch.cuda.stream(stream):
         step()
@@ -584,9 +588,10 @@ def run_ours(args):
 
         def step():
             for l in range(N_LAYERS):
-                rc = lib.gdn_layer_step(pool.h, l, C.byref(wcs[l]), C.byref(ios[l]), sptr, cptr, b, b, sp)
+                rc = lib.gdn_layer_step_ex(pool.h, l, C.byref(wcs[l]), C.byref(ios[l]), sptr, cptr, b, b,
+                                           STABLE if l else 0, sp)
                 if rc:
-                    abi.check(rc, "gdn_layer_step")
+                    abi.check(rc, "gdn_layer_step_ex")
         return step
 
     def capture(b, proj, out):
@@ -706,10 +711,11 @@ def run_ours(args):
         for gi, (a, b) in enumerate(groups):
             stream.wait_event(ev_in[gi])
             for l in range(a, b):
-                rc = lib.gdn_layer_step(pool.h, l, C.byref(wcs_e[l]), C.byref(ios_e[l]),
-                                        C.c_void_p(slots_all.data_ptr()), C.c_void_p(cu_all.data_ptr()), B, B, sp)
+                rc = lib.gdn_layer_step_ex(pool.h, l, C.byref(wcs_e[l]), C.byref(ios_e[l]),
+                                           C.c_void_p(slots_all.data_ptr()), C.c_void_p(cu_all.data_ptr()), B, B,
+                                           STABLE if l else 0, sp)
                 if rc:
-                    abi.check(rc, "gdn_layer_step")
+                    abi.check(rc, "gdn_layer_step_ex")
             ev_out[gi].record(stream)
             d2h.wait_event(ev_out[gi])
             with torch.cuda.stream(d2h):
@@ -790,7 +796,8 @@ def run_ours(args):
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32 state, bf16 io", "data": "synthetic",
                 "config": {"workload": f"config2: 30-layer GDN stack, batched S=1 decode, B={B} per GPU",
                            "batch_per_gpu": B, "layers": N_LAYERS, "parallelism": f"slot-range shards x{world}",
-                           "timed_step": "30 fused gdn_layer_step launches (CUDA graph); projections not included",
+                           "timed_step": "30 fused layer steps, gdn_layer_step_ex (layers 2-30 with GDN_STEP_TABLES_STABLE), "
+                                        "one CUDA graph; projections not included",
                            "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
                                N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,

@@ -157,6 +157,18 @@ GDN_API int gdn_layer_step(gdn_pool* pool, int32_t layer, const gdn_layer_weight
                    const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens,
                    void* stream);
 
+/* gdn_layer_step with flags.  GDN_STEP_TABLES_STABLE: the routing tables were already used by
+ * an earlier GDN call of this step after they were last written, and the call before this one on
+ * the stream was for a different layer (typically layers 2..L of a step whose tables were uploaded
+ * before layer 1).  The step then reads its routing entries and conv windows while the preceding
+ * kernel is still running, and only the token inputs after it.  Same results as gdn_layer_step.
+ * (An executor feature of this library; the reference's per-layer call is gated_delta_kernel,
+ * metal_gdn.rs:170-218.) */
+#define GDN_STEP_TABLES_STABLE 1u
+GDN_API int gdn_layer_step_ex(gdn_pool* pool, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                              const int32_t* slot_ids, const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens,
+                              uint32_t flags, void* stream);
+
 /* Parameters of a whole mixer layer (GatedDeltaNet, qwen3_5.rs:466-503) and of its
  * decoder-layer input norm.  Device pointers.  w_in holds the four input
  * projections stacked by rows in the reference's merged order (qwen3_5.rs:1038-1047):

@@ -23,6 +23,8 @@ GDN_E_DEVICE = 7
 GDN_ENTRY_DECODE = 0
 GDN_ENTRY_PREFILL_FIRST = 1
 GDN_ENTRY_PREFILL_CONT = 2
+GDN_STEP_TABLES_STABLE = 1
+
 GDN_FINISH_EOS = 0
 GDN_FINISH_MAX_TOKENS = 1
 
@@ -82,6 +84,8 @@ SIGNATURES = {
     "gdn_pool_check": (_int, [_vp, C.POINTER(_i32), _int]),
     "gdn_layer_step": (_int, [_vp, _i32, C.POINTER(GdnLayerWeightsC), C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32,
                               _vp]),
+    "gdn_layer_step_ex": (_int, [_vp, _i32, C.POINTER(GdnLayerWeightsC), C.POINTER(GdnStepIOC), _vp, _vp, _i32,
+                                 _i32, C.c_uint32, _vp]),
     "gdn_linear": (_int, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp]),
     "gdn_weight_tile_bytes": (_i64, [_i32, _i32]),
     "gdn_weight_tile": (_int, [_i32, _i32, _vp, _vp, _vp]),

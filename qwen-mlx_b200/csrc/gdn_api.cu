@@ -390,8 +390,9 @@ static int check_common(gdn_pool* p, int32_t layer, const int32_t* slot_ids, con
     return GDN_OK;
 }
 
-int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
-                   const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, void* stream) {
+static int layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                      const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, uint32_t flags,
+                      void* stream) {
     int rc = check_common(p, layer, slot_ids, cu, n_seq, n_tokens);
     if (rc) return rc;
     if (!w || !w->conv_w || !w->A_log || !w->dt_bias || !w->norm_w) return fail(GDN_E_INVALID, "NULL layer weight");
@@ -424,6 +425,7 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     pa.rec = p->recs;
     pa.rec_cap = p->rec_cap;
     pa.err = p->err;
+    pa.tables_stable = (flags & GDN_STEP_TABLES_STABLE) ? 1 : 0;
     gdn::RecurArgs ra;
     std::memset(&ra, 0, sizeof ra);
     ra.rec = rec;
@@ -449,6 +451,18 @@ int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const
     if (e == cudaSuccess && has_long) e = gdn::launch_wy(ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");
     return ok();
+}
+
+int gdn_layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                   const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, void* stream) {
+    return layer_step(p, layer, w, io, slot_ids, cu, n_seq, n_tokens, 0u, stream);
+}
+
+int gdn_layer_step_ex(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, const gdn_step_io* io,
+                      const int32_t* slot_ids, const int32_t* cu, int32_t n_seq, int32_t n_tokens, uint32_t flags,
+                      void* stream) {
+    if (flags & ~(uint32_t)GDN_STEP_TABLES_STABLE) return fail(GDN_E_INVALID, "unknown flags 0x%x", flags);
+    return layer_step(p, layer, w, io, slot_ids, cu, n_seq, n_tokens, flags, stream);
 }
 
 static bool mixer_weights_ok(const gdn_mixer_weights* w) {
@@ -517,7 +531,9 @@ static int mixer_layer(gdn_pool* p, int32_t layer, const gdn_mixer_weights* w, c
     io.z = p->proj + p->D; io.ld_z = ldp;
     io.ab = p->proj + p->D + zd; io.ld_ab = ldp;
     io.out = p->gated; io.ld_out = zd;
-    rc = gdn_layer_step(p, layer, &w->step, &io, slot_ids, cu, n_seq, n_tokens, stream);
+    // The in-projection kernel stands between the caller's kernels and the step, and lets the step start
+    // only after everything before it has finished: the tables and this layer's conv state are settled.
+    rc = layer_step(p, layer, &w->step, &io, slot_ids, cu, n_seq, n_tokens, GDN_STEP_TABLES_STABLE, stream);
     if (rc) return rc;
     return projection(p, n_tokens, H, zd, p->gated, zd, w->w_out, w->w_out_tiles, w->w_out_q4, y, ld_y, s,
                       "out-projection");

@@ -111,10 +111,16 @@ __device__ __forceinline__ void load_taps(const PrepArgs& a, const uint16_t* cs,
 // v channels / z columns of the k-head's v-heads (Hv/Hk * 128 of each).
 // Loads are issued in two batches: everything indexed by the token (inputs, weights,
 // and the routing entries of the sequence the token belongs to when each sequence
-// has one token), then the slot's conv windows.
+// has one token), then the slot's conv windows.  With a.tables_stable (the routing tables were
+// complete before the preceding kernel started, and that kernel does not write this layer's conv
+// state) the routing, weight and window loads are issued before the wait on the preceding kernel,
+// which may still be running, and only the token inputs are read after it.
 __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
-    pdl_wait();
-    pdl_launch_dependents();
+    const bool early = a.tables_stable != 0;
+    if (!early) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
     __shared__ float s_red[8];
 
     const int n = blockIdx.x;
@@ -126,33 +132,41 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     const int qk_ch = (low ? 0 : a.hk * DK) + hk * DK + c;
     const int nv = ratio * DV;             // v channels of this k-head group
     const int v_idx0 = tid;                // first v channel handled by this thread (ratio <= 2: the only one)
-
-    // ---- batch 1: token-indexed loads (no dependence on the routing tables)
-    const int guess = n < a.n_seq ? n : a.n_seq - 1;
-    const int cu_g0 = __ldg(a.cu_seqlens + guess);
-    const int cu_g1 = __ldg(a.cu_seqlens + guess + 1);
-    const int slot_g = __ldg(a.slot_ids + guess);
-    const float x_qk = bf2f(a.qkv[(long long)n * a.ld_qkv + qk_ch]);
-    float w_qk[4];
-    unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)qk_ch * KC)), w_qk);
-    float x_v = 0.f, z_v = 0.f, w_v[4] = {0.f, 0.f, 0.f, 0.f};
     int v_ch = 0, v_hv = 0, v_c = 0;
     if (v_idx0 < nv) {
         v_hv = hk * ratio + v_idx0 / DV;
         v_c = v_idx0 % DV;
         v_ch = 2 * a.hk * DK + v_hv * DV + v_c;
-        x_v = bf2f(a.qkv[(long long)n * a.ld_qkv + v_ch]);
-        z_v = bf2f(a.z[(long long)n * a.ld_z + (long long)v_hv * DV + v_c]);
-        unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)v_ch * KC)), w_v);
     }
-    float gb_b = 0.f, gb_a = 0.f, gb_alog = 0.f, gb_dt = 0.f;
+
+    // ---- batch 1: routing guess, weights (and, unless early, the token's inputs)
+    const int guess = n < a.n_seq ? n : a.n_seq - 1;
+    const int cu_g0 = __ldg(a.cu_seqlens + guess);
+    const int cu_g1 = __ldg(a.cu_seqlens + guess + 1);
+    const int slot_g = __ldg(a.slot_ids + guess);
+    float w_qk[4];
+    unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)qk_ch * KC)), w_qk);
+    float w_v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (v_idx0 < nv) unpack_w4(__ldg(reinterpret_cast<const uint2*>(a.conv_w + (size_t)v_ch * KC)), w_v);
+    float gb_alog = 0.f, gb_dt = 0.f;
     if (tid < ratio) {
-        const int hv = hk * ratio + tid;
-        gb_b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
-        gb_a = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
-        gb_alog = a.A_log[hv];
-        gb_dt = a.dt_bias[hv];
+        gb_alog = a.A_log[hk * ratio + tid];
+        gb_dt = a.dt_bias[hk * ratio + tid];
     }
+    float x_qk = 0.f, x_v = 0.f, z_v = 0.f, gb_b = 0.f, gb_a = 0.f;
+    auto load_inputs = [&]() {
+        x_qk = bf2f(a.qkv[(long long)n * a.ld_qkv + qk_ch]);
+        if (v_idx0 < nv) {
+            x_v = bf2f(a.qkv[(long long)n * a.ld_qkv + v_ch]);
+            z_v = bf2f(a.z[(long long)n * a.ld_z + (long long)v_hv * DV + v_c]);
+        }
+        if (tid < ratio) {
+            const int hv = hk * ratio + tid;
+            gb_b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
+            gb_a = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
+        }
+    };
+    if (!early) load_inputs();
 
     // ---- routing
     int seq, slot;
@@ -177,10 +191,28 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     const bool decode = (T == 1);
     uint16_t* cs = a.conv + (size_t)slot * (KC - 1) * a.D;
 
-    // ---- batch 2: conv windows (and earlier tokens of a multi-token sequence)
+    // ---- batch 2: conv windows (a one-token sequence's taps are its window rows and its input)
     float xq[4], xv[4] = {0.f, 0.f, 0.f, 0.f};
-    load_taps(a, cs, qk_ch, t0, t, x_qk, xq);
-    if (v_idx0 < nv) load_taps(a, cs, v_ch, t0, t, x_v, xv);
+    if (decode) {
+#pragma unroll
+        for (int j = 0; j < KC - 1; ++j) xq[j] = bf2f(cs[(size_t)j * a.D + qk_ch]);
+        if (v_idx0 < nv) {
+#pragma unroll
+            for (int j = 0; j < KC - 1; ++j) xv[j] = bf2f(cs[(size_t)j * a.D + v_ch]);
+        }
+    }
+    if (early) {
+        pdl_wait();
+        pdl_launch_dependents();
+        load_inputs();
+    }
+    if (decode) {
+        xq[KC - 1] = x_qk;
+        xv[KC - 1] = x_v;
+    } else {
+        load_taps(a, cs, qk_ch, t0, t, x_qk, xq);
+        if (v_idx0 < nv) load_taps(a, cs, v_ch, t0, t, x_v, xv);
+    }
     if (decode) {
         // A one-token sequence: this thread is the only reader of these windows in this call,
         // so it shifts them in place (new window = last K-1 rows of [old window; x]).

@@ -52,6 +52,7 @@ struct PrepArgs {
     uint8_t* rec;                // scratch records [Hv][rec_cap][REC_BYTES]
     long long rec_cap;
     int32_t* err;
+    int32_t tables_stable;       // routing tables and this layer's conv state may be read before the PDL wait
 };
 
 struct RecurArgs {

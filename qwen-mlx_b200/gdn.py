@@ -239,12 +239,17 @@ class StatePool:
 
     # ---------------------------------------------------------------- compute
     def layer_step(self, layer: int, w: LayerWeights, qkv, z, ab, out, slot_ids, cu_seqlens, n_tokens: int,
-                   stream=None):
-        """Fused layer step; qkv/z/ab/out are [N, ld] device tensors, tables are device int32."""
+                   stream=None, flags: int = 0):
+        """Fused layer step; qkv/z/ab/out are [N, ld] device tensors, tables are device int32.  flags:
+        abi.GDN_STEP_TABLES_STABLE for the later layers of a step (gdn_layer_step_ex)."""
         io = abi.GdnStepIOC(qkv.data_ptr(), qkv.stride(0), z.data_ptr(), z.stride(0), ab.data_ptr(), ab.stride(0),
                             out.data_ptr(), out.stride(0))
-        abi.call("gdn_layer_step", self.h, layer, C.byref(w.c), C.byref(io), _ptr(slot_ids), _ptr(cu_seqlens),
-                 slot_ids.numel(), n_tokens, _stream(stream))
+        if flags:
+            abi.call("gdn_layer_step_ex", self.h, layer, C.byref(w.c), C.byref(io), _ptr(slot_ids), _ptr(cu_seqlens),
+                     slot_ids.numel(), n_tokens, flags, _stream(stream))
+        else:
+            abi.call("gdn_layer_step", self.h, layer, C.byref(w.c), C.byref(io), _ptr(slot_ids), _ptr(cu_seqlens),
+                     slot_ids.numel(), n_tokens, _stream(stream))
 
     def layer_step_raw(self, layer: int, w_c, io_c, slot_ptr, cu_ptr, n_seq, n_tokens, stream_ptr):
         """Same as layer_step with prebuilt ctypes arguments (no per-call Python allocation)."""

@@ -255,3 +255,54 @@ def test_device_bounds_check_skips_bad_slot(H, synth, oracle):
     assert h.pool.check() == 0          # cleared by the previous read
     ref = oracle.layer_step(cfg, h.w, inp["qkv"][:1], inp["z"][:1], inp["ab"][:1], conv0[:1], rec0[:1], cu[:2])
     assert rel_l2(synth.bf16_to_f32(out[:1]), synth.bf16_to_f32(ref[0])) < TOL
+
+
+@pytest.mark.parametrize("B", [8, 33])
+def test_stable_tables_flag_gives_identical_results(gdn, synth, B):
+    """gdn_layer_step_ex with GDN_STEP_TABLES_STABLE (layers 2..L of a step read routing and windows early)
+    computes exactly what gdn_layer_step computes: outputs and states byte-identical over a 4-layer,
+    3-step decode chain with scrambled slots."""
+    import importlib
+    abi = importlib.import_module("qwen_mlx_b200.abi")
+    cfg = synth.GdnConfig(n_layers=4)
+    rng = np.random.default_rng(11)
+    slots = rng.permutation(64)[:B].astype(np.int32)
+    cu = np.arange(B + 1, dtype=np.int32)
+    ws = [gdn.LayerWeights(synth.layer_weights(cfg, l, with_proj=False), DEV) for l in range(cfg.n_layers)]
+    conv0, rec0 = synth.random_states(cfg, B, seed=21, tag="stable")
+    results = []
+    for use_flag in (False, True):
+        outs = []
+        with gdn.StatePool(cfg, n_slots=64, device=0) as pool:
+            for l in range(cfg.n_layers):
+                for i in range(B):
+                    pool.import_(int(slots[i]), l, rec0[i], conv0[i])
+            sd, cd = torch.from_numpy(slots).to(DEV), torch.from_numpy(cu).to(DEV)
+            for step in range(3):
+                for l in range(cfg.n_layers):
+                    inp = synth.step_inputs(cfg, B, seed=70 + 10 * step + l, tag="stable")
+                    out = torch.empty((B, cfg.z_dim), dtype=torch.bfloat16, device=DEV)
+                    pool.layer_step(l, ws[l], gdn.bf16_to_device(inp["qkv"], DEV), gdn.bf16_to_device(inp["z"], DEV),
+                                    gdn.bf16_to_device(inp["ab"], DEV), out, sd, cd, B,
+                                    flags=abi.GDN_STEP_TABLES_STABLE if (use_flag and l > 0) else 0)
+                    outs.append(out)
+            torch.cuda.synchronize()
+            assert pool.check() == 0
+            st = [pool.export(int(s), l) for l in range(cfg.n_layers) for s in slots]
+        results.append(([gdn.bf16_to_host(o) for o in outs], st))
+    (o0, s0), (o1, s1) = results
+    assert all(np.array_equal(a, b) for a, b in zip(o0, o1))
+    assert all(np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) for a, b in zip(s0, s1))
+
+
+def test_layer_step_ex_rejects_unknown_flags(gdn, synth):
+    import importlib
+    abi = importlib.import_module("qwen_mlx_b200.abi")
+    cfg = synth.GdnConfig(n_layers=1)
+    w = gdn.LayerWeights(synth.layer_weights(cfg, 0, with_proj=False), DEV)
+    with gdn.StatePool(cfg, n_slots=4, device=0) as pool:
+        z = torch.zeros((1, 16384), dtype=torch.bfloat16, device=DEV)
+        t = torch.zeros(2, dtype=torch.int32, device=DEV)
+        with pytest.raises(abi.GdnError) as e:
+            pool.layer_step(0, w, z, z, z, z, t[:1], t, 1, flags=0x10)
+        assert e.value.code == abi.GDN_E_INVALID
