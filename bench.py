@@ -233,8 +233,10 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 state, bf16 io", "data": "synthetic",
-            "config": {"workload": f"config2: 30-layer GDN stack, batched S=1 decode, B={B}",
-                       "batch_per_gpu": B, "layers": N_LAYERS, "l2": "n/a (CPU)"},
+            "config": {"workload": f"config2: 30-layer GDN stack, batched S=1 decode, B={B} per GPU",
+                       "batch_per_gpu": B, "layers": N_LAYERS,
+                       "parallelism": f"slot-range shards x{args.gpus} (CPU arm: rank 0 times one shard's B)",
+                       "l2": "n/a (CPU)"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": sample + "; CPU restatement of the reference layer (MLX/Metal unavailable)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
