@@ -66,6 +66,7 @@ def parse():
     p.add_argument("--no-mixer", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-mixed", action="store_true")
+    p.add_argument("--no-sharded", action="store_true")
     p.add_argument("--e2e-groups", default=E2E_GROUPS,
                    help="layers per host<->device copy group of the e2e step, comma separated")
     p.add_argument("--prefill-only", action="store_true",
@@ -393,6 +394,71 @@ TOKEN_IO_BYTES = 8192 * 2 + 4096 * 2 + 64 * 2 + 4096 * 2    # qkv, z, a/b in; ga
 STATE_BYTES_PER_SEQ_LAYER = BYTES_PER_SEQ_LAYER - TOKEN_IO_BYTES
 
 
+def _time_ragged(torch, dev, cfg, abi, lib, lws, stream, barrier, dist, mpool, plans, warm, n_tab, per_layer_io,
+                 gen):
+    """Run `plans` (per step: pool slot ids, cu_seqlens) as one packed gdn_layer_step_ex call per layer, eagerly
+    (token counts change every step), with the step's tables uploaded from pinned host memory inside the step.
+    The first `warm` steps are untimed.  Returns (device ms of the timed steps, max over ranks, timed plans).
+    With `per_layer_io` every layer reads its own projection rows; otherwise all layers share one input and one
+    output buffer (larger than L2 at these token counts)."""
+    n_max = max(int(c[-1]) for _, c in plans)
+    mpool.reserve_tokens(n_max)
+    n_io = N_LAYERS if per_layer_io else 1
+    proj = torch.randn((n_io, n_max, PROJ_LD), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty((n_io, n_max, cfg.z_dim), dtype=torch.bfloat16, device=dev)
+    tab_h = torch.empty(2 * (n_tab + 1), dtype=torch.int32).pin_memory()
+    tab_d = torch.empty(2 * (n_tab + 1), dtype=torch.int32, device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    ios = [abi.GdnStepIOC(proj[i].data_ptr(), PROJ_LD, proj[i].data_ptr() + 8192 * 2, PROJ_LD,
+                          proj[i].data_ptr() + (8192 + 4096) * 2, PROJ_LD, out[i].data_ptr(), cfg.z_dim)
+           for i in range(n_io)]
+
+    def step(k):
+        sl, cu = plans[k]
+        n = len(sl)
+        tab_h[:n] = torch.from_numpy(sl)
+        tab_h[n_tab + 1:n_tab + 2 + n] = torch.from_numpy(cu)
+        with torch.cuda.stream(stream):
+            tab_d.copy_(tab_h, non_blocking=True)
+            for l in range(N_LAYERS):
+                rc = lib.gdn_layer_step_ex(mpool.h, l, C.byref(lws[l].c), C.byref(ios[l % n_io]),
+                                           C.c_void_p(tab_d.data_ptr()), C.c_void_p(tab_d.data_ptr() + (n_tab + 1) * 4),
+                                           n, int(cu[-1]), STABLE if l else 0, sp)
+                if rc:
+                    abi.check(rc, "gdn_layer_step_ex")
+        stream.synchronize()   # the pinned table buffer is reused by the next step
+
+    for k in range(warm):
+        step(k)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(warm, len(plans)):
+        step(k)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert mpool.check() == 0
+    del proj, out
+    return ms, plans[warm:]
+
+
+def _ragged_summary(ms, timed, world, hbm_peak):
+    tokens = sum(int(c[-1]) for _, c in timed)
+    seqs = sum(len(sl) for sl, _ in timed)
+    step_bytes = sum(N_LAYERS * (len(sl) * STATE_BYTES_PER_SEQ_LAYER + int(c[-1]) * TOKEN_IO_BYTES
+                                 + BYTES_PER_LAUNCH_CONST) for sl, c in timed)
+    return {"steps": len(timed), "tokens_per_gpu": tokens, "sequence_steps_per_gpu": seqs,
+            "tok_s": world * tokens / (ms / 1e3), "ms_per_step": ms / len(timed),
+            "hbm_frac_of_measured": step_bytes / (ms / 1e3) / 1e9 / hbm_peak}
+
+
 def run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, world, args, hbm_peak):
     """Config 3 (ragged continuous batching): a 256-slot pool with 64 live sequences holding prior state;
     every step a seeded 50-100% subset is active and ~10% of the active ones carry a prefill chunk of
@@ -411,61 +477,50 @@ def run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, w
         order = rng.permutation(n_act)
         act, lens = act[order], lens[order]
         plans.append((slots_live[act], np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)))
-    n_max = max(int(c[-1]) for _, c in plans)
     mpool = gdn.StatePool(cfg, n_slots=n_slots, device=dev.index)
-    mpool.reserve_tokens(n_max)
-    proj = torch.randn((N_LAYERS, n_max, PROJ_LD), device=dev, generator=gen).to(torch.bfloat16)
-    out = torch.empty((N_LAYERS, n_max, cfg.z_dim), dtype=torch.bfloat16, device=dev)
-    tab_h = torch.empty(2 * (n_live + 1), dtype=torch.int32).pin_memory()
-    tab_d = torch.empty(2 * (n_live + 1), dtype=torch.int32, device=dev)
-    sp = C.c_void_p(stream.cuda_stream)
-    ios = [abi.GdnStepIOC(proj[l].data_ptr(), PROJ_LD, proj[l].data_ptr() + 8192 * 2, PROJ_LD,
-                          proj[l].data_ptr() + (8192 + 4096) * 2, PROJ_LD, out[l].data_ptr(), cfg.z_dim)
-           for l in range(N_LAYERS)]
-
-    def step(k):
-        sl, cu = plans[k]
-        n = len(sl)
-        tab_h[:n] = torch.from_numpy(sl)
-        tab_h[n_live + 1:n_live + 2 + n] = torch.from_numpy(cu)
-        with torch.cuda.stream(stream):
-            tab_d.copy_(tab_h, non_blocking=True)
-            for l in range(N_LAYERS):
-                rc = lib.gdn_layer_step_ex(mpool.h, l, C.byref(lws[l].c), C.byref(ios[l]),
-                                           C.c_void_p(tab_d.data_ptr()), C.c_void_p(tab_d.data_ptr() + (n_live + 1) * 4),
-                                           n, int(cu[-1]), STABLE if l else 0, sp)
-                if rc:
-                    abi.check(rc, "gdn_layer_step_ex")
-        stream.synchronize()   # the pinned table buffer is reused by the next step
-
-    for k in range(warm):
-        step(k)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for k in range(warm, n_steps):
-        step(k)
-    e1.record(stream)
-    e1.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    assert mpool.check() == 0
-    timed = plans[warm:]
-    tokens = sum(int(c[-1]) for _, c in timed)
-    seqs = sum(len(sl) for sl, _ in timed)
-    step_bytes = sum(N_LAYERS * (len(sl) * STATE_BYTES_PER_SEQ_LAYER + int(c[-1]) * TOKEN_IO_BYTES
-                                 + BYTES_PER_LAUNCH_CONST) for sl, c in timed)
+    ms, timed = _time_ragged(torch, dev, cfg, abi, lib, lws, stream, barrier, dist, mpool, plans, warm, n_live,
+                             True, gen)
     mpool.close()
-    del proj, out
     return {"workload": "config3: 256-slot pool, 64 live, 50-100% active per step, ~10% of them with a prefill "
-                        "chunk U[1,512], 30 fused layer steps, eager launches",
-            "steps": len(timed), "tokens": tokens, "sequence_steps": seqs, "tok_s": world * tokens / (ms / 1e3),
-            "ms_per_step": ms / len(timed), "hbm_frac_of_measured": step_bytes / (ms / 1e3) / 1e9 / hbm_peak}
+                        "chunk U[1,512], 30 fused layer steps, eager launches", **_ragged_summary(ms, timed, world,
+                                                                                                   hbm_peak)}
+
+
+def config5_plans(rank: int, n_steps: int, slots_per_gpu: int = 256):
+    """Step plans of config 5 for the GPU owning global slots [256 rank, 256 (rank + 1)): all 256 local
+    sequences step every time; a seeded 10% of them carry a prefill chunk of U[64, 1024] tokens and the rest
+    one decode token, packed in a random order.  Context lengths are drawn log-uniform in [16, 32768] as the
+    workload states; they decide nothing in a GDN step, whose state per sequence has a fixed size, so the
+    pre-existing state is a seeded random fill."""
+    rng = np.random.default_rng(5000 + rank)
+    ctx = np.exp(rng.uniform(np.log(16), np.log(32768), slots_per_gpu)).astype(np.int64)
+    plans = []
+    for _ in range(n_steps):
+        n_pref = int(round(0.1 * slots_per_gpu))
+        lens = np.ones(slots_per_gpu, np.int64)
+        lens[:n_pref] = rng.integers(64, 1025, n_pref)
+        order = rng.permutation(slots_per_gpu)
+        plans.append((order.astype(np.int32), np.concatenate([[0], np.cumsum(lens[order])]).astype(np.int32)))
+    return plans, ctx
+
+
+def run_sharded(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, rank, args,
+                hbm_peak):
+    """Config 5 (sharded serving, weak scaling): each GPU owns 256 slots of the 256 * world sequences (2048 at
+    8 GPUs), partitioned by slot range, and runs its own packed steps with no exchange between GPUs.  Time is
+    the max over ranks; tok/s is the whole job's."""
+    n_steps, warm = 11, 3
+    plans, ctx = config5_plans(rank, n_steps)
+    own = pool is None or pool.n_slots < 256
+    mpool = gdn.StatePool(cfg, n_slots=256, device=dev.index) if own else pool
+    ms, timed = _time_ragged(torch, dev, cfg, abi, lib, lws, stream, barrier, dist, mpool, plans, warm, 256,
+                             False, gen)
+    if own:
+        mpool.close()
+    return {"workload": "config5: 256 slots per GPU (slot-range shards, %d sequences in all), every step 90%% "
+                        "S=1 decode + 10%% prefill chunks U[64,1024], context log-U[16,32768], 30 fused layer "
+                        "steps, eager launches, no collective" % (256 * world),
+            "median_context_rank0": int(np.median(ctx)), **_ragged_summary(ms, timed, world, hbm_peak)}
 
 
 def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, args, tc_peak):
@@ -768,6 +823,12 @@ def run_ours(args):
     if not args.no_mixed:
         mixed = run_mixed(torch, dev, gen, cfg, gdn, abi, lib, lws, stream, barrier, dist, world, args, hbm_peak)
 
+    # ---- config-5 sharded serving: 256 slots per GPU, 90% decode / 10% prefill chunks, no collective
+    sharded = None
+    if not args.no_sharded:
+        sharded = run_sharded(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier, dist, world, rank,
+                              args, hbm_peak)
+
     # ---- the whole mixer stack (projections + pre-norm + residual) at the same B
     mixer = None
     if not args.no_mixer:
@@ -803,7 +864,8 @@ def run_ours(args):
                            "l2": "no flush: state per step %.2f GB > 126 MB L2" % (
                                N_LAYERS * B * BYTES_PER_SEQ_LAYER / 1e9)},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
-                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer, "prefill": prefill, "mixed": mixed}
+                "clocks": clk, "sweep": sweep or None, "mixer_stack": mixer, "prefill": prefill, "mixed": mixed,
+                "sharded": sharded}
     if dist is not None:
         dist.barrier()
         del g
