@@ -1,8 +1,9 @@
 // gdn_decode.cu -- the fused GDN layer step as two kernels chained with
 // programmatic dependent launch (sm_100a).
 //
-// K1 gdn_prep_kernel (token-parallel, small; gdn_prep_tile_kernel, its tiled form, serves
-//    calls with multi-token segments): for every packed token and
+// K1 gdn_prep_kernel (token-parallel, small; its tiled forms serve calls with multi-token
+//    segments: gdn_prep_vec_kernel, 8 channels per lane, when rows allow 16-byte access, else
+//    gdn_prep_tile_kernel, 2 channels per thread): for every packed token and
 //    k-head group, the causal depthwise conv + SiLU of its q, k and v channels
 //    (reference rounding: S=1 -> bf16 products and bf16 sum, qwen3_5.rs:602-610;
 //    S>1 -> f32 conv1d, qwen3_5.rs:617-623), q/k RMSNorm with gains 1/dk and
@@ -486,6 +487,272 @@ __global__ void __launch_bounds__(256) gdn_prep_tile_kernel(const PrepArgs a) {
     }
 }
 
+// ------------------------------------------------------------------ K1, 8-channel lanes
+
+constexpr int PV_TOK = 16;                    // tokens per sub-tile (one sliding conv window per lane)
+constexpr int PV_SUB = 1;                     // sub-tiles per CTA
+constexpr int PV_RING = 4;                    // conv-window prefetch depth (tokens) of the general path
+constexpr int PV_THREADS = PV_SUB * 96;       // per sub-tile: warp q | k, warp v, warp z
+constexpr int PV_ROWS = PV_TOK + KC - 1;      // tap rows of a sub-tile (3 before it)
+static_assert(PV_SUB * PV_TOK <= 32, "one warp routes the CTA's tokens");
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+    unpack_pair(u.x, f[0], f[1]);
+    unpack_pair(u.y, f[2], f[3]);
+    unpack_pair(u.z, f[4], f[5]);
+    unpack_pair(u.w, f[6], f[7]);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    return make_uint4(pack_pair(f[0], f[1]), pack_pair(f[2], f[3]), pack_pair(f[4], f[5]), pack_pair(f[6], f[7]));
+}
+
+// Conv + SiLU of one lane's 8 channels over the sub-tile's tokens.  raw[32 r] is tap row n0-3+r of the channels
+// (r < 19, in the lane's shared-memory column).  QK: the lane's channels are q (lanes 0-15) or k (lanes 16-31) of
+// the k-head; each token's RMSNorm sum is reduced over the 16 lanes of the half-warp and the normalised values go
+// to the records of the k-head's v-heads.  Otherwise the channels are v channels of v-head `hv0` and go to that
+// head's records.  SIMPLE: every token sits at position >= 3 of a multi-token sequence (no window taps, no decode
+// rounding, fast SiLU), as in prep_tile_tokens.  Otherwise the conv-window rows of the tokens at positions < 3
+// are fetched PV_RING tokens ahead into the lane's column of `ring` (PV_RING slots of 3 rows).
+template <bool SIMPLE, bool QK>
+__device__ __forceinline__ void prep_vec_conv(const PrepArgs& a, int ch, bool active, int n0, int ratio, int hv0,
+                                              int rec_off, const uint4* raw, uint4* ring, const float (&w)[8][4],
+                                              const int* s_seq, const int* s_t, const int* s_T, const int* s_slot) {
+    const int lane = threadIdx.x & 31;
+    // window rows of token jj (positions < 3 only) into ring slot jj % PV_RING; one commit group per token
+    auto prefetch = [&](int jj) {
+        if (jj < PV_TOK) {
+            const int t = s_t[jj];
+            if (s_seq[jj] >= 0 && active && t < KC - 1) {
+                const uint16_t* cs = a.conv + (size_t)s_slot[jj] * (KC - 1) * a.D + ch;
+#pragma unroll
+                for (int p = 0; p < KC - 1; ++p)
+                    if (t + p < KC - 1)
+                        cp_async16(smem_u32(ring + ((jj % PV_RING) * (KC - 1) + p) * 32), cs + (size_t)(t + p) * a.D, 16u);
+            }
+        }
+        cp_async_commit();
+    };
+    float xm[KC - 1][8];
+    if (SIMPLE) {
+#pragma unroll
+        for (int p = 0; p < KC - 1; ++p) unpack8(raw[p * 32], xm[p]);
+    } else {
+#pragma unroll 1
+        for (int jj = 0; jj < PV_RING; ++jj) prefetch(jj);
+    }
+#pragma unroll 1
+    for (int j = 0; j < PV_TOK; ++j) {
+        float xc[8];
+        unpack8(raw[(j + KC - 1) * 32], xc);
+        const bool valid = s_seq[j] >= 0;        // uniform over the warp
+        float o[8];
+        if (SIMPLE) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float x4[KC] = {xm[0][c], xm[1][c], xm[2][c], xc[c]};
+                o[c] = conv_silu_fast(x4, w[c]);
+            }
+        } else {
+            cp_async_wait_group<PV_RING - 1>();  // token j's window rows have landed
+            const int t = s_t[j];
+            const bool win = valid && active && t < KC - 1;
+            const bool decode = valid && active && s_T[j] == 1;
+            const uint4* rs = ring + (j % PV_RING) * (KC - 1) * 32;
+            uint4 tap[KC - 1];
+#pragma unroll
+            for (int p = 0; p < KC - 1; ++p) tap[p] = win && t + p < KC - 1 ? rs[p * 32] : raw[(j + p) * 32];
+            if (decode) {
+                uint16_t* cs = a.conv + (size_t)s_slot[j] * (KC - 1) * a.D + ch;
+                *reinterpret_cast<uint4*>(cs) = tap[1];
+                *reinterpret_cast<uint4*>(cs + a.D) = tap[2];
+                *reinterpret_cast<uint4*>(cs + 2 * (size_t)a.D) = raw[(j + KC - 1) * 32];
+            }
+            float x[KC - 1][8];
+#pragma unroll
+            for (int p = 0; p < KC - 1; ++p) unpack8(tap[p], x[p]);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float x4[KC] = {x[0][c], x[1][c], x[2][c], xc[c]};
+                o[c] = conv_silu(x4, w[c], decode);
+            }
+        }
+        if (QK) {
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) ss += o[c] * o[c];
+#pragma unroll
+            for (int m = 8; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+            if (valid) {
+                const float nrm = 1.0f / sqrtf(ss / (float)DK + 1e-6f);
+                const float gain = lane < 16 ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
+                float v[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) v[c] = rbf(o[c] * nrm) * gain;
+                const uint4 val = pack8(v);
+                for (int r = 0; r < ratio; ++r)
+                    *reinterpret_cast<uint4*>(a.rec + ((long long)(hv0 + r) * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = val;
+            }
+        } else if (valid && active) {
+            *reinterpret_cast<uint4*>(a.rec + ((long long)hv0 * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = pack8(o);
+        }
+        if (SIMPLE) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                xm[0][c] = xm[1][c];
+                xm[1][c] = xm[2][c];
+                xm[2][c] = xc[c];
+            }
+        } else {
+            prefetch(j + PV_RING);   // slot j % PV_RING was consumed above
+        }
+    }
+    if (!SIMPLE) cp_async_wait_all();
+}
+
+// K1 for calls with multi-token segments when the inputs allow 16-byte access: same records, rounding and
+// conv-window updates as gdn_prep_tile_kernel, with each lane owning 8 consecutive channels.  One CTA per
+// (16 packed tokens, k-head): warp 0 takes the q channels (lanes 0-15) and k channels (lanes 16-31) of the
+// k-head, warp 1 the v channels and warp 2 the z columns of its v-heads (lanes 16r .. 16r+15: v-head
+// hk * Hv/Hk + r), and warp 2 also the gates.  A conv lane copies its 19 tap rows (16 bytes each) into its own
+// shared-memory column up front and slides a 3-row window through a rolled token loop (an unrolled one
+// overflows the instruction cache); a z lane loads its rows 8 at a time.
+__global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ uint4 s_raw[PV_SUB][2][PV_ROWS][32];              // [sub-tile][q|k, v][tap row][lane]
+    __shared__ uint4 s_ring[PV_SUB][2][PV_RING * (KC - 1)][32];  // conv-window rows of the general path
+    __shared__ int s_seq[PV_SUB * PV_TOK], s_t[PV_SUB * PV_TOK], s_T[PV_SUB * PV_TOK], s_slot[PV_SUB * PV_TOK];
+    __shared__ int s_simple[PV_SUB];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int sub = warp / 3, role = warp % 3;
+    const int hk = blockIdx.y;
+    const int ratio = a.hv / a.hk;
+    const int nb = blockIdx.x * PV_SUB * PV_TOK;
+    const int n0 = nb + sub * PV_TOK;
+    const int half = lane >> 4, c8 = 8 * (lane & 15);
+    const int hv0 = hk * ratio;
+    const bool active = role == 0 || half < ratio;
+
+    // ---- this lane's tap rows and weights, issued before the routing
+    int ch = 0;
+    float w[8][4];
+    const uint4* col = &s_raw[sub][role < 2 ? role : 0][0][lane];
+    uint4* ring = &s_ring[sub][role < 2 ? role : 0][0][lane];
+    if (role < 2) {
+        ch = role == 0 ? (half ? a.hk * DK : 0) + hk * DK + c8 : 2 * a.hk * DK + (hv0 + half) * DV + c8;
+#pragma unroll
+        for (int r = 0; r < PV_ROWS; ++r) {
+            const int row = n0 - (KC - 1) + r;
+            const bool ok = active && row >= 0 && row < a.n_tokens;
+            cp_async16(smem_u32(col + r * 32), a.qkv + (ok ? (long long)row * a.ld_qkv + ch : 0), ok ? 16u : 0u);
+        }
+        cp_async_commit();
+        const uint4* wp = reinterpret_cast<const uint4*>(a.conv_w + (size_t)ch * KC);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 u = active ? __ldg(wp + i) : make_uint4(0u, 0u, 0u, 0u);
+            unpack_w4(make_uint2(u.x, u.y), w[2 * i]);
+            unpack_w4(make_uint2(u.z, u.w), w[2 * i + 1]);
+        }
+    }
+
+    // ---- routing of the CTA's tokens (s_seq < 0: no such token, or a rejected sequence)
+    if (warp == 0) {
+        bool simple_tok = true;
+        if (lane < PV_SUB * PV_TOK) {
+            const int n = nb + lane;
+            int seq = -1, t = 0, T = 0, slot = -1;
+            if (n < a.n_tokens) {
+                const int guess = n < a.n_seq ? n : a.n_seq - 1;
+                if (__ldg(a.cu_seqlens + guess) <= n && n < __ldg(a.cu_seqlens + guess + 1))
+                    seq = guess;
+                else
+                    seq = find_seq(a.cu_seqlens, a.n_seq, n);
+                if (seq < 0) {
+                    if (hk == 0) atomicOr(a.err, ERR_BAD_SEQLENS);
+                } else {
+                    const int t0 = __ldg(a.cu_seqlens + seq);
+                    T = __ldg(a.cu_seqlens + seq + 1) - t0;
+                    slot = __ldg(a.slot_ids + seq);
+                    t = n - t0;
+                    if (slot < 0 || slot >= a.n_slots || t0 + T > a.n_tokens) {
+                        if (hk == 0 && t == 0)
+                            atomicOr(a.err, slot < 0 || slot >= a.n_slots ? ERR_BAD_SLOT : ERR_BAD_SEQLENS);
+                        seq = -1;
+                    }
+                }
+            }
+            s_seq[lane] = seq;
+            s_t[lane] = t;
+            s_T[lane] = T;
+            s_slot[lane] = slot;
+            simple_tok = seq < 0 || (t >= KC - 1 && T > 1);
+        }
+        const unsigned bits = __ballot_sync(0xffffffffu, simple_tok);
+        if (lane < PV_SUB) s_simple[lane] = ((bits >> (lane * PV_TOK)) & 0xffffu) == 0xffffu;
+    }
+    __syncthreads();
+
+    const int* q_seq = s_seq + sub * PV_TOK;
+    const int* q_t = s_t + sub * PV_TOK;
+    const int* q_T = s_T + sub * PV_TOK;
+    const int* q_slot = s_slot + sub * PV_TOK;
+    const bool simple = s_simple[sub] != 0;
+    if (role < 2) cp_async_wait_all();       // the lane's own column: no barrier needed
+    if (role == 0) {
+        const int off = (half ? 256 : 0) + 2 * c8;
+        if (simple)
+            prep_vec_conv<true, true>(a, ch, true, n0, ratio, hv0, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+        else
+            prep_vec_conv<false, true>(a, ch, true, n0, ratio, hv0, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+    } else if (role == 1) {
+        const int off = 512 + 2 * c8;
+        if (simple)
+            prep_vec_conv<true, false>(a, ch, active, n0, ratio, hv0 + half, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+        else
+            prep_vec_conv<false, false>(a, ch, active, n0, ratio, hv0 + half, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+    } else {
+        // silu(z) of the lane's 8 columns, 8 rows at a time
+        if (active) {
+            const uint16_t* zp = a.z + (long long)n0 * a.ld_z + (hv0 + half) * DV + c8;
+#pragma unroll 1
+            for (int jb = 0; jb < PV_TOK; jb += 8) {
+                uint4 zr[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    zr[r] = n0 + jb + r < a.n_tokens ? __ldg(reinterpret_cast<const uint4*>(zp + (long long)(jb + r) * a.ld_z))
+                                                     : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    if (q_seq[jb + r] < 0) continue;
+                    float zv[8];
+                    unpack8(zr[r], zv);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) zv[c] = simple ? silu_bf_fast(zv[c]) : silu_bf(zv[c]);
+                    *reinterpret_cast<uint4*>(a.rec + ((long long)(hv0 + half) * a.rec_cap + n0 + jb + r) * REC_BYTES +
+                                              768 + 2 * c8) = pack8(zv);
+                }
+            }
+        }
+        // gates (compiled_beta_g): lane = token (lane & 15) of v-head hv0 + half
+        const int j = lane & 15;
+        if (half < ratio && q_seq[j] >= 0) {
+            const int n = n0 + j;
+            const int hv = hv0 + half;
+            const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
+            const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
+            const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+            const float logdecay = -(expf(a.A_log[hv]) * sp);
+            float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
+            gb[0] = expf(logdecay);
+            gb[1] = rbf(sigmoid_f32(b));
+            gb[2] = logdecay;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ K2
 
 // All 288 threads meet here.  Normally every issued copy was consumed; after a
@@ -760,14 +1027,28 @@ cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStre
     const bool pairs_aligned = ((reinterpret_cast<uintptr_t>(p.qkv) | reinterpret_cast<uintptr_t>(p.z)) & 3u) == 0 &&
                                (p.ld_qkv & 1) == 0 && (p.ld_z & 1) == 0;
     const bool tiled = p.n_tokens > p.n_seq && pairs_aligned && p.hv <= 2 * p.hk;
+    // ... and the 8-channel form when every row, weight, window and record access can be 16 bytes wide.
+    const bool vec = tiled &&
+                     ((reinterpret_cast<uintptr_t>(p.qkv) | reinterpret_cast<uintptr_t>(p.z) |
+                       reinterpret_cast<uintptr_t>(p.conv_w) | reinterpret_cast<uintptr_t>(p.conv) |
+                       reinterpret_cast<uintptr_t>(p.rec)) & 15u) == 0 &&
+                     (p.ld_qkv & 7) == 0 && (p.ld_z & 7) == 0 && (p.D & 7) == 0;
     cudaLaunchConfig_t c1 = {};
-    c1.gridDim = tiled ? dim3((unsigned)((p.n_tokens + PT_TOK - 1) / PT_TOK), (unsigned)p.hk, 1)
-                       : dim3((unsigned)p.n_tokens, (unsigned)p.hk, 1);
-    c1.blockDim = dim3(256, 1, 1);
+    if (vec) {
+        constexpr int per_cta = PV_SUB * PV_TOK;
+        c1.gridDim = dim3((unsigned)((p.n_tokens + per_cta - 1) / per_cta), (unsigned)p.hk, 1);
+        c1.blockDim = dim3(PV_THREADS, 1, 1);
+    } else {
+        c1.gridDim = tiled ? dim3((unsigned)((p.n_tokens + PT_TOK - 1) / PT_TOK), (unsigned)p.hk, 1)
+                           : dim3((unsigned)p.n_tokens, (unsigned)p.hk, 1);
+        c1.blockDim = dim3(256, 1, 1);
+    }
     c1.stream = stream;
     c1.attrs = attr;
     c1.numAttrs = 1;
-    e = tiled ? cudaLaunchKernelEx(&c1, gdn_prep_tile_kernel, p) : cudaLaunchKernelEx(&c1, gdn_prep_kernel, p);
+    e = vec     ? cudaLaunchKernelEx(&c1, gdn_prep_vec_kernel, p)
+        : tiled ? cudaLaunchKernelEx(&c1, gdn_prep_tile_kernel, p)
+                : cudaLaunchKernelEx(&c1, gdn_prep_kernel, p);
     if (e != cudaSuccess) return e;
 
     const int n_items = r.n_seq * r.hv;

@@ -55,7 +55,6 @@ constexpr int WQ_BLK = 288;                  // 4-bit block: codes 256 B, scales
 constexpr int WG_TILE = 16 * WG_BLK;         // bf16 unit of a full slab (16 row groups)
 constexpr int WQ_TILE = 16 * WQ_BLK;         // 4-bit unit of a full slab
 constexpr uint64_t WG_WAIT_NS = 2000000000ull;
-constexpr int WG_RING_BYTES = 204800;
 
 template <int MP, bool Q4>
 struct WgShape {

@@ -101,3 +101,44 @@ def test_chunked_prefill_strong_decay(gdn, synth, oracle):
         r, _ = pool.export(0, 0)
         assert np.all(np.isfinite(r))
         assert rel_l2(r, ref_rs[0]) < TOL
+
+
+@pytest.mark.parametrize("pad", [0, 2])
+def test_prep_forms_by_row_alignment(gdn, synth, oracle, pad):
+    """The prep of a call with multi-token segments has an 8-channel form (16-byte aligned rows, pad 0) and a
+    2-channel form (rows only 4-byte aligned, pad 2); both match the oracle, with decode tokens and segment
+    starts inside the same 16-token tiles."""
+    cfg = synth.GdnConfig(n_layers=1)
+    w = synth.layer_weights(cfg, 0, with_proj=False)
+    lens = [1, 70, 2, 40, 1, 1, 100, 5]
+    slots = np.array([3, 1, 6, 0, 5, 2, 4, 7], np.int32)
+    conv0, rec0 = synth.random_states(cfg, len(lens), seed=9, tag="pad")
+    cu = _cu(lens)
+    N = int(cu[-1])
+    inp = synth.step_inputs(cfg, N, seed=9, tag="pad")
+
+    def rows(a, ld):
+        t = torch.zeros((N, ld), dtype=torch.bfloat16, device=DEV)
+        t[:, :a.shape[1]] = gdn.bf16_to_device(a, DEV)
+        return t[:, :a.shape[1]]
+
+    qkv, z = rows(inp["qkv"], cfg.conv_dim + pad), rows(inp["z"], cfg.z_dim + pad)
+    assert qkv.stride(0) == cfg.conv_dim + pad
+    f = synth.bf16_to_f32
+    with gdn.StatePool(cfg, n_slots=8, device=0) as pool:
+        pool.reserve_tokens(N)
+        for i, s in enumerate(slots):
+            pool.import_(int(s), 0, rec0[i], conv0[i])
+        out = torch.empty((N, cfg.z_dim), dtype=torch.bfloat16, device=DEV)
+        pool.layer_step(0, gdn.LayerWeights(w, DEV), qkv, z, gdn.bf16_to_device(inp["ab"], DEV), out,
+                        torch.from_numpy(slots).to(DEV), torch.from_numpy(cu).to(DEV), N)
+        torch.cuda.synchronize()
+        assert pool.check() == 0
+        ref_out, ref_cs, ref_rs, _ = oracle.layer_step(cfg, w, inp["qkv"], inp["z"], inp["ab"], conv0, rec0, cu)
+        got = gdn.bf16_to_host(out)
+        for i, s in enumerate(slots):
+            a, b = cu[i], cu[i + 1]
+            assert rel_l2(f(got[a:b]), f(ref_out[a:b])) < TOL, f"output of segment {i} (T={lens[i]})"
+            r, c = pool.export(int(s), 0)
+            assert rel_l2(r, ref_rs[i]) < TOL, f"state of segment {i}"
+            assert np.array_equal(c, ref_cs[i]), f"conv state of segment {i}"
