@@ -142,3 +142,31 @@ def test_prep_forms_by_row_alignment(gdn, synth, oracle, pad):
             r, c = pool.export(int(s), 0)
             assert rel_l2(r, ref_rs[i]) < TOL, f"state of segment {i}"
             assert np.array_equal(c, ref_cs[i]), f"conv state of segment {i}"
+
+
+def test_chunked_prefill_long_prompt_no_drift(gdn, synth, oracle):
+    """A 4096-token prompt (64 chunks of the tensor-core path, each passing the f32 state through hi/lo bf16
+    splits) packed with a decode token and a 700-token prompt, from random state: the last chunk's outputs and
+    the final states are as close to the oracle as the first chunk's, so no error builds up over the chunks."""
+    cfg = synth.GdnConfig(n_layers=1)
+    w = synth.layer_weights(cfg, 0, with_proj=False)
+    lens = [4096, 1, 700]
+    slots = np.array([2, 0, 5], np.int32)
+    conv0, rec0 = synth.random_states(cfg, len(lens), seed=12, tag="long")
+    f = synth.bf16_to_f32
+    with gdn.StatePool(cfg, n_slots=8, device=0) as pool:
+        pool.reserve_tokens(int(sum(lens)))
+        for i, s in enumerate(slots):
+            pool.import_(int(s), 0, rec0[i], conv0[i])
+        out, (ref_out, ref_cs, ref_rs, _) = _run(gdn, synth, oracle, cfg, w, lens, slots, conv0, rec0, 12, "long",
+                                                 pool=pool)
+        cu = _cu(lens)
+        first = rel_l2(f(out[:64]), f(ref_out[:64]))
+        last = rel_l2(f(out[4096 - 64:4096]), f(ref_out[4096 - 64:4096]))
+        assert first < TOL and last < TOL, (first, last)
+        for i, s in enumerate(slots):
+            a, b = cu[i], cu[i + 1]
+            assert rel_l2(f(out[a:b]), f(ref_out[a:b])) < TOL, f"output of segment {i} (T={lens[i]})"
+            r, c = pool.export(int(s), 0)
+            assert rel_l2(r, ref_rs[i]) < TOL, f"state of segment {i}"
+            assert np.array_equal(c, ref_cs[i]), f"conv state of segment {i}"
