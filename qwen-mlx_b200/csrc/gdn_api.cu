@@ -72,6 +72,8 @@ struct gdn_pool {
     int n_sm;                // multiprocessors of the pool's device
     int* wg_cnt;             // weight-streaming GEMM: per-row-tile arrival counters [kWgMaxTiles] (zero at rest)
     float* wg_ws;            // weight-streaming GEMM: partial sums [wg_workspace_floats(n_sm)]
+    uint16_t* wdq;           // one projection weight expanded from 4-bit tiles to bf16 [wdq_elems]
+    size_t wdq_elems;
     uint16_t* proj;          // scratch [rec_cap][D + Hv*dv + 2*Hv]: projection outputs
     uint16_t* gated;         // scratch [rec_cap][Hv*dv]: layer-step output (out_proj input)
     uint16_t* hn;            // scratch [rec_cap][hidden]: normed stack input
@@ -195,6 +197,8 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
     p->gemm_ws = nullptr;
     p->wg_cnt = nullptr;
     p->wg_ws = nullptr;
+    p->wdq = nullptr;
+    p->wdq_elems = 0;
     p->n_sm = 0;
     rc = reserve_records(p, n_slots > 1024 ? n_slots : 1024);
     if (rc == GDN_OK) {
@@ -208,6 +212,11 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         if (e == cudaSuccess) e = cudaMalloc(&p->wg_cnt, kWgMaxTiles * sizeof(int));
         if (e == cudaSuccess) e = cudaMalloc(&p->wg_ws, gdn::wg_workspace_floats(p->n_sm) * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(p->wg_cnt, 0, kWgMaxTiles * sizeof(int));
+        if (e == cudaSuccess) {
+            const size_t in_w = (size_t)proj_ld(p) * p->cfg.hidden, out_w = (size_t)p->cfg.hidden * p->cfg.n_v_heads * 128;
+            p->wdq_elems = in_w > out_w ? in_w : out_w;
+            e = cudaMalloc(&p->wdq, p->wdq_elems * sizeof(uint16_t));
+        }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) rc = fail(GDN_E_NOMEM, "projection GEMM workspace: %s", cudaGetErrorString(e));
     }
@@ -219,6 +228,7 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         cudaFree(p->gemm_ws);
         cudaFree(p->wg_cnt);
         cudaFree(p->wg_ws);
+        cudaFree(p->wdq);
         gdn::gemm_destroy(p->gemm);
         delete p;
         return rc;
@@ -251,6 +261,7 @@ int gdn_pool_destroy(gdn_pool* p) {
     cudaFree(p->gemm_ws);
     cudaFree(p->wg_cnt);
     cudaFree(p->wg_ws);
+    cudaFree(p->wdq);
     delete p;
     return ok();
 }
@@ -270,7 +281,8 @@ int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
                  p->cfg.n_layers +
              sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES +
              (size_t)p->rec_cap * 2 * (proj_ld(p) + p->cfg.n_v_heads * 128 + 2 * p->cfg.hidden) + (32u << 20) +
-             kWgMaxTiles * sizeof(int) + (size_t)gdn::wg_workspace_floats(p->n_sm) * sizeof(float);
+             kWgMaxTiles * sizeof(int) + (size_t)gdn::wg_workspace_floats(p->n_sm) * sizeof(float) +
+             p->wdq_elems * sizeof(uint16_t);
     return ok();
 }
 
@@ -495,14 +507,22 @@ static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, 
     return GDN_OK;
 }
 
-// One projection y = x w^T: 4-bit tiles when given (any token count), else bf16 tiles for calls of at
-// most WG_MAX_M tokens, else cuBLASLt on the row-major weight.
+// One projection y = x w^T: 4-bit tiles when given (calls of at most WG_MAX_M tokens stream them; longer
+// calls expand the weight to bf16 once into the pool's scratch and run one cuBLASLt GEMM), else bf16 tiles
+// for calls of at most WG_MAX_M tokens, else cuBLASLt on the row-major weight.
 static int projection(gdn_pool* p, int M, int N, int K, const uint16_t* x, long long ldx, const uint16_t* w,
                       const void* w_tiles, const void* w_q4, uint16_t* y, long long ldy, cudaStream_t s,
                       const char* what) {
     if (w_q4) {
         if (!wg_rows_ok(K, x, ldx, w_q4) || K % 64 != 0)
             return fail(GDN_E_INVALID, "%s: 4-bit projection needs K %% 64 == 0 and 16-byte aligned rows", what);
+        if (M > gdn::WG_MAX_M && (size_t)N * K <= p->wdq_elems) {
+            const cudaError_t e = gdn::launch_wq_untile(w_q4, N, K, p->wdq, s);
+            if (e != cudaSuccess) return cuda_fail(e, "4-bit weight expansion");
+            if (gdn::gemm_bf16_nt(p->gemm, M, N, K, x, ldx, p->wdq, y, ldy, s))
+                return fail(GDN_E_CUDA, "%s: cuBLASLt GEMM failed (M=%d N=%d K=%d)", what, M, N, K);
+            return GDN_OK;
+        }
         return wg_run(p, true, M, N, K, x, ldx, w_q4, y, ldy, s, what);
     }
     if (w_tiles && M <= gdn::WG_MAX_M && wg_rows_ok(K, x, ldx, w_tiles))

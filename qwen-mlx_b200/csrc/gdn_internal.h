@@ -118,6 +118,8 @@ cudaError_t launch_wg_tile(const uint16_t* w, int N, int K, uint8_t* tiles, cuda
 cudaError_t launch_wq_tile(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases, int N, int K,
                            uint8_t* tiles, cudaStream_t stream);
 cudaError_t launch_wg_gemm(const WgGemm& g, cudaStream_t stream);
+// 4-bit tiles (wq_tile_bytes layout, K % 64 == 0) -> row-major bf16 weight w [N][K], 16-byte aligned.
+cudaError_t launch_wq_untile(const void* tiles, int N, int K, uint16_t* w, cudaStream_t stream);
 
 // Set the calling thread's gdn_last_error() message and return `code` / GDN_OK.
 int record_error(int code, const char* msg);

@@ -1,6 +1,7 @@
 // gdn_wgemm.cu -- weight-streaming projection GEMM (qwen3_5.rs:572-586 in_proj_*, :668 out_proj):
 // y[m][n] = bf16(sum_k x[m][k] * w[n][k]) with f32 accumulation, for calls of at most 64 tokens
-// per launch (longer calls run in blocks of 64 tokens).
+// per launch (longer calls run in blocks of 64 tokens; the mixer instead expands a 4-bit weight to bf16
+// once, wq_untile_kernel, and runs one library GEMM for them).
 //
 // With few tokens the GEMM moves each weight once for 2*M flops: it is bound by streaming the weight
 // out of HBM.  So the weight is stored once, at load, in the layout the tensor core reads ("tiled
@@ -572,6 +573,24 @@ __global__ void __launch_bounds__(WgShape<MP, Q4>::THREADS, 1) wg_gemm_kernel(Wg
 
 // ------------------------------------------------------------------ host side
 
+// 4-bit tiles -> row-major bf16 weight [N][K] (each weight scale * q + bias rounded once, as the loader warps
+// stage it): calls of more than WG_MAX_M tokens expand the weight once and run one library GEMM instead of
+// streaming the tiles once per 64-token block.  Thread = (row n, 8-column chunk).
+__global__ void __launch_bounds__(256) wq_untile_kernel(const uint8_t* __restrict__ tiles, int N, int K, int NRG,
+                                                        uint16_t* __restrict__ w, long long n_chunks) {
+    const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= n_chunks) return;
+    const int kc = K / 8;
+    const long long n = q / kc;
+    const int c8 = (int)(q - n * kc);
+    const int kt = c8 >> 3, c = c8 & 7, rg = (int)(n >> 3), r8 = (int)(n & 7);
+    const uint8_t* blk = tiles + ((long long)kt * NRG + rg) * WQ_BLK;
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(blk + c * 32 + r8 * 4);
+    const uint32_t sb = *reinterpret_cast<const uint16_t*>(blk + 256 + r8 * 2);
+    const uint32_t bb = *reinterpret_cast<const uint16_t*>(blk + 272 + r8 * 2);
+    *reinterpret_cast<uint4*>(w + n * K + c8 * 8) = wq_dequant8(word, sb | (sb << 16), bb | (bb << 16));
+}
+
 long long wg_tile_bytes(int N, int K) {
     const long long NRG = (N + 7) / 8, KT = (K + WG_K - 1) / WG_K;
     return NRG * KT * WG_BLK;
@@ -596,6 +615,14 @@ cudaError_t launch_wq_tile(const uint32_t* wq, const uint16_t* scales, const uin
     const long long n_words = NRG * KT * 64;
     wq_tile_kernel<<<(unsigned)((n_words + 255) / 256), 256, 0, stream>>>(wq, scales, biases, N, K, (int)NRG, tiles,
                                                                           n_words);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wq_untile(const void* tiles, int N, int K, uint16_t* w, cudaStream_t stream) {
+    if (K % WG_K != 0 || N <= 0) return cudaErrorInvalidValue;
+    const long long NRG = (N + 7) / 8, n_chunks = (long long)N * (K / 8);
+    wq_untile_kernel<<<(unsigned)((n_chunks + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const uint8_t*>(tiles), N, K, (int)NRG, w, n_chunks);
     return cudaGetLastError();
 }
 

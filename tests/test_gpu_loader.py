@@ -15,7 +15,10 @@ DEV = torch.device("cuda:0")
 TOL = 1e-3
 
 
-def test_quantized_checkpoint_stack_matches_oracle(gdn, synth, oracle, tmp_path):
+@pytest.mark.parametrize("first", [[7, 40, 2], [7, 90, 2]])
+def test_quantized_checkpoint_stack_matches_oracle(gdn, synth, oracle, tmp_path, first):
+    """First step 49 tokens (4-bit weight-streaming kernel) or 99 tokens (more than 64: the weight is expanded
+    to bf16 once per projection and multiplied by the library GEMM), then two decode steps."""
     import importlib
     loader = importlib.import_module("qwen_mlx_b200.loader")
     _write_checkpoint(synth, loader, tmp_path, quantized=True, seed=7)
@@ -36,7 +39,7 @@ def test_quantized_checkpoint_stack_matches_oracle(gdn, synth, oracle, tmp_path)
     alt = {o: (cs.copy(), rs.copy()) for o in ALT_ORDERS}
     f = synth.bf16_to_f32
     with gdn.StatePool(cfg, n_slots=8, device=0) as pool:
-        for it, lens in enumerate([[7, 40, 2], [1, 1, 1], [1, 1, 1]]):
+        for it, lens in enumerate([first, [1, 1, 1], [1, 1, 1]]):
             cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
             N = int(cu[-1])
             h0 = synth.normal_bf16(50 + it, "ck_h", (N, cfg.hidden))
