@@ -507,16 +507,19 @@ static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, 
     return GDN_OK;
 }
 
-// One projection y = x w^T: 4-bit tiles when given (calls of at most WG_MAX_M tokens stream them; longer
-// calls expand the weight to bf16 once into the pool's scratch and run one cuBLASLt GEMM), else bf16 tiles
-// for calls of at most WG_MAX_M tokens, else cuBLASLt on the row-major weight.
+// One projection y = x w^T: 4-bit tiles when given (calls of at most WG_MAX_M tokens on a weight with
+// enough rows for whole slabs on every SM stream them; longer calls, and weights of fewer rows (the
+// out-projection, where streaming needs split-k partial sums), expand the weight to bf16 once into the
+// pool's scratch and run one cuBLASLt GEMM), else bf16 tiles for calls of at most WG_MAX_M tokens, else
+// cuBLASLt on the row-major weight.
 static int projection(gdn_pool* p, int M, int N, int K, const uint16_t* x, long long ldx, const uint16_t* w,
                       const void* w_tiles, const void* w_q4, uint16_t* y, long long ldy, cudaStream_t s,
                       const char* what) {
     if (w_q4) {
         if (!wg_rows_ok(K, x, ldx, w_q4) || K % 64 != 0)
             return fail(GDN_E_INVALID, "%s: 4-bit projection needs K %% 64 == 0 and 16-byte aligned rows", what);
-        if (M > gdn::WG_MAX_M && (size_t)N * K <= p->wdq_elems) {
+        const bool whole_slabs = (N + 7) / 8 >= 8 * p->n_sm;
+        if ((M > gdn::WG_MAX_M || !whole_slabs) && (size_t)N * K <= p->wdq_elems) {
             const cudaError_t e = gdn::launch_wq_untile(w_q4, N, K, p->wdq, s);
             if (e != cudaSuccess) return cuda_fail(e, "4-bit weight expansion");
             if (gdn::gemm_bf16_nt(p->gemm, M, N, K, x, ldx, p->wdq, y, ldy, s))
