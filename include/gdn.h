@@ -175,7 +175,9 @@ GDN_API int gdn_layer_step_ex(gdn_pool* pool, int32_t layer, const gdn_layer_wei
  * in_proj_qkv (D rows) | in_proj_z (Hv*dv) | in_proj_b (Hv) | in_proj_a (Hv).
  * Each projection may also (or instead) be given in a tiled form:
  *   *_q4    gdn_weight_tile_q4 tiles of the MLX 4-bit quantized weight (the reference's
- *           4-bit checkpoint, qwen3_5.rs:929-935): used for every call when present;
+ *           4-bit checkpoint, qwen3_5.rs:929-935): used for every call when present (streamed by
+ *           the weight-streaming kernel for calls of at most 64 tokens on a weight of at least
+ *           64 * #SMs rows; otherwise expanded to bf16 in the pool's scratch, then cuBLASLt);
  *   *_tiles gdn_weight_tile tiles of the bf16 weight: used for calls of at most 64 tokens.
  * Otherwise (and for longer calls without 4-bit tiles) the row-major bf16 weight runs on
  * cuBLASLt, so a row-major weight may be NULL only when one of the tiled forms covers
@@ -243,8 +245,9 @@ GDN_API int gdn_linear_q4(gdn_pool* pool, int32_t n_tokens, int32_t n_out, int32
 /* A whole mixer layer (GatedDeltaNet::forward_with_cache, qwen3_5.rs:559-669):
  * y = out_proj(gdn_layer_step(in_proj(x))) over a packed ragged batch.
  * x [n_tokens][ld_x], y [n_tokens][ld_y] bf16, hidden columns.  The projections run as
- * gdn_mixer_weights says: 4-bit tiles on the weight-streaming kernel, bf16 tiles on it for
- * calls of at most 64 tokens, otherwise cuBLASLt (library GEMM), all with f32 accumulation.
+ * gdn_mixer_weights says: 4-bit tiles on the weight-streaming kernel (or expanded to bf16 for
+ * cuBLASLt, see above), bf16 tiles on it for calls of at most 64 tokens, otherwise cuBLASLt
+ * (library GEMM), all with f32 accumulation.
  * Asynchronous. */
 GDN_API int gdn_mixer_step(gdn_pool* pool, int32_t layer, const gdn_mixer_weights* w, const gdn_bf16* x,
                            int64_t ld_x, gdn_bf16* y, int64_t ld_y, const int32_t* slot_ids,
