@@ -297,11 +297,21 @@ GDN_API int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int3
  * device looks up the scratch's device address; make that first call before
  * capturing a stream into a CUDA graph.  All calls share the scratch, so calls
  * that overlap on the GPU (other streams or threads) race: serialise them.
- * Asynchronous on `stream`; device-side bounds-check bits are not reported, so
- * validate the tables with gdn_validate_tables. */
+ * Asynchronous on `stream`.  The kernels' bounds checks and bounded waits record
+ * failures in an error word inside the same array (read it with gdn_noalloc_check);
+ * validate the tables with gdn_validate_tables before the call. */
 GDN_API int gdn_layer_step_noalloc(const gdn_config* cfg, int32_t n_slots, float* rec_state, gdn_bf16* conv_state,
                                    const gdn_layer_weights* w, const gdn_step_io* io, const int32_t* slot_ids,
                                    const int32_t* cu_seqlens, int32_t n_seq, int32_t n_tokens, void* stream);
+
+/* No counterpart in the reference.  The device error word of gdn_layer_step_noalloc on the
+ * current device: bits (1 << GDN_E_BAD_SLOT) / (1 << GDN_E_BAD_SEQLENS) when a kernel skipped a
+ * sequence whose slot or token range failed its bounds check, (1 << 7) when a bounded device
+ * wait gave up.  A call that set a bit returned GDN_OK, but its outputs and the states it
+ * touched are not to be trusted.  Synchronous (waits for the device); clears the word when
+ * `reset` is non-zero.  Allocates nothing.  The word is shared by every no-alloc call on the
+ * device and keeps its bits until cleared. */
+GDN_API int gdn_noalloc_check(int32_t* flags, int reset);
 
 #ifdef __cplusplus
 }

@@ -102,6 +102,7 @@ SIGNATURES = {
     "gdn_beta_g": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gdn_layer_step_noalloc": (_int, [C.POINTER(GdnConfigC), _i32, _vp, _vp, C.POINTER(GdnLayerWeightsC),
                                       C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32, _vp]),
+    "gdn_noalloc_check": (_int, [C.POINTER(_i32), _int]),
     # include/gdn_host.h
     "gdn_pack_step": (_int, [C.POINTER(GdnStepEntryC), _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gdn_sched_create": (_int, [C.POINTER(GdnSchedConfigC), C.POINTER(_vp)]),

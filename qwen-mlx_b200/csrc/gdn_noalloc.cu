@@ -37,6 +37,28 @@ constexpr int MAX_DEVICES = 64;
 std::mutex g_setup_mutex;
 uint8_t* g_scratch_ptr[MAX_DEVICES] = {nullptr};
 
+// Set-up, once per device, with that device current: the device address of the scratch array
+// (the host-side symbol is not a device address; the kernels get this pointer), and a cleared
+// error word.  The first call on a device does this, so make it before capturing any stream into
+// a CUDA graph.
+int scratch_of_current_device(uint8_t** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
+        return gdn::record_error(GDN_E_CUDA, "cudaGetDevice failed or device index out of range");
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (!g_scratch_ptr[dev]) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) return gdn::record_error(GDN_E_CUDA, "cudaGetSymbolAddress of the scratch failed");
+        const int32_t zero = 0;
+        e = cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof zero, NOALLOC_RECORD_BYTES, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return gdn::record_error(GDN_E_CUDA, "clearing the no-alloc error word failed");
+        g_scratch_ptr[dev] = static_cast<uint8_t*>(ptr);
+    }
+    *out = g_scratch_ptr[dev];
+    return GDN_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -68,23 +90,9 @@ int gdn_layer_step_noalloc(const gdn_config* cfg, int32_t n_slots, float* rec_st
                             "per call at 32 v-heads); split the batch or use gdn_layer_step with a pool");
     if (n_seq == 0 || n_tokens == 0) return gdn::record_ok();
 
-    // Set-up, once per device, with that device current: the device address of the scratch array.
-    // (The host-side symbol is not a device address; the kernels get this pointer.)  The first
-    // call on a device does this, so make it before capturing any stream into a CUDA graph.
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
-        return record_error(GDN_E_CUDA, "cudaGetDevice failed or device index out of range");
     uint8_t* scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_setup_mutex);
-        if (!g_scratch_ptr[dev]) {
-            void* ptr = nullptr;
-            const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-            if (e != cudaSuccess || !ptr) return record_error(GDN_E_CUDA, "cudaGetSymbolAddress of the scratch failed");
-            g_scratch_ptr[dev] = static_cast<uint8_t*>(ptr);
-        }
-        scratch = g_scratch_ptr[dev];
-    }
+    const int rc = scratch_of_current_device(&scratch);
+    if (rc != GDN_OK) return rc;
 
     gdn::PrepArgs pa;
     std::memset(&pa, 0, sizeof pa);
@@ -122,6 +130,27 @@ int gdn_layer_step_noalloc(const gdn_config* cfg, int32_t n_slots, float* rec_st
 
     const cudaError_t e = gdn::launch_layer_step_v2(pa, ra, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return record_error(GDN_E_CUDA, cudaGetErrorString(e));
+    return gdn::record_ok();
+}
+
+// The device error word of the no-alloc step on the current device.  The kernels record a failed
+// bounds check (1 << GDN_E_BAD_SLOT, 1 << GDN_E_BAD_SEQLENS) or a bounded wait that gave up (1 << 7)
+// there; a call that set a bit returned GDN_OK but its outputs and the state it touched are not to be
+// trusted.  Waits for the device, reads the word and clears it when `reset` is non-zero; allocates
+// nothing.
+int gdn_noalloc_check(int32_t* flags, int reset) {
+    if (!flags) return gdn::record_error(GDN_E_INVALID, "flags is NULL");
+    uint8_t* scratch = nullptr;
+    const int rc = scratch_of_current_device(&scratch);
+    if (rc != GDN_OK) return rc;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess)
+        e = cudaMemcpyFromSymbol(flags, g_noalloc_scratch, sizeof(int32_t), NOALLOC_RECORD_BYTES, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && reset) {
+        const int32_t zero = 0;
+        e = cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof zero, NOALLOC_RECORD_BYTES, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) return gdn::record_error(GDN_E_CUDA, cudaGetErrorString(e));
     return gdn::record_ok();
 }
 
