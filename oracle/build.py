@@ -20,7 +20,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-REF_TREE = Path(os.environ.get("GDN_REFERENCE_TREE", "/root/reference"))
+# The reference tree: $GDN_REFERENCE_TREE, else a directory named "reference" beside this repository.
+REF_TREE = Path(os.environ.get("GDN_REFERENCE_TREE", str(HERE.parent.parent / "reference")))
 METAL_RS = "src/models/metal_gdn.rs"
 
 ORACLE_SO = BUILD / "libgdn_oracle.so"

@@ -48,22 +48,60 @@ def _key(seed: int, stream: str) -> np.uint64:
     return splitmix64(k)[0]
 
 
+_BLOCK = 1 << 18   # elements per block: large arrays are generated block by block, in parallel
+
+
+def _blocks(n: int, fn):
+    """Run fn(start, stop) over [0, n) in blocks; several threads for large n (numpy releases the GIL
+    inside its elementwise loops).  Every element depends only on its own index, so the result does
+    not depend on the block size or the thread count."""
+    spans = [(a, min(a + _BLOCK, n)) for a in range(0, n, _BLOCK)]
+    if len(spans) <= 2:
+        for a, b in spans:
+            fn(a, b)
+        return
+    from concurrent.futures import ThreadPoolExecutor
+    import os
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+        list(ex.map(lambda s: fn(*s), spans))
+
+
+def _uniform_span(key: np.uint64, a: int, b: int) -> np.ndarray:
+    idx = np.arange(a, b, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        bits = splitmix64(idx + key)
+    return (bits >> _U64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+
+
 def uniform(seed: int, stream: str, n: int, lo: float = 0.0, hi: float = 1.0) -> np.ndarray:
     """n float64 uniforms in [lo, hi) for (seed, stream)."""
-    idx = np.arange(n, dtype=np.uint64)
-    with np.errstate(over="ignore"):
-        bits = splitmix64(idx + _key(seed, stream))
-    u = (bits >> _U64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
-    return lo + (hi - lo) * u
+    key = _key(seed, stream)
+    out = np.empty(n, np.float64)
+
+    def fill(a, b):
+        out[a:b] = lo + (hi - lo) * _uniform_span(key, a, b)
+
+    _blocks(n, fill)
+    return out
+
+
+def _normal_span(key: np.uint64, a: int, b: int, std: float) -> np.ndarray:
+    u = _uniform_span(key, 2 * a, 2 * b)
+    r = np.sqrt(-2.0 * np.log1p(-u[0::2]))
+    return std * r * np.cos(2.0 * math.pi * u[1::2])
 
 
 def normal(seed: int, stream: str, n: int, std: float = 1.0) -> np.ndarray:
-    """n float64 normals N(0, std^2) for (seed, stream) (Box-Muller, cosine branch)."""
-    u = uniform(seed, stream, 2 * n)
-    u1 = u[0::2]
-    u2 = u[1::2]
-    r = np.sqrt(-2.0 * np.log1p(-u1))
-    return std * r * np.cos(2.0 * math.pi * u2)
+    """n float64 normals N(0, std^2) for (seed, stream) (Box-Muller, cosine branch): normal j uses
+    uniforms 2j and 2j + 1 of the stream."""
+    key = _key(seed, stream)
+    out = np.empty(n, np.float64)
+
+    def fill(a, b):
+        out[a:b] = _normal_span(key, a, b, std)
+
+    _blocks(n, fill)
+    return out
 
 
 # ---------------------------------------------------------------- bf16 bits
@@ -84,8 +122,16 @@ def bf16_to_f32(h: np.ndarray) -> np.ndarray:
 
 
 def normal_bf16(seed: int, stream: str, shape, std: float = 1.0) -> np.ndarray:
+    """normal(seed, stream, n, std) rounded to f32, then to bf16 bit patterns."""
     n = int(np.prod(shape))
-    return f32_to_bf16(normal(seed, stream, n, std).astype(np.float32)).reshape(shape)
+    key = _key(seed, stream)
+    out = np.empty(n, np.uint16)
+
+    def fill(a, b):
+        out[a:b] = f32_to_bf16(_normal_span(key, a, b, std).astype(np.float32))
+
+    _blocks(n, fill)
+    return out.reshape(shape)
 
 
 # ---------------------------------------------------------------- model config

@@ -66,3 +66,18 @@ def test_oracle_config1_mixer_matches_golden(oracle):
         o, conv, rec = oracle.mixer_step(cfg, w, x[t:t + 1], conv, rec, np.array([0, 1], np.int32))
         outs.append(o)
     _check("orc_cfg1_mixer_64steps", {"out": np.concatenate(outs), "conv": conv, "rec": rec})
+
+
+def test_oracle_long_prompt_layer_matches_full_size_golden(oracle):
+    """The oracle on the long-prompt prefill set (30,016 tokens, one full-width layer) reproduces the
+    committed full-size fixture bit for bit (tests/golden/make_golden_full.py)."""
+    import make_golden_full as mgf
+    meta = json.loads((GOLDEN / "manifest_full.json").read_text())["cfg4_layer"]
+    cfg, w, inp, cu = mgf.cfg4_inputs()
+    out, cs, rs = mgf.run_cfg4(oracle, cfg, w, inp, cu)
+    assert _sha(out) == meta["sha256"]["out"]
+    assert _sha(rs) == meta["sha256"]["rec"]
+    assert _sha(cs) == meta["sha256"]["conv"]
+    full = np.load(GOLDEN / "golden_full.npz")
+    for k, a in mgf.cfg4_samples(out, rs, cu).items():
+        assert np.array_equal(a, full[f"cfg4_layer/{k}"]), k

@@ -130,7 +130,8 @@ def test_stack_step_prefill_then_decode(gdn, synth, oracle):
 
 
 def test_config1_golden_mixer_64_decode_steps(gdn, synth, oracle):
-    """one layer with projections, B=1, zero state, 64 decode steps of x ~ N(0,1)."""
+    """Single-sequence decode: one full-width layer with projections, B=1, zero state, 64 decode steps of
+    x ~ N(0,1), against the committed fixture."""
     gdir = Path(__file__).resolve().parent / "golden"
     sys.path.insert(0, str(gdir))
     import make_golden as mg
