@@ -70,6 +70,9 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--sweep", default=None, help="comma-separated batch sizes of the sweep (default 1..2048)")
+    p.add_argument("--decode-kernel", type=int, default=0,
+                   help="gdn_set_decode_kernel mode: 0 by batch size, 1 split, 2 fused, 3 two-kernel")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-mixer", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
@@ -675,7 +678,9 @@ def run_ours(args):
 
     cfg = synth.GdnConfig(n_layers=N_LAYERS)
     B = args.batch
-    sweep_bs = [] if (args.no_sweep or world > 1 or args.prefill_only) else [1, 2, 4, 8, 16, 32, 64, 256, 1024, 2048]
+    sweep_bs = [] if (args.no_sweep or world > 1 or args.prefill_only) else (
+        [int(x) for x in args.sweep.split(",")] if args.sweep else [1, 2, 4, 8, 16, 32, 64, 256, 1024, 2048])
+    abi.check(lib.gdn_set_decode_kernel(args.decode_kernel), "gdn_set_decode_kernel")
     n_slots = max([B] + sweep_bs)
     if args.prefill_only:
         n_slots = max(n_slots, len(args.prefill_lens.split(",")) if args.prefill_lens else len(CONFIG4_LENS))

@@ -72,8 +72,12 @@ typedef struct gdn_config {
 typedef struct gdn_layer_weights {
     const gdn_bf16* conv_w; /* [D][K]  conv1d.weight */
     const float* A_log;     /* [Hv]    A_log */
-    const float* dt_bias;   /* [Hv]    dt_bias */
+    const float* dt_bias;   /* [Hv]    dt_bias, as f32 values (a bf16 parameter widened exactly) */
     const gdn_bf16* norm_w; /* [dv]    norm.weight (RMSNormGated) */
+    /* Non-zero when the checkpoint stores dt_bias in bf16.  MLX then adds a + dt_bias and takes its exp
+     * as bf16 ops, each rounded to bf16, before the f32 log(. + 1) (compiled_ops.rs:36-40); with 0 the
+     * add and exp are f32, as for an f32 dt_bias. */
+    int32_t dt_bias_bf16;
 } gdn_layer_weights;
 
 /* Projection outputs feeding one layer step and its output, packed by token.
@@ -281,6 +285,27 @@ GDN_API int gdn_gated_delta_kernel(const gdn_bf16* q, const gdn_bf16* k, const g
  * -> beta [N][Hv] bf16, g [N][Hv] f32.  Device pointers. */
 GDN_API int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
                const float* dt_bias, gdn_bf16* beta, float* g, void* stream);
+
+/* gdn_beta_g for a dt_bias stored in bf16 (dt_bias_bf16 != 0, see gdn_layer_weights): the same
+ * closure (compiled_ops.rs:12-49) with a + dt_bias and its exp rounded to bf16. */
+GDN_API int gdn_beta_g_ex(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
+                          const float* dt_bias, int32_t dt_bias_bf16, gdn_bf16* beta, float* g, void* stream);
+
+/* Which kernel runs decode-only calls (n_tokens == n_seq) of gdn_layer_step and the entry points
+ * built on it: 0 (default) by batch size -- fewer than 64 sequences the split kernel (each
+ * (sequence, v-head) state tile split by dv rows over 4 CTAs of a cluster; Hv/Hk <= 2), 64 or
+ * more the fused one-kernel step; 1 always the split kernel; 2 always the fused kernel; 3 the
+ * two-kernel step (prep, then recurrence).  Results agree within f32 rounding.  Process-wide;
+ * set it before capturing graphs.  (A tuning and test control of this library; the reference
+ * has one kernel, metal_gdn.rs:170-218.) */
+GDN_API int gdn_set_decode_kernel(int mode);
+
+/* Failure-detection tests only (no counterpart in the reference).  Shortens the bound of the split
+ * kernel's state wait to `wait_ns` and makes CTA `skip_block` of it arm its barrier without
+ * issuing the copy, so that wait runs out: the kernel records 1 << 7 in the pool's error word
+ * (gdn_pool_check), leaves that CTA's 32 state rows and outputs unwritten and returns.
+ * gdn_test_set_wait_fault(-1, 2000000000) restores normal operation.  Process-wide. */
+GDN_API int gdn_test_set_wait_fault(int32_t skip_block, int64_t wait_ns);
 
 /* ------------------------------------------------------- no-allocation variant
  * No counterpart in the reference.  The fused layer step of gdn_layer_step for

@@ -143,16 +143,26 @@ void orc_linear(const uint16_t* x, const uint16_t* w, int64_t M, int32_t N, int3
     free(xf);
 }
 
-/* compiled_ops.rs:12-49.  ab row = [b (Hv) | a (Hv)] (merged order, qwen3_5.rs:583). */
+/* compiled_ops.rs:12-49.  ab row = [b (Hv) | a (Hv)] (merged order, qwen3_5.rs:583).
+ * dt_bf16 != 0: the checkpoint stores dt_bias in bf16 (given here widened to f32).  MLX then computes
+ * add(a_raw, dt_bias) and exp of it as bf16 ops (each rounded to bf16, :36-37); add(exp_sum, 1.0f)
+ * promotes to f32 (:38-39).  With an f32 dt_bias the add promotes to f32 and everything after is f32. */
 void orc_gates(const uint16_t* ab, int64_t ld_ab, int64_t n_tok, int32_t hv, const float* A_log,
-               const float* dt_bias, float* g, uint16_t* beta) {
+               const float* dt_bias, int32_t dt_bf16, float* g, uint16_t* beta) {
     for (int64_t t = 0; t < n_tok; ++t)
         for (int32_t h = 0; h < hv; ++h) {
             float b = bf(ab[t * ld_ab + h]);
             float a = bf(ab[t * ld_ab + hv + h]);
             beta[t * hv + h] = tobf(sigmoidf_(b));
             float s = a + dt_bias[h];
-            float sp = logf(expf(s) + 1.0f);
+            float es;
+            if (dt_bf16) {
+                s = rnd(s);
+                es = rnd(expf(s));
+            } else {
+                es = expf(s);
+            }
+            float sp = logf(es + 1.0f);
             float e = expf(A_log[h]);
             g[t * hv + h] = expf(-(e * sp));
         }
@@ -297,6 +307,7 @@ typedef struct orc_layer_w {
     const float* A_log;      /* [Hv] */
     const float* dt_bias;    /* [Hv] */
     const uint16_t* norm_w;  /* [dv] */
+    int32_t dt_bias_bf16;    /* dt_bias stored in bf16 by the checkpoint (see orc_gates) */
 } orc_layer_w;
 
 /*
@@ -344,7 +355,7 @@ int orc_layer_step(const orc_cfg* c, const orc_layer_w* w, const uint16_t* qkv, 
         memcpy(vv + t * hv * dv, row + 2 * hk * dk, sizeof(uint16_t) * hv * dv);
     }
     /* 3. gates */
-    orc_gates(ab, ld_ab, N, hv, w->A_log, w->dt_bias, g, beta);
+    orc_gates(ab, ld_ab, N, hv, w->A_log, w->dt_bias, w->dt_bias_bf16, g, beta);
     /* 4. recurrence */
     orc_recurrence_packed(qn, kn, vv, g, beta, rec_state, cu, n_seq, hk, hv, dk, dv, y);
     /* 5. gated RMSNorm: silu(z) * rms_norm(y, norm_w, eps) */

@@ -36,7 +36,8 @@ class OrcCfg(C.Structure):
 
 
 class OrcLayerW(C.Structure):
-    _fields_ = [("conv_w", C.c_void_p), ("A_log", C.c_void_p), ("dt_bias", C.c_void_p), ("norm_w", C.c_void_p)]
+    _fields_ = [("conv_w", C.c_void_p), ("A_log", C.c_void_p), ("dt_bias", C.c_void_p), ("norm_w", C.c_void_p),
+                ("dt_bias_bf16", C.c_int32)]
 
 
 class OrcMixerW(C.Structure):
@@ -60,7 +61,7 @@ def lib():
         L.orc_recurrence_packed.argtypes = [_u16p, _u16p, _u16p, _f32p, _u16p, _f32p, _i32p, C.c_int32, C.c_int32,
                                             C.c_int32, C.c_int32, C.c_int32, _u16p]
         L.orc_recurrence_packed.restype = C.c_int
-        L.orc_gates.argtypes = [_u16p, C.c_int64, C.c_int64, C.c_int32, _f32p, _f32p, _f32p, _u16p]
+        L.orc_gates.argtypes = [_u16p, C.c_int64, C.c_int64, C.c_int32, _f32p, _f32p, C.c_int32, _f32p, _u16p]
         L.orc_gates.restype = None
         L.orc_rms_norm.argtypes = [_u16p, _u16p, C.c_int64, C.c_int32, C.c_float, _u16p]
         L.orc_rms_norm.restype = None
@@ -160,12 +161,15 @@ def ref_recurrence(q, k, v, g, beta, state, T, B, hk, hv, dk, dv):
     return y, st_out
 
 
-def gates(ab, A_log, dt_bias, hv):
+def gates(ab, A_log, dt_bias, hv, dt_bias_bf16=False):
+    """compiled_beta_g: (g f32, beta bf16).  dt_bias_bf16: the checkpoint stores dt_bias in bf16 (passed
+    widened to f32), so a + dt_bias and its exp round to bf16 as MLX computes them."""
     ab = _c(ab, np.uint16)
     n = ab.shape[0]
     g = np.zeros((n, hv), np.float32)
     beta = np.zeros((n, hv), np.uint16)
-    lib().orc_gates(ab, ab.shape[1], n, hv, _c(A_log, np.float32), _c(dt_bias, np.float32), g, beta)
+    lib().orc_gates(ab, ab.shape[1], n, hv, _c(A_log, np.float32), _c(dt_bias, np.float32),
+                    1 if dt_bias_bf16 else 0, g, beta)
     return g, beta
 
 
@@ -236,7 +240,7 @@ def _layer_w(w):
     keep = {k: _c(w[k], np.uint16 if k in ("conv_w", "norm_w") else np.float32)
             for k in ("conv_w", "A_log", "dt_bias", "norm_w")}
     s = OrcLayerW(keep["conv_w"].ctypes.data, keep["A_log"].ctypes.data, keep["dt_bias"].ctypes.data,
-                  keep["norm_w"].ctypes.data)
+                  keep["norm_w"].ctypes.data, 1 if w.get("dt_bias_bf16", False) else 0)
     return s, keep
 
 

@@ -41,7 +41,7 @@ class GdnConfigC(C.Structure):
 
 
 class GdnLayerWeightsC(C.Structure):
-    _fields_ = [("conv_w", _vp), ("A_log", _vp), ("dt_bias", _vp), ("norm_w", _vp)]
+    _fields_ = [("conv_w", _vp), ("A_log", _vp), ("dt_bias", _vp), ("norm_w", _vp), ("dt_bias_bf16", _i32)]
 
 
 class GdnStepIOC(C.Structure):
@@ -100,9 +100,12 @@ SIGNATURES = {
     "gdn_gated_delta_kernel": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                       _vp]),
     "gdn_beta_g": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gdn_beta_g_ex": (_int, [_vp, _i64, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _vp]),
     "gdn_layer_step_noalloc": (_int, [C.POINTER(GdnConfigC), _i32, _vp, _vp, C.POINTER(GdnLayerWeightsC),
                                       C.POINTER(GdnStepIOC), _vp, _vp, _i32, _i32, _vp]),
     "gdn_noalloc_check": (_int, [C.POINTER(_i32), _int]),
+    "gdn_set_decode_kernel": (_int, [_int]),
+    "gdn_test_set_wait_fault": (_int, [_i32, _i64]),
     # include/gdn_host.h
     "gdn_pack_step": (_int, [C.POINTER(GdnStepEntryC), _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gdn_sched_create": (_int, [C.POINTER(GdnSchedConfigC), C.POINTER(_vp)]),

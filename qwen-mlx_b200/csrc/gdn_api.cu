@@ -438,6 +438,7 @@ static int layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, co
     pa.rec_cap = p->rec_cap;
     pa.err = p->err;
     pa.tables_stable = (flags & GDN_STEP_TABLES_STABLE) ? 1 : 0;
+    pa.dt_bf16 = w->dt_bias_bf16 ? 1 : 0;
     gdn::RecurArgs ra;
     std::memset(&ra, 0, sizeof ra);
     ra.rec = rec;
@@ -734,13 +735,32 @@ int gdn_gated_delta_kernel(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16*
     return ok();
 }
 
-int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
-               const float* dt_bias, gdn_bf16* beta, float* g, void* stream) {
+int gdn_set_decode_kernel(int mode) {
+    if (mode < 0 || mode > 3) return fail(GDN_E_INVALID, "decode kernel mode %d not in 0..3", mode);
+    gdn::g_decode_kernel = mode;
+    return ok();
+}
+
+int gdn_test_set_wait_fault(int32_t skip_block, int64_t wait_ns) {
+    if (wait_ns <= 0) return fail(GDN_E_INVALID, "wait_ns must be positive");
+    gdn::g_split_ctl.skip_block = skip_block;
+    gdn::g_split_ctl.wait_ns = (unsigned long long)wait_ns;
+    return ok();
+}
+
+int gdn_beta_g_ex(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
+                  const float* dt_bias, int32_t dt_bias_bf16, gdn_bf16* beta, float* g, void* stream) {
     if (!ab || !A_log || !dt_bias || !beta || !g) return fail(GDN_E_INVALID, "NULL tensor");
     if (n_tokens < 0 || hv <= 0 || ld_ab < 2 * hv) return fail(GDN_E_INVALID, "bad shape");
-    cudaError_t e = gdn::launch_beta_g(ab, ld_ab, n_tokens, hv, A_log, dt_bias, beta, g, (cudaStream_t)stream);
+    cudaError_t e = gdn::launch_beta_g(ab, ld_ab, n_tokens, hv, A_log, dt_bias, dt_bias_bf16 ? 1 : 0, beta, g,
+                                       (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_beta_g launch");
     return ok();
+}
+
+int gdn_beta_g(const gdn_bf16* ab, int64_t ld_ab, int32_t n_tokens, int32_t hv, const float* A_log,
+               const float* dt_bias, gdn_bf16* beta, float* g, void* stream) {
+    return gdn_beta_g_ex(ab, ld_ab, n_tokens, hv, A_log, dt_bias, 0, beta, g, stream);
 }
 
 }  // extern "C"

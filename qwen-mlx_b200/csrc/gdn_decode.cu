@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepArgs a) {
     // ---- gates (compiled_beta_g)
     if (tid < ratio) {
         const int hv = hk * ratio + tid;
-        const float sp = logf(expf(gb_a + gb_dt) + 1.0f);
+        const float sp = gate_softplus(gb_a, gb_dt, a.dt_bf16);
         float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
         const float logdecay = -(expf(gb_alog) * sp);
         gb[0] = expf(logdecay);
@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(256) gdn_prep_tile_kernel(const PrepArgs a) {
         const int hv = hk * ratio + idx % ratio;
         const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
         const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
-        const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+        const float sp = gate_softplus(av, a.dt_bias[hv], a.dt_bf16);
         const float logdecay = -(expf(a.A_log[hv]) * sp);
         float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
         gb[0] = expf(logdecay);
@@ -743,7 +743,7 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
             const int hv = hv0 + half;
             const float b = bf2f(a.ab[(long long)n * a.ld_ab + hv]);
             const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
-            const float sp = logf(expf(av + a.dt_bias[hv]) + 1.0f);
+            const float sp = gate_softplus(av, a.dt_bias[hv], a.dt_bf16);
             const float logdecay = -(expf(a.A_log[hv]) * sp);
             float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
             gb[0] = expf(logdecay);
@@ -1001,6 +1001,9 @@ __global__ void __launch_bounds__(K2_THREADS, 1) gdn_recur_kernel(const RecurArg
 
 static int g_num_sms[64] = {0};
 
+int g_decode_kernel = 0;
+SplitCtl g_split_ctl = {2000000000ull, -1};
+
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1015,9 +1018,15 @@ cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStre
         g_num_sms[dev] = sms;
     }
     if (p.n_tokens == 0 || r.n_seq == 0) return cudaSuccess;
-    // one token per sequence on average, and enough sequences that (sequence, k-head) items balance over
-    // the SMs: the fused one-kernel decode step (below that the finer (sequence, v-head) items of K2 win)
-    if (p.n_tokens == p.n_seq && r.wy_min_t == 0 && r.n_seq >= FUSED_MIN_SEQ) return launch_decode_fused(p, r, stream);
+    // One token per sequence on average: few sequences take the split kernel (4 CTAs per (sequence, v-head)
+    // tile), many the fused one-kernel step ((sequence, k-head) items balance over the SMs there).
+    if (p.n_tokens == p.n_seq && r.wy_min_t == 0) {
+        const bool split_ok = r.hv % r.hk == 0 && r.hv / r.hk <= 2;
+        const int mode = g_decode_kernel;
+        if (split_ok && (mode == 1 || (mode == 0 && r.n_seq < SPLIT_MAX_SEQ)))
+            return launch_decode_split(p, r, g_split_ctl, stream);
+        if (mode == 2 || (mode == 0 && r.n_seq >= FUSED_MIN_SEQ)) return launch_decode_fused(p, r, stream);
+    }
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

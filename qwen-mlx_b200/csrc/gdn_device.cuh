@@ -29,6 +29,17 @@ __device__ __forceinline__ float sigmoid_f32(float x) { return __frcp_rn(1.0f + 
 // nn::silu on a bf16 value: computed in f32, rounded once to bf16.
 __device__ __forceinline__ float silu_bf(float x) { return rbf(x * sigmoid_f32(x)); }
 
+// softplus(a + dt_bias) of compiled_beta_g (compiled_ops.rs:36-40).  With an f32 dt_bias, MLX promotes
+// a + dt_bias to f32; with a bf16 dt_bias (dt_bf16) the add and its exp are bf16 ops, each rounded to
+// bf16, and the + 1 (an f32 constant) promotes back to f32.
+__device__ __forceinline__ float gate_softplus(float a, float dt, bool dt_bf16) {
+    if (dt_bf16) {
+        const float s = rbf(a + dt);
+        return logf(rbf(expf(s)) + 1.0f);
+    }
+    return logf(expf(a + dt) + 1.0f);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -68,6 +79,59 @@ __device__ __forceinline__ float reduce_scatter16(const float (&p)[16], int lane
     float keep = b1 ? a2[1] : a2[0];
     float a1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
     return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+}
+
+// Reduce-scatter of 8 per-lane partials across the warp: returns the full 32-lane sum of
+// partial r = (lane >> 2) & 7 (every lane of a group of 4 holds the same value).
+__device__ __forceinline__ float reduce_scatter8(const float (&p)[8], int lane) {
+    float a4[4];
+    const bool b4 = lane & 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float send = b4 ? p[j] : p[j + 4];
+        const float keep = b4 ? p[j + 4] : p[j];
+        a4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float a2[2];
+    const bool b3 = lane & 8;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const float send = b3 ? a4[j] : a4[j + 2];
+        const float keep = b3 ? a4[j + 2] : a4[j];
+        a2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    const bool b2 = lane & 4;
+    const float send = b2 ? a2[0] : a2[1];
+    float a1 = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+    return a1;
+}
+
+// The 4 conv taps of channel ch (conv weight [D][4] bf16, 8-byte aligned rows).
+__device__ __forceinline__ void fd_unpack_w(const uint16_t* cw, int ch, float (&w)[4]) {
+    const uint2 wu = __ldg(reinterpret_cast<const uint2*>(cw + (size_t)ch * KC));
+    w[0] = __uint_as_float(wu.x << 16);
+    w[1] = __uint_as_float(wu.x & 0xffff0000u);
+    w[2] = __uint_as_float(wu.y << 16);
+    w[3] = __uint_as_float(wu.y & 0xffff0000u);
+}
+
+// silu(sum w x) with the decode (bf16 products + bf16 sum) or conv1d (f32) rounding.
+__device__ __forceinline__ float fd_conv_silu(const float (&x)[4], const float (&w)[4], bool decode) {
+    float acc;
+    if (decode) {
+        acc = rbf(x[0] * w[0]);
+        acc = acc + rbf(x[1] * w[1]);
+        acc = acc + rbf(x[2] * w[2]);
+        acc = acc + rbf(x[3] * w[3]);
+    } else {
+        acc = x[0] * w[0];
+        acc = acc + x[1] * w[1];
+        acc = acc + x[2] * w[2];
+        acc = acc + x[3] * w[3];
+    }
+    return silu_bf(rbf(acc));
 }
 
 }  // namespace gdn

@@ -93,31 +93,6 @@ __device__ __forceinline__ void fd_taps(const PrepArgs& p, const uint16_t* cs, i
     }
 }
 
-__device__ __forceinline__ void fd_unpack_w(const uint16_t* cw, int ch, float (&w)[4]) {
-    const uint2 wu = __ldg(reinterpret_cast<const uint2*>(cw + (size_t)ch * KC));
-    w[0] = __uint_as_float(wu.x << 16);
-    w[1] = __uint_as_float(wu.x & 0xffff0000u);
-    w[2] = __uint_as_float(wu.y << 16);
-    w[3] = __uint_as_float(wu.y & 0xffff0000u);
-}
-
-// silu(sum w x) with the decode (bf16 products + bf16 sum) or conv1d (f32) rounding.
-__device__ __forceinline__ float fd_conv_silu(const float (&x)[4], const float (&w)[4], bool decode) {
-    float acc;
-    if (decode) {
-        acc = rbf(x[0] * w[0]);
-        acc = acc + rbf(x[1] * w[1]);
-        acc = acc + rbf(x[2] * w[2]);
-        acc = acc + rbf(x[3] * w[3]);
-    } else {
-        acc = x[0] * w[0];
-        acc = acc + x[1] * w[1];
-        acc = acc + x[2] * w[2];
-        acc = acc + x[3] * w[3];
-    }
-    return silu_bf(rbf(acc));
-}
-
 // The conv window of channel ch after a segment of T >= 2 tokens: the last K-1 rows of [window; tokens].
 __device__ __forceinline__ void fd_window_writeback(const PrepArgs& p, uint16_t* cs, int ch, int t0, int T) {
     uint16_t w[KC - 1];
@@ -128,33 +103,6 @@ __device__ __forceinline__ void fd_window_writeback(const PrepArgs& p, uint16_t*
     }
 #pragma unroll
     for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * p.D + ch] = w[j];
-}
-
-// Reduce-scatter of 8 per-lane partials across the warp: returns the full 32-lane sum of
-// partial r = (lane >> 2) & 7 (every lane of a group of 4 holds the same value).
-__device__ __forceinline__ float reduce_scatter8(const float (&p)[8], int lane) {
-    float a4[4];
-    const bool b4 = lane & 16;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float send = b4 ? p[j] : p[j + 4];
-        const float keep = b4 ? p[j + 4] : p[j];
-        a4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-    float a2[2];
-    const bool b3 = lane & 8;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const float send = b3 ? a4[j] : a4[j + 2];
-        const float keep = b3 ? a4[j + 2] : a4[j];
-        a2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-    const bool b2 = lane & 4;
-    const float send = b2 ? a2[0] : a2[1];
-    float a1 = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
-    a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
-    a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
-    return a1;
 }
 
 // All threads meet; then thread 0 waits (bounded) for state copies issued but never consumed,
@@ -359,7 +307,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
                 }
                 float g_dec = 0.f, g_beta = 0.f, g_log = 0.f;
                 if (pt < ratio) {
-                    const float sp = logf(expf(gb_a + gb_dt) + 1.0f);
+                    const float sp = gate_softplus(gb_a, gb_dt, p.dt_bf16);
                     g_log = -(expf(gb_alog) * sp);
                     g_dec = expf(g_log);
                     g_beta = rbf(sigmoid_f32(gb_b));
@@ -483,7 +431,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) gdn_decode_fused_kernel(const P
                     if (pt == 0) {
                         const float b = bf2f(p.ab[n * p.ld_ab + hv]);
                         const float av = bf2f(p.ab[n * p.ld_ab + r.hv + hv]);
-                        const float sp = logf(expf(av + p.dt_bias[hv]) + 1.0f);
+                        const float sp = gate_softplus(av, p.dt_bias[hv], p.dt_bf16);
                         const float logdecay = -(expf(p.A_log[hv]) * sp);
                         float* gb = reinterpret_cast<float*>(rec + 1024);
                         gb[0] = expf(logdecay);

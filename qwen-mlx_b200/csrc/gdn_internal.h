@@ -53,6 +53,7 @@ struct PrepArgs {
     long long rec_cap;
     int32_t* err;
     int32_t tables_stable;       // routing tables and this layer's conv state may be read before the PDL wait
+    int32_t dt_bf16;             // dt_bias is a bf16 parameter: a + dt_bias and its exp round to bf16 (gate_softplus)
 };
 
 struct RecurArgs {
@@ -83,6 +84,19 @@ cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStre
 // one persistent kernel (gdn_fused.cu).
 constexpr int FUSED_MIN_SEQ = 64;
 cudaError_t launch_decode_fused(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);
+// Decode-only calls of few sequences, Hv/Hk <= 2: each (sequence, v-head) tile split by dv rows over 4 CTAs of a
+// cluster (gdn_split.cu).
+struct SplitCtl {
+    unsigned long long wait_ns;  // bound of the state-slice wait (2 s; shortened only by failure-detection tests)
+    int skip_block;              // failure-detection tests: this CTA's state copy is never issued (-1: none)
+};
+cudaError_t launch_decode_split(const PrepArgs& p, const RecurArgs& r, const SplitCtl& ctl, cudaStream_t stream);
+// Which decode-only kernel launch_layer_step_v2 uses (gdn_set_decode_kernel): 0 by batch size, 1 split, 2 fused
+// (>= 1 sequence), 3 the two-kernel step.
+extern int g_decode_kernel;
+// Sequences below which decode-only calls take the split kernel (by-batch-size selection).
+constexpr int SPLIT_MAX_SEQ = 8;
+extern SplitCtl g_split_ctl;
 
 // Projections and the decoder pre-norm / residual (gdn_proj.cu).
 struct GemmCtx;
@@ -126,6 +140,6 @@ int record_error(int code, const char* msg);
 int record_ok();
 cudaError_t launch_recurrence(const StepArgs& a, cudaStream_t stream);
 cudaError_t launch_beta_g(const uint16_t* ab, long long ld_ab, int n_tokens, int hv, const float* A_log,
-                          const float* dt_bias, uint16_t* beta, float* g, cudaStream_t stream);
+                          const float* dt_bias, int dt_bf16, uint16_t* beta, float* g, cudaStream_t stream);
 
 }  // namespace gdn

@@ -103,6 +103,7 @@ int gdn_layer_step_noalloc(const gdn_config* cfg, int32_t n_slots, float* rec_st
     pa.conv_w = w->conv_w;
     pa.A_log = w->A_log;
     pa.dt_bias = w->dt_bias;
+    pa.dt_bf16 = w->dt_bias_bf16 ? 1 : 0;
     pa.slot_ids = slot_ids;
     pa.cu_seqlens = cu_seqlens;
     pa.n_seq = n_seq; pa.n_slots = n_slots; pa.n_tokens = n_tokens;

@@ -141,4 +141,21 @@ __device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Thread-block clusters.  Every thread of every CTA of the cluster arrives, then waits (.aligned: called
+// from warp-uniform control flow); arrive releases this thread's earlier memory accesses to the threads
+// that pass the matching wait.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+
+// Store one f32 into the shared memory of CTA `rank` of this cluster, at the address `local` has in
+// this CTA (distributed shared memory; plain store, no multicast).
+__device__ __forceinline__ void st_cluster_f32(const void* local, uint32_t rank, float v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(remote), "f"(v) : "memory");
+}
+
 }  // namespace gdn

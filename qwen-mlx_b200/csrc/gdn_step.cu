@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(NT, 2) gdn_recurrence_kernel(const StepArgs a)
 
 // beta = bf16(sigmoid(b)), g = exp(-exp(A_log) * softplus(a + dt_bias))   (compiled_ops.rs:30-43)
 __global__ void beta_g_kernel(const uint16_t* __restrict__ ab, long long ld_ab, int n_tokens, int hv,
-                              const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                              const float* __restrict__ A_log, const float* __restrict__ dt_bias, int dt_bf16,
                               uint16_t* __restrict__ beta, float* __restrict__ g) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)n_tokens * hv) return;
@@ -115,7 +115,7 @@ __global__ void beta_g_kernel(const uint16_t* __restrict__ ab, long long ld_ab, 
     const float b = bf2f(ab[t * ld_ab + h]);
     const float av = bf2f(ab[t * ld_ab + hv + h]);
     beta[i] = f2bf(sigmoid_f32(b));
-    const float sp = logf(expf(av + dt_bias[h]) + 1.0f);
+    const float sp = gate_softplus(av, dt_bias[h], dt_bf16 != 0);
     g[i] = expf(-(expf(A_log[h]) * sp));
 }
 
@@ -125,12 +125,12 @@ cudaError_t launch_recurrence(const StepArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_beta_g(const uint16_t* ab, long long ld_ab, int n_tokens, int hv, const float* A_log,
-                          const float* dt_bias, uint16_t* beta, float* g, cudaStream_t stream) {
+                          const float* dt_bias, int dt_bf16, uint16_t* beta, float* g, cudaStream_t stream) {
     const long long n = (long long)n_tokens * hv;
     if (n == 0) return cudaSuccess;
     const int threads = 256;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
-    beta_g_kernel<<<blocks, threads, 0, stream>>>(ab, ld_ab, n_tokens, hv, A_log, dt_bias, beta, g);
+    beta_g_kernel<<<blocks, threads, 0, stream>>>(ab, ld_ab, n_tokens, hv, A_log, dt_bias, dt_bf16, beta, g);
     return cudaGetLastError();
 }
 

@@ -70,13 +70,14 @@ def gated_delta_kernel(q, k, v, g, beta, state, seq_len, batch, hk, hv, dk, dv, 
     return y, new_state
 
 
-def beta_g(ab, A_log, dt_bias, hv, stream=None):
-    """compiled_beta_g over an [N, >=2*Hv] (b | a) buffer: returns (beta bf16 [N,Hv], g f32 [N,Hv])."""
+def beta_g(ab, A_log, dt_bias, hv, stream=None, dt_bias_bf16=False):
+    """compiled_beta_g over an [N, >=2*Hv] (b | a) buffer: returns (beta bf16 [N,Hv], g f32 [N,Hv]).
+    dt_bias_bf16: dt_bias is a bf16 parameter (given widened to f32); a + dt_bias and its exp round to bf16."""
     n = ab.shape[0]
     beta = torch.empty((n, hv), dtype=torch.bfloat16, device=ab.device)
     g = torch.empty((n, hv), dtype=torch.float32, device=ab.device)
-    abi.call("gdn_beta_g", _ptr(ab), ab.stride(0), n, hv, _ptr(A_log), _ptr(dt_bias), _ptr(beta), _ptr(g),
-             _stream(stream))
+    abi.call("gdn_beta_g_ex", _ptr(ab), ab.stride(0), n, hv, _ptr(A_log), _ptr(dt_bias), 1 if dt_bias_bf16 else 0,
+             _ptr(beta), _ptr(g), _stream(stream))
     return beta, g
 
 
@@ -88,8 +89,10 @@ class LayerWeights:
         self.A_log = f32_to_device(w["A_log"], device)
         self.dt_bias = f32_to_device(w["dt_bias"], device)
         self.norm_w = bf16_to_device(w["norm_w"], device)
+        # a checkpoint that stores dt_bias in bf16 (loader: "dt_bias_bf16") gets the bf16 gate arithmetic
+        self.dt_bias_bf16 = bool(w.get("dt_bias_bf16", False))
         self.c = abi.GdnLayerWeightsC(self.conv_w.data_ptr(), self.A_log.data_ptr(), self.dt_bias.data_ptr(),
-                                      self.norm_w.data_ptr())
+                                      self.norm_w.data_ptr(), 1 if self.dt_bias_bf16 else 0)
 
 
 def tile_weight(w, stream=None):

@@ -20,8 +20,10 @@ weight dict the rest of the package uses: `conv_w` [D, K] bf16, `A_log`, `dt_bia
 and either bf16 `w_qkv`, `w_z`, `w_b`, `w_a`, `w_out` or, for a quantized checkpoint, `q4_in` / `q4_out` =
 (w_q uint32, scales, biases) with the in-projection rows merged in the order `[qkv; z; b; a]` (the reference's
 `[qkv; z]` then `[b; a]`).  bf16 tensors are numpy uint16 bit patterns.  A_log and dt_bias are widened to f32
-(the kernels compute the gates in f32; a checkpoint that stores them in bf16 makes the reference add `a + dt_bias`
-in bf16, one rounding the f32 path does not have).
+(exactly), and `dt_bias_bf16` records whether the checkpoint stores dt_bias in bf16: the reference then adds
+`a + dt_bias` and takes its exp as bf16 ops (compiled_ops.rs:36-37), and the kernels and the oracle reproduce those
+two roundings when the flag is set.  (A_log is cast to f32 by the reference itself, :41, so its dtype changes
+nothing.)
 """
 from __future__ import annotations
 
@@ -189,6 +191,7 @@ def load_gdn_layers(model_dir) -> tuple[GdnConfig, list[int], list[dict]]:
             "conv_w": np.ascontiguousarray(conv),
             "A_log": _f32(ck, f"{p}.A_log"),
             "dt_bias": _f32(ck, f"{p}.dt_bias"),
+            "dt_bias_bf16": ck.dtype(f"{p}.dt_bias") == "BF16",
             "norm_w": _bf16(ck, f"{p}.norm.weight"),
             "pre_w": _bf16(ck, f"{PREFIX}.{l}.input_layernorm.weight"),
         }

@@ -135,3 +135,21 @@ def test_beta_g_kernel(gdn, synth, oracle):
     assert rel_l2(g.cpu().numpy(), g_ref) < 1e-5
     mism = np.count_nonzero(gdn.bf16_to_host(beta) != beta_ref)
     assert mism <= 2   # bf16 rounding of sigmoid may flip only on ulp-level exp differences
+
+
+def test_beta_g_kernel_bf16_dt_bias(gdn, synth, oracle):
+    """gdn_beta_g_ex with a bf16 dt_bias: the add and its exp round to bf16, as in the oracle's bf16 mode."""
+    hv = 32
+    ab = synth.normal_bf16(5, "bg16", (41, 2 * hv))
+    A_log = synth.uniform(5, "A", hv, 0.0, np.log(16.0)).astype(np.float32)
+    dt = synth.bf16_to_f32(synth.f32_to_bf16(synth.uniform(5, "dt", hv, -1, 1).astype(np.float32)))
+    dev = torch.device("cuda:0")
+    beta, g = gdn.beta_g(gdn.bf16_to_device(ab, dev), gdn.f32_to_device(A_log, dev), gdn.f32_to_device(dt, dev), hv,
+                         dt_bias_bf16=True)
+    torch.cuda.synchronize()
+    g_ref, beta_ref = oracle.gates(ab, A_log, dt, hv, dt_bias_bf16=True)
+    g_f32, _ = oracle.gates(ab, A_log, dt, hv)
+    assert rel_l2(g.cpu().numpy(), g_ref) < 1e-5
+    assert rel_l2(g.cpu().numpy(), g_f32) > 1e-4        # the f32 gates are measurably different
+    assert np.count_nonzero(gdn.bf16_to_host(beta) != beta_ref) <= 2
+

@@ -85,6 +85,7 @@ def test_loader_selection_merge_and_layout(synth, loader, tmp_path, quantized):
     for l, w in zip(layers, ws):
         assert np.array_equal(w["conv_w"], ref[(l, "conv")].reshape(-1, 4))
         assert w["dt_bias"].dtype == np.float32 and np.allclose(w["dt_bias"], np.linspace(-1, 1, HV), atol=1e-2)
+        assert w["dt_bias_bf16"] is True                 # stored bf16: the bf16 gate arithmetic applies
         assert np.all(synth.bf16_to_f32(w["norm_w"]) == 1.5)
         order = ["in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a"]   # [qkv; z] then [b; a]
         if quantized:

@@ -130,6 +130,28 @@ def test_gates_formula(oracle, synth):
     assert np.all((g > 0) & (g < 1))
 
 
+def test_gates_bf16_dt_bias_rounds_the_add_and_exp(oracle, synth):
+    """A checkpoint that stores dt_bias in bf16: MLX adds a_raw + dt_bias and exponentiates in bf16
+    (compiled_ops.rs:36-37), then adds the f32 constant 1 in f32 (:38-39).  The oracle's bf16 mode equals
+    that two-rounding restatement and differs from the f32 mode."""
+    hv = 32
+    ab = synth.normal_bf16(2, "gab16", (64, 2 * hv))
+    A_log = synth.uniform(2, "A", hv, 0.0, np.log(16.0)).astype(np.float32)
+    dt = synth.bf16_to_f32(synth.f32_to_bf16(synth.uniform(2, "dt", hv, -1, 1).astype(np.float32)))
+    g16, beta16 = oracle.gates(ab, A_log, dt, hv, dt_bias_bf16=True)
+    g32, beta32 = oracle.gates(ab, A_log, dt, hv)
+    f = synth.bf16_to_f32
+    r = lambda x: f(synth.f32_to_bf16(np.asarray(x, np.float32)))
+    a = f(ab[:, hv:])
+    s = r(a + dt[None, :])
+    es = r(np.exp(s.astype(np.float64)).astype(np.float32))
+    sp = np.log(es.astype(np.float64) + 1.0)
+    g_ref = np.exp(-np.exp(A_log.astype(np.float64)) * sp)
+    assert rel_l2(g16, g_ref) < 1e-6
+    assert np.array_equal(beta16, beta32)            # beta does not involve dt_bias
+    assert np.count_nonzero(g16 != g32) > g16.size // 4   # the two roundings change most gates
+
+
 def test_conv_one_hot_tap_kat(oracle, synth):
     """A conv weight with a single 1.0 tap returns silu of the tap-shifted input, on both rounding paths."""
     cfg = synth.GdnConfig(n_layers=1)

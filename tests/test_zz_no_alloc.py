@@ -44,7 +44,7 @@ def test_noalloc_rejects_more_tokens_than_its_scratch(abi):
     """128 tokens fit at 32 v-heads; 129 are refused before any device work."""
     cfg = abi.GdnConfigC(2048, 16, 32, 128, 128, 4, 1, 1e-6)
     fake = C.c_void_p(1 << 20)   # aligned, never dereferenced: the size check comes first
-    w = abi.GdnLayerWeightsC(fake.value, fake.value, fake.value, fake.value)
+    w = abi.GdnLayerWeightsC(fake.value, fake.value, fake.value, fake.value, 0)
     io = abi.GdnStepIOC(fake.value, 8192, fake.value, 4096, fake.value, 64, fake.value, 4096)
     rc = _call(abi, cfg, 4, fake, fake, w, io, fake, fake, 1, 129, None)
     assert rc == abi.GDN_E_INVALID
