@@ -80,6 +80,10 @@ struct gdn_pool {
     uint16_t* mix;           // scratch [rec_cap][hidden]: mixer output
     uint8_t* recs;           // scratch: per-(v-head, token) records of the layer step [Hv][rec_cap][REC_BYTES]
     long long rec_cap;       // tokens per call the scratch holds
+    uint8_t* wy_tiles;       // scratch: chunked-prefill tile sets [wy_cap][Hv][WY_TILESET_BYTES]
+    long long wy_cap;        // chunks the tile scratch holds (rec_cap / 32 + 1: segments of >= 32 tokens)
+    int32_t* wy_cb;          // chunked-prefill plan: chunk prefix per sequence [65536] ...
+    int32_t* wy_plan;        // ... and the chunk count, sequence count and ranking [WY_PLAN_INTS]
 };
 
 static constexpr int kDeviceWords = 16;  // one 64-byte allocation
@@ -87,29 +91,40 @@ static constexpr int kWgMaxTiles = 4096;  // arrival counters: weight-streaming 
 
 static long long proj_ld(const gdn_pool* p) { return (long long)p->D + p->cfg.n_v_heads * 128 + 2 * p->cfg.n_v_heads; }
 
+static long long wy_chunks_for(long long tokens) { return tokens / gdn::WY_MIN_T + 1; }
+
+static size_t wy_tile_bytes(const gdn_pool* p, long long tokens) {
+    return (size_t)wy_chunks_for(tokens) * p->cfg.n_v_heads * gdn::WY_TILESET_BYTES;
+}
+
 static int reserve_records(gdn_pool* p, long long tokens) {
     if (tokens <= p->rec_cap) return GDN_OK;
     const size_t rec_bytes = (size_t)tokens * p->cfg.n_v_heads * gdn::REC_BYTES;
     const size_t proj_bytes = (size_t)tokens * proj_ld(p) * 2;
     const size_t gated_bytes = (size_t)tokens * p->cfg.n_v_heads * 128 * 2;
     const size_t hid_bytes = (size_t)tokens * p->cfg.hidden * 2;
-    uint8_t* buf = nullptr;
+    const size_t tile_bytes = wy_tile_bytes(p, tokens);
+    uint8_t *buf = nullptr, *tiles = nullptr;
     uint16_t *proj = nullptr, *gated = nullptr, *hn = nullptr, *mix = nullptr;
     cudaError_t e = cudaMalloc(&buf, rec_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&proj, proj_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&gated, gated_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&hn, hid_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&mix, hid_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&tiles, tile_bytes);
     if (e != cudaSuccess) {
-        cudaFree(buf); cudaFree(proj); cudaFree(gated); cudaFree(hn); cudaFree(mix);
+        cudaFree(buf); cudaFree(proj); cudaFree(gated); cudaFree(hn); cudaFree(mix); cudaFree(tiles);
         return fail(GDN_E_NOMEM, "cudaMalloc of step scratch for %lld tokens failed: %s", tokens, cudaGetErrorString(e));
     }
     if (p->recs) {
         cudaDeviceSynchronize();
         cudaFree(p->recs); cudaFree(p->proj); cudaFree(p->gated); cudaFree(p->hn); cudaFree(p->mix);
+        cudaFree(p->wy_tiles);
     }
     p->recs = buf;
     p->proj = proj; p->gated = gated; p->hn = hn; p->mix = mix;
+    p->wy_tiles = tiles;
+    p->wy_cap = wy_chunks_for(tokens);
     p->rec_cap = tokens;
     return GDN_OK;
 }
@@ -192,7 +207,20 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
     }
     p->recs = nullptr;
     p->proj = p->gated = p->hn = p->mix = nullptr;
+    p->wy_tiles = nullptr;
+    p->wy_cap = 0;
     p->rec_cap = 0;
+    p->wy_cb = nullptr;
+    p->wy_plan = nullptr;
+    e = cudaMalloc(&p->wy_cb, (65536 + gdn::WY_PLAN_INTS) * sizeof(int32_t));
+    if (e != cudaSuccess) {
+        cudaFree(p->rec);
+        cudaFree(p->conv);
+        cudaFree(p->err);
+        delete p;
+        return fail(GDN_E_NOMEM, "cudaMalloc of the prefill plan failed: %s", cudaGetErrorString(e));
+    }
+    p->wy_plan = p->wy_cb + 65536;
     p->gemm = nullptr;
     p->gemm_ws = nullptr;
     p->wg_cnt = nullptr;
@@ -225,6 +253,7 @@ int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, gdn_pool
         cudaFree(p->conv);
         cudaFree(p->err);
         cudaFree(p->recs); cudaFree(p->proj); cudaFree(p->gated); cudaFree(p->hn); cudaFree(p->mix);
+        cudaFree(p->wy_tiles); cudaFree(p->wy_cb);
         cudaFree(p->gemm_ws);
         cudaFree(p->wg_cnt);
         cudaFree(p->wg_ws);
@@ -257,6 +286,8 @@ int gdn_pool_destroy(gdn_pool* p) {
     cudaFree(p->gated);
     cudaFree(p->hn);
     cudaFree(p->mix);
+    cudaFree(p->wy_tiles);
+    cudaFree(p->wy_cb);
     gdn::gemm_destroy(p->gemm);
     cudaFree(p->gemm_ws);
     cudaFree(p->wg_cnt);
@@ -282,7 +313,8 @@ int gdn_pool_bytes(const gdn_pool* p, size_t* bytes) {
              sizeof(int32_t) + (size_t)p->rec_cap * p->cfg.n_v_heads * gdn::REC_BYTES +
              (size_t)p->rec_cap * 2 * (proj_ld(p) + p->cfg.n_v_heads * 128 + 2 * p->cfg.hidden) + (32u << 20) +
              kWgMaxTiles * sizeof(int) + (size_t)gdn::wg_workspace_floats(p->n_sm) * sizeof(float) +
-             p->wdq_elems * sizeof(uint16_t);
+             p->wdq_elems * sizeof(uint16_t) + wy_tile_bytes(p, p->rec_cap) +
+             (65536 + gdn::WY_PLAN_INTS) * sizeof(int32_t);
     return ok();
 }
 
@@ -460,6 +492,10 @@ static int layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, co
     const bool has_long = n_tokens > n_seq;
     ra.wy_min_t = has_long ? gdn::WY_MIN_T : 0;
     ra.wy_counter = p->err + 1;
+    ra.wy_tiles = p->wy_tiles;
+    ra.wy_cap_chunks = p->wy_cap;
+    ra.wy_cb = p->wy_cb;
+    ra.wy_plan = p->wy_plan;
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
     if (e == cudaSuccess && has_long) e = gdn::launch_wy(ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");

@@ -507,6 +507,34 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
     return make_uint4(pack_pair(f[0], f[1]), pack_pair(f[2], f[3]), pack_pair(f[4], f[5]), pack_pair(f[6], f[7]));
 }
 
+// Round 8 values to bf16 precision in place, two per conversion instruction (the conversions share the
+// transcendental pipe with the SiLU's exponential and reciprocal, which bounds this kernel).
+__device__ __forceinline__ void rbf8(float (&f)[8]) {
+#pragma unroll
+    for (int c = 0; c < 8; c += 2) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f[c], f[c + 1]);
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+        f[c] = __uint_as_float(u << 16);
+        f[c + 1] = __uint_as_float(u & 0xffff0000u);
+    }
+}
+
+// Pack 8 values that are already bf16-exact (no rounding left to do): bit moves only.
+__device__ __forceinline__ uint4 pack8_exact(const float (&f)[8]) {
+    uint32_t u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        u[i] = (__float_as_uint(f[2 * i]) >> 16) | (__float_as_uint(f[2 * i + 1]) & 0xffff0000u);
+    return make_uint4(u[0], u[1], u[2], u[3]);
+}
+
+// silu of 8 bf16-exact values with the fast sigmoid of silu_bf_fast, rounded to bf16 in pairs.
+__device__ __forceinline__ void silu8_fast(float (&f)[8]) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) f[c] = f[c] * __fdividef(1.0f, 1.0f + __expf(-f[c]));
+    rbf8(f);
+}
+
 // Conv + SiLU of one lane's 8 channels over the sub-tile's tokens.  raw[32 r] is tap row n0-3+r of the channels
 // (r < 19, in the lane's shared-memory column).  QK: the lane's channels are q (lanes 0-15) or k (lanes 16-31) of
 // the k-head; each token's RMSNorm sum is reduced over the 16 lanes of the half-warp and the normalised values go
@@ -548,11 +576,17 @@ __device__ __forceinline__ void prep_vec_conv(const PrepArgs& a, int ch, bool ac
         const bool valid = s_seq[j] >= 0;        // uniform over the warp
         float o[8];
         if (SIMPLE) {
+            // conv_silu_fast for 8 channels, with the two bf16 roundings done in pairs
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const float x4[KC] = {xm[0][c], xm[1][c], xm[2][c], xc[c]};
-                o[c] = conv_silu_fast(x4, w[c]);
+                float acc = xm[0][c] * w[c][0];
+                acc = acc + xm[1][c] * w[c][1];
+                acc = acc + xm[2][c] * w[c][2];
+                acc = acc + xc[c] * w[c][3];
+                o[c] = acc;
             }
+            rbf8(o);
+            silu8_fast(o);
         } else {
             cp_async_wait_group<PV_RING - 1>();  // token j's window rows have landed
             const int t = s_t[j];
@@ -588,13 +622,16 @@ __device__ __forceinline__ void prep_vec_conv(const PrepArgs& a, int ch, bool ac
                 const float gain = lane < 16 ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
                 float v[8];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) v[c] = rbf(o[c] * nrm) * gain;
+                for (int c = 0; c < 8; ++c) v[c] = o[c] * nrm;
+                rbf8(v);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) v[c] *= gain;
                 const uint4 val = pack8(v);
                 for (int r = 0; r < ratio; ++r)
                     *reinterpret_cast<uint4*>(a.rec + ((long long)(hv0 + r) * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = val;
             }
         } else if (valid && active) {
-            *reinterpret_cast<uint4*>(a.rec + ((long long)hv0 * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = pack8(o);
+            *reinterpret_cast<uint4*>(a.rec + ((long long)hv0 * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = pack8_exact(o);
         }
         if (SIMPLE) {
 #pragma unroll
@@ -729,10 +766,14 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
                     if (q_seq[jb + r] < 0) continue;
                     float zv[8];
                     unpack8(zr[r], zv);
+                    if (simple) {
+                        silu8_fast(zv);
+                    } else {
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) zv[c] = simple ? silu_bf_fast(zv[c]) : silu_bf(zv[c]);
+                        for (int c = 0; c < 8; ++c) zv[c] = silu_bf(zv[c]);
+                    }
                     *reinterpret_cast<uint4*>(a.rec + ((long long)(hv0 + half) * a.rec_cap + n0 + jb + r) * REC_BYTES +
-                                              768 + 2 * c8) = pack8(zv);
+                                              768 + 2 * c8) = pack8_exact(zv);
                 }
             }
         }

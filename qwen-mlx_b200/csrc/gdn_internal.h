@@ -72,8 +72,17 @@ struct RecurArgs {
     int32_t hk, hv, D;
     int32_t* err;
     int32_t wy_min_t;            // > 0: segments of at least this many tokens go to the chunked kernel
-    int32_t* wy_counter;         // chunked kernel's work-ticket counter (zeroed by launch_wy)
+    int32_t* wy_counter;         // chunked kernel's work-ticket counter (zeroed by the plan kernel)
+    uint8_t* wy_tiles;           // per (chunk, v-head) tile sets of the chunk-parallel pass [wy_cap_chunks][Hv][48 KiB]
+    long long wy_cap_chunks;     // chunks the tile scratch holds
+    int32_t* wy_cb;              // [n_seq] chunk prefix per sequence (plan kernel)
+    int32_t* wy_plan;            // [0] chunks, [1] qualifying sequences, [2..] them longest first
 };
+
+// Sequences the plan kernel ranks longest first (more run in call order); tile set per (chunk, v-head).
+constexpr int WY_SORT_CAP = 1024;
+constexpr int WY_TILESET_BYTES = 6 * 8192;
+constexpr int WY_PLAN_INTS = 2 + WY_SORT_CAP;
 
 // Sequences of at least this many tokens in one call run the chunked (WY) tensor-core kernel.
 constexpr int WY_MIN_T = 32;

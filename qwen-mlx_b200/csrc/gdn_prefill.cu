@@ -11,40 +11,46 @@
 //   D = U - W S0^T                                        (accumulated onto U in TMEM)
 //   Y = diag(gamma) Q S0^T + P (.) QK D,  P[t][s] = exp(lg_t - lg_s) (s <= t)
 //   S_C = gamma_C S0 + D^T diag(exp(lg_C - lg_s)) K
-// f32 operands (T, W, S0, D, P (.) QK) enter the bf16 MMAs as hi + lo bf16 pairs
-// (hi = bf16(x), lo = bf16(x - hi)); products of two split operands drop lo*lo.
-// The f32 state S lives in TMEM for the whole sequence: each chunk scales it by
-// gamma_C in place and the state-update MMA accumulates onto it.  The epilogue
-// rounds y to bf16 (metal_gdn.rs:54) and applies silu(z) * rms_norm(y, norm_w, eps)
-// (qwen3_5.rs:660-665).  Decays stay in log space, so long chunks of strong decay
-// cannot underflow into 0/0.
+// f32 operands (T beta, T beta gamma, W, S0, D, P (.) QK) enter the bf16 MMAs as hi + lo bf16
+// pairs (hi = bf16(x), lo = bf16(x - hi)); products of two split operands drop lo*lo.  Decays
+// stay in log space, so long chunks of strong decay cannot underflow into 0/0.
 //
-// Every operand tile is stored token-major ([t][d], [t][v], [s][v]) in the core-matrix
-// layout of gdn_umma.cuh and read K-major or MN-major as each product needs, so no tile
-// is ever transposed and every shared-memory store is a 16-byte vector.
+// Everything up to T beta, T beta gamma and P (.) QK depends only on the chunk's own inputs, so it
+// is computed for every chunk at once; only D, Y and the state update need the state entering the
+// chunk.  A call with long segments runs three kernels after the prep:
+//   gdn_wy_plan_kernel   (one CTA) numbers the chunks of the qualifying segments (an exclusive
+//                        prefix over the sequences), ranks the sequences longest first, and zeroes
+//                        the sequential kernel's work ticket;
+//   gdn_wy_chunk_kernel  (chunk-parallel, 2 CTAs per SM, work item = (chunk, k-head)): G and QK of
+//                        the k-head once, then for each of its v-heads (two at a time, one per warp
+//                        group) M, the blocked inverse
+//                        T = (I + M)^-1 and the tiles T beta, T beta gamma and P (.) QK as hi / lo
+//                        bf16 pairs, stored to global memory in the exact shared-memory layout the
+//                        sequential kernel multiplies from (48 KiB per chunk and v-head);
+//   gdn_wy_kernel        (sequential, one CTA per SM, work item = (sequence, v-head), longest
+//                        chains first): per chunk one bulk copy brings the chunk's tiles, then
+//                        U, W, D, Q S0^T, P D and the state update on the tensor cores, and the
+//                        epilogue rounds y to bf16 (metal_gdn.rs:54) and applies
+//                        silu(z) * rms_norm(y, norm_w, eps) (qwen3_5.rs:660-665).
+// The f32 state S lives in TMEM for the whole sequence: each chunk scales it by gamma_C in place and
+// the state-update MMA accumulates onto it.
 //
-// Work items are (sequence, v-head) pairs of the segments with at least wy_min_t
-// tokens.  Each CTA (256 threads, 8 warps, one per SM) first ranks those sequences
-// longest first, then takes items from a global ticket counter, so the longest
-// sequential chains start first.  Inputs are the prep kernel's records; the next
-// chunk's K, V and Q are prefetched with cp.async while the current one computes.
+// Every operand tile is stored token-major ([t][d], [t][v], [s][v]) in the core-matrix layout of
+// gdn_umma.cuh and read K-major or MN-major as each product needs, so no tile is ever transposed and
+// every shared-memory store is a 16-byte vector.  Every product is an M = 128 MMA whose 128 rows are
+// v, d or [Q; K] stacked, so every TMEM lane carries data: G and QK come out of one [Q; K] K^T
+// product, and U, W, D, Q S0^T and P D are formed transposed (U^T = V^T (T beta)^T,
+// W^T = K^T (T beta gamma)^T, D^T = U^T - S0 W^T, (Q S0^T)^T = S0 Q^T, (P D)^T = D^T P^T).
 //
-// Every product but the intra-chunk inverse is an M=128 tcgen05 MMA whose 128 rows are v, d or
-// [Q; K] stacked, so every TMEM lane carries data: G and QK come out of one [Q; K] K^T product, and U, W,
-// D, Q S0^T and P D are formed transposed (U^T = V^T (T beta)^T, W^T = K^T (T beta gamma)^T,
-// D^T = U^T - S0 W^T, (Q S0^T)^T = S0 Q^T, (P D)^T = D^T P^T), each operand being a token-major tile read
-// K-major or MN-major.  The epilogue transposes y once through shared memory for the per-token norm.
-//
-// Shared memory (bytes); bf16 tiles in the layout of gdn_umma.cuh:
+// Shared memory of gdn_wy_kernel (bytes); bf16 tiles in the layout of gdn_umma.cuh:
 //   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity)
 //   R_V   16K  V [64 s][128 v]
 //   R_X   64K  S0 hi, lo [128 v][128 d]  -> D^T hi, D^T lo, Dd^T hi, Dd^T lo [128 v][64 s]
-//   R_T   17K  M, then T = (I + M)^-1 in place (f32, row stride LDT)  -> y [64 t][128 v] bf16 (row stride LDY)
-//   R_N    6K  N_ik = T_ii M_ik for the six blocks below the diagonal (f32 16 x 16)
-//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] -> -W^T hi, -W^T lo [128 d][64 t]
-//   R_P   16K  (P (.) QK) hi, lo [64 t][64 s]
-// TMEM (cta_group::1, all 128 lanes): S [0,128) = state [v][d]; GQ [128,192) = [QK; G]; U [192,256) = U^T
-// then D^T; W [256,320) = W^T; QS [320,384) = (Q S0^T)^T; PD [384,448) = (P D)^T.
+//   R_T   17K  y [64 t][128 v] bf16 (row stride LDY), the epilogue's transpose
+//   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] (bulk copy) -> -W^T hi, -W^T lo [128 d][64 t]
+//   R_P   16K  (P (.) QK) hi, lo [64 t][64 s] (same bulk copy)
+// TMEM (cta_group::1, all 128 lanes): S [0,128) = state [v][d]; U [192,256) = U^T then D^T;
+// W [256,320) = W^T; QS [320,384) = (Q S0^T)^T; PD [384,448) = (P D)^T.
 #include "gdn_device.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
@@ -55,17 +61,27 @@ namespace gdn {
 constexpr int WC = 64;                 // tokens per chunk
 constexpr int WY_THREADS = 256;
 constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
-constexpr int WY_SORT_CAP = 1024;      // sequences ranked longest-first; more fall back to call order
 constexpr int R_QK = 0, R_V = 65536, R_X = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
               R_P = 204800, R_SMALL = 221184;
 static_assert(R_N + 6 * 256 * 4 <= R_TB, "prefill shared memory layout");
+static_assert(R_P == R_TB + 32768, "the chunk tile set lands in one bulk copy");
 constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
 static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
 constexpr int SMALL_FLOATS = 2 * 64 + 2 * 64 + 3 * 2 * 64 + 128;
-constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + WY_SORT_CAP * 4 + 80;
+constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + 96;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
-constexpr uint32_t TM_S = 0, TM_GQ = 128, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
+constexpr uint32_t TM_S = 0, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
 constexpr uint64_t WY_WAIT_NS = 2000000000ull;
+constexpr uint32_t TILESET = WY_TILESET_BYTES;   // T beta hi, lo | T beta gamma hi, lo | P (.) QK hi, lo
+static_assert(TILESET == 6 * 8192, "tile set layout");
+
+// gdn_wy_chunk_kernel shared memory: Q | K tiles, per warp group M / T (f32) and N blocks, per-v-head gates (up
+// to 8 heads)
+constexpr int A_TN = WC * LDT * 4 + 6 * 256 * 4;
+constexpr int A_QK = 0, A_T = 32768, A_SMALL = A_T + 2 * A_TN;
+constexpr int A_SMEM = A_SMALL + 5 * 8 * WC * 4 + 32;
+constexpr int WA_THREADS = 256;
+constexpr int WP_THREADS = 1024;
 
 __device__ __forceinline__ uint32_t pack_bf2(float lo_half, float hi_half) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(lo_half, hi_half);
@@ -162,6 +178,342 @@ __device__ __forceinline__ bool wy_qualifies(const RecurArgs& a, int seq, int& t
     return slot >= 0 && slot < a.n_slots && T >= a.wy_min_t && t0 >= 0 && t0 + T <= a.n_tokens;
 }
 
+
+// 16-byte vector at row r, column group c8 of a [rows][COLS] bf16 tile in global memory (same layout).
+template <int COLS>
+__device__ __forceinline__ void st_tile_g(uint8_t* base, int r, int c8, const uint4& v) {
+    *reinterpret_cast<uint4*>(base + (r >> 3) * (COLS / 8) * 128 + c8 * 128 + (r & 7) * 16) = v;
+}
+
+// ------------------------------------------------------------------ plan (one CTA)
+// wy_cb[i] = number of 64-token chunks of the qualifying sequences before sequence i (exclusive prefix);
+// wy_plan[0] = all chunks (or -1 when they exceed the scratch: error flagged, nothing runs), wy_plan[1] =
+// qualifying sequences m, wy_plan[2 ..] = them ranked longest first (ties: call order) when m <= WY_SORT_CAP.
+__global__ void __launch_bounds__(WP_THREADS, 1) gdn_wy_plan_kernel(const RecurArgs a) {
+    __shared__ int s_warp[WP_THREADS / 32];
+    __shared__ int s_run, s_cnt;
+    __shared__ int l_seq[WY_SORT_CAP], l_len[WY_SORT_CAP];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();
+    if (tid == 0) {
+        s_run = 0;
+        s_cnt = 0;
+        *a.wy_counter = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < a.n_seq; base += WP_THREADS) {
+        const int i = base + tid;
+        int t0 = 0, T = 0, slot = 0;
+        const bool q = i < a.n_seq && wy_qualifies(a, i, t0, T, slot);
+        const int nc = q ? (T + WC - 1) / WC : 0;
+        if (q) {
+            const int e = atomicAdd(&s_cnt, 1);
+            if (e < WY_SORT_CAP) {
+                l_seq[e] = i;
+                l_len[e] = T;
+            }
+        }
+        int x = nc;   // inclusive warp scan
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) s_warp[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int w = s_warp[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            s_warp[lane] = w;   // inclusive over warps
+        }
+        __syncthreads();
+        const int excl = s_run + (warp ? s_warp[warp - 1] : 0) + x - nc;
+        if (i < a.n_seq) a.wy_cb[i] = excl;
+        __syncthreads();
+        if (tid == 0) s_run += s_warp[WP_THREADS / 32 - 1];
+        __syncthreads();
+    }
+    const int m = s_cnt;
+    if (m <= WY_SORT_CAP) {
+        for (int e = tid; e < m; e += WP_THREADS) {
+            const int le = l_len[e], se = l_seq[e];
+            int r = 0;
+            for (int f = 0; f < m; ++f) {
+                const int lf = l_len[f];
+                r += (lf > le) || (lf == le && l_seq[f] < se);
+            }
+            a.wy_plan[2 + r] = se;
+        }
+    }
+    if (tid == 0) {
+        const long long total = s_run;
+        if (total > a.wy_cap_chunks) {
+            atomicOr(a.err, ERR_BAD_SEQLENS);
+            a.wy_plan[0] = -1;
+        } else {
+            a.wy_plan[0] = (int)total;
+        }
+        a.wy_plan[1] = m;
+    }
+}
+
+// ------------------------------------------------------------------ chunk-parallel pass
+// Per item (chunk, k-head): [QK; G] = [Q; K] K^T once, then the k-head's v-heads two at a time, one per
+// warp group (warps 0-3 and 4-7; each group reaches all 128 TMEM lanes, one warp per lane quarter), each
+// with its own M / T and N regions and group-local named barriers.
+__device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float* fT, float* fN, const float* lgc,
+                                        const float* gamc, const float* betc, uint32_t tcol, int gt, int bar_id) {
+    const int gw = gt >> 5, lane = gt & 31;     // warp of the group = TMEM lane quarter
+    const int L = gw * 32 + lane;
+    // ---- lanes 0..63 hold QK row t -> P (.) QK hi/lo tiles; lanes 64..127 hold G row t -> M (f32)
+    {
+        const bool is_g = L >= WC;
+        const int t = L & (WC - 1);
+        const float lg_t = lgc[t];
+        const float b_t = betc[t];
+#pragma unroll 1
+        for (int jj = 0; jj < 4; ++jj) {
+            float x[16];
+            tmem_ld16(tcol + jj * 16, x);
+            if (is_g) {
+                float mv[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int s = jj * 16 + e;
+                    mv[e] = s < t ? b_t * exp2f(lg_t - lgc[s]) * x[e] : 0.f;
+                }
+                float* mrow = fT + t * LDT + jj * 16;
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4*>(mrow + e) = make_float4(mv[e], mv[e + 1], mv[e + 2], mv[e + 3]);
+            } else {
+                float pv[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int s = jj * 16 + e;
+                    pv[e] = s <= t ? exp2f(lg_t - lgc[s]) * x[e] : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    uint4 h4, l4;
+                    split8(pv + 8 * u, h4, l4);
+                    st_tile_g<64>(out + 32768, t, jj * 2 + u, h4);
+                    st_tile_g<64>(out + 40960, t, jj * 2 + u, l4);
+                }
+            }
+        }
+    }
+    named_bar_sync(bar_id, 128);
+    // ---- T = (I + M)^-1 by 16 x 16 blocks, in place over M: the diagonal blocks by forward substitution
+    // (warps 2, 3 of the group; lane: block 2 (gw - 2) + lane/16, column s)
+    if (gw >= 2) {
+        const int b = 2 * (gw - 2) + (lane >> 4), s = lane & 15;
+        float* Mb = fT + 16 * b * LDT + 16 * b;
+        float col[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) col[q] = q == s ? 1.f : 0.f;
+#pragma unroll
+        for (int t = 1; t < 16; ++t) {
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int j4 = 0; j4 < t; j4 += 4) {
+                const float4 mv = *reinterpret_cast<const float4*>(Mb + t * LDT + j4);
+                a0 = fmaf(mv.x, col[j4], a0);
+                a1 = fmaf(mv.y, col[j4 + 1], a1);
+                a0 = fmaf(mv.z, col[j4 + 2], a0);
+                a1 = fmaf(mv.w, col[j4 + 3], a1);
+            }
+            if (t > s) col[t] = -(a0 + a1);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 16; ++q) Mb[q * LDT + s] = col[q];
+    }
+    named_bar_sync(bar_id, 128);
+    // N_ik = T_ii M_ik for the six blocks below the diagonal (pair index i(i-1)/2 + k); each task is 4
+    // consecutive outputs of one row: 384 tasks
+    for (int task = gt; task < 6 * 64; task += 128) {
+        const int pi = task >> 6, rem = task & 63;
+        const int r = rem >> 2, c4 = (rem & 3) * 4;
+        const int i = pi < 1 ? 1 : (pi < 3 ? 2 : 3);
+        const int kk = pi - i * (i - 1) / 2;
+        const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
+        const float* Mk = fT + 16 * i * LDT + 16 * kk + c4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m4 = 0; m4 < 16; m4 += 4) {
+            const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
+            const float tv[4] = {tr.x, tr.y, tr.z, tr.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 mr = *reinterpret_cast<const float4*>(Mk + (m4 + q) * LDT);
+                acc.x = fmaf(tv[q], mr.x, acc.x);
+                acc.y = fmaf(tv[q], mr.y, acc.y);
+                acc.z = fmaf(tv[q], mr.z, acc.z);
+                acc.w = fmaf(tv[q], mr.w, acc.w);
+            }
+        }
+        *reinterpret_cast<float4*>(fN + pi * 256 + r * 16 + c4) = acc;
+    }
+    named_bar_sync(bar_id, 128);
+    // block rows 1..3: T_ij = -sum_{k=j}^{i-1} N_ik T_kj (4 outputs per task)
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+        for (int task = gt; task < 64 * i; task += 128) {
+            const int jb = task >> 6, rem = task & 63;
+            const int r = rem >> 2, c4 = (rem & 3) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int kk = jb; kk < i; ++kk) {
+                const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
+                const float* Tc = fT + 16 * kk * LDT + 16 * jb + c4;
+#pragma unroll
+                for (int m4 = 0; m4 < 16; m4 += 4) {
+                    const float4 nr = *reinterpret_cast<const float4*>(Nr + m4);
+                    const float nv4[4] = {nr.x, nr.y, nr.z, nr.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 tr = *reinterpret_cast<const float4*>(Tc + (m4 + q) * LDT);
+                        acc.x = fmaf(nv4[q], tr.x, acc.x);
+                        acc.y = fmaf(nv4[q], tr.y, acc.y);
+                        acc.z = fmaf(nv4[q], tr.z, acc.z);
+                        acc.w = fmaf(nv4[q], tr.w, acc.w);
+                    }
+                }
+            }
+            *reinterpret_cast<float4*>(fT + (16 * i + r) * LDT + 16 * jb + c4) =
+                make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
+        }
+        named_bar_sync(bar_id, 128);
+    }
+    // ---- (T beta) and (T beta gamma) hi/lo tiles; thread (row t, columns [32 cq, +32))
+    {
+        const int t = gt & 63, cq = gt >> 6;
+#pragma unroll 1
+        for (int h16 = 0; h16 < 2; ++h16) {
+            const int c0 = 32 * cq + 16 * h16;
+            const float* Tr = fT + t * LDT + c0;
+            float tb[16], tg[16];
+#pragma unroll
+            for (int e4 = 0; e4 < 16; e4 += 4) {
+                const float4 x = *reinterpret_cast<const float4*>(Tr + e4);
+                tb[e4] = x.x; tb[e4 + 1] = x.y; tb[e4 + 2] = x.z; tb[e4 + 3] = x.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int s = c0 + e;
+                const float x = s <= t ? tb[e] * betc[s] : 0.f;
+                tb[e] = x;
+                tg[e] = x * gamc[s];
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                uint4 h4, l4;
+                const int cg = c0 / 8 + u;
+                split8(tb + 8 * u, h4, l4);
+                st_tile_g<64>(out, t, cg, h4);
+                st_tile_g<64>(out + 8192, t, cg, l4);
+                split8(tg + 8 * u, h4, l4);
+                st_tile_g<64>(out + 16384, t, cg, h4);
+                st_tile_g<64>(out + 24576, t, cg, l4);
+            }
+        }
+    }
+    named_bar_sync(bar_id, 128);   // M / T region free for the group's next head
+}
+
+__global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const RecurArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* s_beta = reinterpret_cast<float*>(smem + A_SMALL);   // [8][64]
+    float* s_lgr = s_beta + 8 * WC;                             // [8][64] log g per token
+    float* s_lg = s_lgr + 8 * WC;                               // [8][64] cumulative, log2 units
+    float* s_gam = s_lg + 8 * WC;                               // [8][64] exp(lg_t)
+    float* s_tail = s_gam + 8 * WC;                             // [8][64] (unused here)
+    uint64_t* bar = reinterpret_cast<uint64_t*>(s_tail + 8 * WC);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int grp = warp >> 2, gt = tid & 127;                  // warp group, thread within it
+    const uint32_t sb = smem_u32(smem);
+    const int ratio = a.hv / a.hk;
+    float* fT = reinterpret_cast<float*>(smem + A_T + grp * A_TN);
+    float* fN = reinterpret_cast<float*>(smem + A_T + grp * A_TN + WC * LDT * 4);
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, 64);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tcol = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    uint32_t ph = 0;
+    pdl_wait();
+    const int total = __ldg(a.wy_plan);
+    const int n_items = total > 0 ? total * a.hk : 0;
+
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const int g = it / a.hk, hk = it - g * a.hk;
+        // the sequence holding chunk g: the last one whose chunk prefix is <= g
+        int lo = 0, hi = a.n_seq;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (__ldg(a.wy_cb + mid) <= g) lo = mid; else hi = mid;
+        }
+        const int seq = lo;
+        const int cb = __ldg(a.wy_cb + seq);
+        const int c = g - cb;
+        int t0, T, slot;
+        if (!wy_qualifies(a, seq, t0, T, slot) || c < 0 || c * WC >= T) continue;   // not reached
+        const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
+        const long long row = (long long)t0 + (long long)c * WC;
+        const uint8_t* recq = a.recs + ((long long)(hk * ratio) * a.rec_cap + row) * REC_BYTES;
+        load_field(sb + A_QK, recq, 0, nv, tid);
+        load_field(sb + A_QK + 16384, recq, 256, nv, tid);
+        for (int j = 0; j < ratio; ++j)
+            load_gates(s_beta + j * WC, s_lgr + j * WC,
+                       a.recs + ((long long)(hk * ratio + j) * a.rec_cap + row) * REC_BYTES, nv, tid);
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+        if (warp < ratio) wy_scan(s_lgr + warp * WC, s_lg + warp * WC, s_gam + warp * WC, s_tail + warp * WC, lane);
+        wy_sync_for_mma();
+        // [QK; G] = [Q; K] K^T -> TMEM columns [0, 64) (rows 0..63 QK, rows 64..127 G)
+        if (tid == 0) {
+            const uint32_t id = umma_idesc_bf16(128, 64);
+            const uint64_t da = umma_desc(sb + A_QK, 128, 0), db = umma_desc(sb + A_QK + 16384, 128, 0);
+            for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem, da + ks * KSTEP_K, db + ks * KSTEP_K, id, ks > 0);
+            umma_commit(bar);
+        }
+        if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+        __syncthreads();
+        if (*s_abort) break;
+
+        for (int j0 = 0; j0 < ratio; j0 += 2) {
+            const int j = j0 + grp;
+            if (j < ratio) {
+                const int hv = hk * ratio + j;
+                uint8_t* out = a.wy_tiles + ((size_t)(cb + c) * a.hv + hv) * TILESET;
+                wa_head(a, out, fT, fN, s_lg + j * WC, s_gam + j * WC, s_beta + j * WC, tcol, gt, 1 + grp);
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+// ------------------------------------------------------------------ sequential pass
 __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     float* s_beta = reinterpret_cast<float*>(smem + R_SMALL);  // [2][64] (chunk parity)
@@ -170,16 +522,13 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     float* s_gam = s_lg + 2 * WC;                                 // [2][64] exp(lg_t)
     float* s_tail = s_gam + 2 * WC;                               // [2][64] exp(lg_last - lg_t)
     float* s_nw = s_tail + 2 * WC;                                // norm_w [128]
-    int* s_order = reinterpret_cast<int*>(s_nw + DV);             // sequences, longest first
-    uint64_t* bar = reinterpret_cast<uint64_t*>(s_order + WY_SORT_CAP);   // MMA batches waited in order
+    uint64_t* bar = reinterpret_cast<uint64_t*>(s_nw + DV);       // MMA batches waited in order
     uint64_t* bar_qs = bar + 1;                                   // (Q S0^T)^T, issued early
     uint64_t* bar_s = bar + 2;                                    // state update, waited when S is next used
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 3);
+    uint64_t* bar_tb = bar + 3;                                   // the chunk's tile set (bulk copy)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
-    int* s_cnt = const_cast<int*>(s_ticket + 1);
-    float* fT = reinterpret_cast<float*>(smem + R_T);
-    float* fN = reinterpret_cast<float*>(smem + R_N);
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -192,8 +541,8 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         mbar_init(bar, 1);
         mbar_init(bar_qs, 1);
         mbar_init(bar_s, 1);
+        mbar_init(bar_tb, 1);
         *s_abort = 0;
-        *s_cnt = 0;
         fence_mbar_init();
     }
     for (int i = tid; i < DV; i += WY_THREADS) s_nw[i] = bf2f(a.norm_w[i]);
@@ -203,41 +552,14 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    uint32_t ph = 0, ph_qs = 0, ph_s = 0;
+    uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0;
+    bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
     pdl_wait();
 
-    // ---- the qualifying sequences, ranked longest first (ties: call order)
-    {
-        int* l_seq = reinterpret_cast<int*>(smem + R_X);
-        int* l_len = l_seq + WY_SORT_CAP;
-        for (int i = tid; i < a.n_seq; i += WY_THREADS) {
-            int t0, T, slot;
-            if (wy_qualifies(a, i, t0, T, slot)) {
-                const int e = atomicAdd(s_cnt, 1);
-                if (e < WY_SORT_CAP) {
-                    l_seq[e] = i;
-                    l_len[e] = T;
-                }
-            }
-        }
-        __syncthreads();
-        const int m = *s_cnt;
-        if (m <= WY_SORT_CAP) {
-            for (int e = tid; e < m; e += WY_THREADS) {
-                const int le = l_len[e], se = l_seq[e];
-                int r = 0;
-                for (int f = 0; f < m; ++f) {
-                    const int lf = l_len[f];
-                    r += (lf > le) || (lf == le && l_seq[f] < se);
-                }
-                s_order[r] = se;
-            }
-        }
-        __syncthreads();
-    }
-    const int m_seq = *s_cnt;
+    const int total = __ldg(a.wy_plan);
+    const int m_seq = __ldg(a.wy_plan + 1);
     const bool ranked = m_seq <= WY_SORT_CAP;
-    const int n_work = (ranked ? m_seq : a.n_seq) * a.hv;
+    const int n_work = total < 0 ? 0 : (ranked ? m_seq : a.n_seq) * a.hv;
 
     for (;;) {
         if (tid == 0) *s_ticket = atomicAdd(a.wy_counter, 1);
@@ -248,15 +570,22 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         if (stop) break;
         const int si = k / a.hv;
         const int hv = k - si * a.hv;
-        const int seq = ranked ? s_order[si] : si;
+        const int seq = ranked ? __ldg(a.wy_plan + 2 + si) : si;
         int t0, T, slot;
         if (!wy_qualifies(a, seq, t0, T, slot)) continue;
         float* st = a.rec + ((size_t)slot * a.hv + hv) * (DV * DK);
         const float* st_in = (a.rec_in ? a.rec_in : a.rec) + ((size_t)slot * a.hv + hv) * (DV * DK);
         const uint8_t* recb = a.recs + ((long long)hv * a.rec_cap + t0) * REC_BYTES;
+        const uint8_t* tiles = a.wy_tiles + ((size_t)__ldg(a.wy_cb + seq) * a.hv + hv) * TILESET;
+        const size_t tile_step = (size_t)a.hv * TILESET;   // next chunk of the same head
         const int n_chunks = (T + WC - 1) / WC;
 
         // chunk 0's inputs
+        if (tid == 0) {
+            mbar_arrive_expect_tx(bar_tb, TILESET);
+            bulk_g2s(smem + R_TB, tiles, TILESET, bar_tb);
+            tb_pending = true;
+        }
         {
             const int nv = T < WC ? T : WC;
             load_field(sb + R_QK, recb, 0, nv, tid);
@@ -290,17 +619,21 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
             const uint32_t sQ = sb + R_QK + kb * 32768;    // Q [64][128], then K [64][128] at +16384
             const uint32_t sK = sQ + 16384;
-            const float* lgc = s_lg + kb * WC;
             const float* gamc = s_gam + kb * WC;
             const float* tailc = s_tail + kb * WC;
 
-            // ---- phase A: this chunk's inputs landed; next chunk's Q, K and gates in flight
+            // ---- phase A: this chunk's inputs and tile set landed; next chunk's Q, K and gates in flight
             cp_async_wait_all();
             if (c > 0) {
                 // the previous chunk's state update still reads the K buffer refilled below
                 if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 ph_s ^= 1u;
                 tc_fence_after();
+            }
+            if (tid == 0) {
+                if (!mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                else tb_pending = false;
+                ph_tb ^= 1u;
             }
             __syncthreads();
             if (*s_abort) break;
@@ -313,14 +646,25 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             if (c == 0 && warp == 0) wy_scan(s_lgr, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
             wy_sync_for_mma();
 
-            // ---- phase B: [QK; G] = [Q; K] K^T -> GQ (rows 0..63 QK, rows 64..127 G)
+            // ---- phase B: U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major);
+            // they need only the chunk's own inputs and overlap the state split below
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(128, 64);
-                const uint64_t da = umma_desc(sQ, 128, 0), db = umma_desc(sK, 128, 0);
-                for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem + TM_GQ, da + ks * KSTEP_K, db + ks * KSTEP_K, id, ks > 0);
+                const uint32_t id = umma_idesc_bf16(128, 64, true, false);
+                const uint64_t dv = umma_desc_mn(sb + R_V, 128, 0), dk = umma_desc_mn(sK, 128, 0);
+                constexpr uint64_t kmn = umma_kstep_mn(128);
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_bf16(tmem + TM_U, dv + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                }
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_bf16(tmem + TM_W, dk + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                }
                 umma_commit(bar);
             }
-            // ---- phase C2 (overlaps B): S0 hi/lo tiles [v][d]; S *= gamma_last in place
+            // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
             {
                 const float g_last = gamc[WC - 1];
 #pragma unroll
@@ -353,184 +697,10 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                 umma_commit(bar_qs);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-
-            // ---- phase C1: lanes 0..63 hold QK row t -> P (.) QK hi/lo tiles; lanes 64..127 hold G row t -> M (f32)
-            {
-                const bool is_g = L >= WC;
-                const int t = L & (WC - 1);
-                const float lg_t = lgc[t];
-                const float b_t = s_beta[kb * WC + t];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    float x[16];
-                    tmem_ld16(tmem + lane_base + TM_GQ + hh * 32 + j * 16, x);
-                    if (is_g) {
-                        float mv[16];
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const int s = hh * 32 + j * 16 + e;
-                            mv[e] = s < t ? b_t * exp2f(lg_t - lgc[s]) * x[e] : 0.f;
-                        }
-                        float* mrow = fT + t * LDT + hh * 32 + j * 16;
-#pragma unroll
-                        for (int e = 0; e < 16; e += 4)
-                            *reinterpret_cast<float4*>(mrow + e) = make_float4(mv[e], mv[e + 1], mv[e + 2], mv[e + 3]);
-                    } else {
-                        float pv[16];
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const int s = hh * 32 + j * 16 + e;
-                            pv[e] = s <= t ? exp2f(lg_t - lgc[s]) * x[e] : 0.f;
-                        }
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            uint4 hi, lo;
-                            split8(pv + 8 * u, hi, lo);
-                            st_tile<64>(smem + R_P, t, hh * 4 + j * 2 + u, hi);
-                            st_tile<64>(smem + R_P + 8192, t, hh * 4 + j * 2 + u, lo);
-                        }
-                    }
-                }
-            }
-
-            // ---- phase C3: T = (I + M)^-1 by 16 x 16 blocks, in place over M.  The warps that wrote M (2, 3, 6,
-            // 7) meet first; warps 2 and 3 invert the diagonal blocks by forward substitution (lane: block
-            // 2 (warp - 2) + lane/16, column s) while the P writers finish.
-            if (quarter >= 2) {
-                named_bar_sync(1, 128);
-                if (warp < 4) {
-                    const int b = 2 * (warp - 2) + (lane >> 4), s = lane & 15;
-                    float* Mb = fT + 16 * b * LDT + 16 * b;
-                    float col[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) col[j] = j == s ? 1.f : 0.f;
-#pragma unroll
-                    for (int t = 1; t < 16; ++t) {
-                        float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                        for (int j4 = 0; j4 < t; j4 += 4) {
-                            const float4 mv = *reinterpret_cast<const float4*>(Mb + t * LDT + j4);
-                            a0 = fmaf(mv.x, col[j4], a0);
-                            a1 = fmaf(mv.y, col[j4 + 1], a1);
-                            a0 = fmaf(mv.z, col[j4 + 2], a0);
-                            a1 = fmaf(mv.w, col[j4 + 3], a1);
-                        }
-                        if (t > s) col[t] = -(a0 + a1);
-                    }
-                    __syncwarp();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) Mb[j * LDT + s] = col[j];
-                }
-            }
-            __syncthreads();
-            // N_ik = T_ii M_ik for the six blocks below the diagonal (pair index i(i-1)/2 + k); each task
-            // is 4 consecutive outputs of one row: 384 tasks
-            for (int task = tid; task < 6 * 64; task += WY_THREADS) {
-                const int p = task >> 6, rem = task & 63;
-                const int r = rem >> 2, c4 = (rem & 3) * 4;
-                const int i = p < 1 ? 1 : (p < 3 ? 2 : 3);
-                const int kk = p - i * (i - 1) / 2;
-                const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
-                const float* Mk = fT + 16 * i * LDT + 16 * kk + c4;
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int m4 = 0; m4 < 16; m4 += 4) {
-                    const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
-                    const float tv[4] = {tr.x, tr.y, tr.z, tr.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 mr = *reinterpret_cast<const float4*>(Mk + (m4 + q) * LDT);
-                        acc.x = fmaf(tv[q], mr.x, acc.x);
-                        acc.y = fmaf(tv[q], mr.y, acc.y);
-                        acc.z = fmaf(tv[q], mr.z, acc.z);
-                        acc.w = fmaf(tv[q], mr.w, acc.w);
-                    }
-                }
-                *reinterpret_cast<float4*>(fN + p * 256 + r * 16 + c4) = acc;
-            }
-            __syncthreads();
-            // block rows 1..3: T_ij = -sum_{k=j}^{i-1} N_ik T_kj (4 outputs per task)
-#pragma unroll
-            for (int i = 1; i < 4; ++i) {
-                if (tid < 64 * i) {
-                    const int j = tid >> 6, rem = tid & 63;
-                    const int r = rem >> 2, c4 = (rem & 3) * 4;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int kk = j; kk < i; ++kk) {
-                        const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
-                        const float* Tc = fT + 16 * kk * LDT + 16 * j + c4;
-#pragma unroll
-                        for (int m4 = 0; m4 < 16; m4 += 4) {
-                            const float4 nr = *reinterpret_cast<const float4*>(Nr + m4);
-                            const float nv4[4] = {nr.x, nr.y, nr.z, nr.w};
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const float4 tr = *reinterpret_cast<const float4*>(Tc + (m4 + q) * LDT);
-                                acc.x = fmaf(nv4[q], tr.x, acc.x);
-                                acc.y = fmaf(nv4[q], tr.y, acc.y);
-                                acc.z = fmaf(nv4[q], tr.z, acc.z);
-                                acc.w = fmaf(nv4[q], tr.w, acc.w);
-                            }
-                        }
-                    }
-                    *reinterpret_cast<float4*>(fT + (16 * i + r) * LDT + 16 * j + c4) =
-                        make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
-                }
-                __syncthreads();
-            }
-
-            // ---- phase C4: (T beta) and (T beta gamma) hi/lo tiles; thread (row t, columns [16 cq, +16))
-            {
-                const int t = tid & 63, cq = tid >> 6;
-                const float* Tr = fT + t * LDT + 16 * cq;
-                float tb[16], tg[16];
-#pragma unroll
-                for (int e4 = 0; e4 < 16; e4 += 4) {
-                    const float4 x = *reinterpret_cast<const float4*>(Tr + e4);
-                    tb[e4] = x.x; tb[e4 + 1] = x.y; tb[e4 + 2] = x.z; tb[e4 + 3] = x.w;
-                }
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int s = 16 * cq + e;
-                    const float x = s <= t ? tb[e] * s_beta[kb * WC + s] : 0.f;
-                    tb[e] = x;
-                    tg[e] = x * gamc[s];
-                }
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    uint4 hi, lo;
-                    split8(tb + 8 * u, hi, lo);
-                    st_tile<64>(smem + R_TB, t, 2 * cq + u, hi);
-                    st_tile<64>(smem + R_TB + 8192, t, 2 * cq + u, lo);
-                    split8(tg + 8 * u, hi, lo);
-                    st_tile<64>(smem + R_TB + 16384, t, 2 * cq + u, hi);
-                    st_tile<64>(smem + R_TB + 24576, t, 2 * cq + u, lo);
-                }
-            }
-            wy_sync_for_mma();
-
-            // ---- phase D: U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major)
-            if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(128, 64, true, false);
-                const uint64_t dv = umma_desc_mn(sb + R_V, 128, 0), dk = umma_desc_mn(sK, 128, 0);
-                constexpr uint64_t kmn = umma_kstep_mn(128);
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_U, dv + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
-                }
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_W, dk + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
-                }
-                umma_commit(bar);
-            }
-            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
             if (has_next) load_field(sb + R_V, rec1, 512, nv1, tid);   // V is free
             cp_async_commit();
 
-            // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U, (Q S0^T)^T = S0 Q^T -> QS
+            // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 float wv[16];
@@ -557,6 +727,13 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                 umma_commit(bar);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
+            // P tiles follow once P D has read R_P)
+            if (tid == 0 && has_next && !*s_abort) {
+                mbar_arrive_expect_tx(bar_tb, TILESET);
+                bulk_g2s(smem + R_TB, tiles + (size_t)(c + 1) * tile_step, R_P - R_TB, bar_tb);
+                tb_pending = true;
+            }
             if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
             // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
@@ -614,6 +791,9 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                 for (int i = 0; i < 4; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            // P (R_P) is read: the rest of the next chunk's tile set (its P tiles) streams in during the epilogue
+            if (tid == 0 && tb_pending && has_next)
+                bulk_g2s(smem + R_P, tiles + (size_t)(c + 1) * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
 
             // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
             // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
@@ -724,6 +904,7 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     }
 
     cp_async_wait_all();
+    if (tid == 0 && tb_pending) mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS);   // no copy lands after the CTA ends
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
@@ -736,22 +917,39 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!r.wy_counter) return cudaErrorInvalidValue;
+    if (!r.wy_counter || !r.wy_tiles || !r.wy_cb || !r.wy_plan) return cudaErrorInvalidValue;
     if (g_wy_sms[dev] == 0) {
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(gdn_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WY_SMEM);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(gdn_wy_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A_SMEM);
+        if (e != cudaSuccess) return e;
         g_wy_sms[dev] = sms;
     }
     const int n_items = r.n_seq * r.hv;
     if (n_items == 0) return cudaSuccess;
-    e = cudaMemsetAsync(r.wy_counter, 0, sizeof(int32_t), stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c = {};
+    c.stream = stream;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    c.gridDim = dim3(1, 1, 1);
+    c.blockDim = dim3(WP_THREADS, 1, 1);
+    e = cudaLaunchKernelEx(&c, gdn_wy_plan_kernel, r);
     if (e != cudaSuccess) return e;
-    const int grid = n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev];
-    gdn_wy_kernel<<<grid, WY_THREADS, WY_SMEM, stream>>>(r);
-    return cudaGetLastError();
+    c.gridDim = dim3((unsigned)(2 * g_wy_sms[dev]), 1, 1);
+    c.blockDim = dim3(WA_THREADS, 1, 1);
+    c.dynamicSmemBytes = A_SMEM;
+    e = cudaLaunchKernelEx(&c, gdn_wy_chunk_kernel, r);
+    if (e != cudaSuccess) return e;
+    c.gridDim = dim3((unsigned)(n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev]), 1, 1);
+    c.blockDim = dim3(WY_THREADS, 1, 1);
+    c.dynamicSmemBytes = WY_SMEM;
+    return cudaLaunchKernelEx(&c, gdn_wy_kernel, r);
 }
 
 }  // namespace gdn
