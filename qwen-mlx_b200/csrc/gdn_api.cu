@@ -80,7 +80,8 @@ struct gdn_pool {
     uint16_t* mix;           // scratch [rec_cap][hidden]: mixer output
     uint8_t* recs;           // scratch: per-(v-head, token) records of the layer step [Hv][rec_cap][REC_BYTES]
     long long rec_cap;       // tokens per call the scratch holds
-    uint8_t* wy_tiles;       // scratch: chunked-prefill tile sets [wy_cap][Hv][WY_TILESET_BYTES]
+    uint8_t* wy_tiles;       // scratch: chunked-prefill tile sets [wy_cap][Hv][WY_TILESET_BYTES], then the chunk
+                             // table [wy_cap] int2
     long long wy_cap;        // chunks the tile scratch holds (rec_cap / 32 + 1: segments of >= 32 tokens)
     int32_t* wy_cb;          // chunked-prefill plan: chunk prefix per sequence [65536] ...
     int32_t* wy_plan;        // ... and the chunk count, sequence count and ranking [WY_PLAN_INTS]
@@ -94,7 +95,7 @@ static long long proj_ld(const gdn_pool* p) { return (long long)p->D + p->cfg.n_
 static long long wy_chunks_for(long long tokens) { return tokens / gdn::WY_MIN_T + 1; }
 
 static size_t wy_tile_bytes(const gdn_pool* p, long long tokens) {
-    return (size_t)wy_chunks_for(tokens) * p->cfg.n_v_heads * gdn::WY_TILESET_BYTES;
+    return (size_t)wy_chunks_for(tokens) * (p->cfg.n_v_heads * (size_t)gdn::WY_TILESET_BYTES + sizeof(int2));
 }
 
 static int reserve_records(gdn_pool* p, long long tokens) {
@@ -494,6 +495,7 @@ static int layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, co
     ra.wy_counter = p->err + 1;
     ra.wy_tiles = p->wy_tiles;
     ra.wy_cap_chunks = p->wy_cap;
+    ra.wy_chunks = reinterpret_cast<int2*>(p->wy_tiles + (size_t)p->wy_cap * p->cfg.n_v_heads * gdn::WY_TILESET_BYTES);
     ra.wy_cb = p->wy_cb;
     ra.wy_plan = p->wy_plan;
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
@@ -524,9 +526,24 @@ static bool wg_rows_ok(int K, const void* x, long long ldx, const void* tiles) {
     return K % 8 == 0 && ldx % 8 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)tiles & 15u) == 0;
 }
 
-// y = x w^T on the weight-streaming kernel, in token blocks of WG_MAX_M (each block streams the weight).
+// y = x w^T on the weight-streaming kernel, in token blocks of WG_MAX_M (each block streams the weight); a 4-bit
+// call of at most 16 tokens runs the kernel with the dequantized weight in tensor memory instead.
 static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, long long ldx, const void* tiles,
                   uint16_t* y, long long ldy, cudaStream_t s, const char* what) {
+    if (q4 && gdn::wq16_supported(M, N, K)) {
+        gdn::WgGemm g;
+        g.tiles = reinterpret_cast<const uint8_t*>(tiles);
+        g.q4 = true;
+        g.x = x; g.ldx = ldx;
+        g.y = y; g.ldy = ldy;
+        g.M = M; g.N = N; g.K = K;
+        g.n_sm = p->n_sm; g.ws = p->wg_ws; g.cnt = p->wg_cnt; g.err = p->err;
+        const cudaError_t e = gdn::launch_wq16(g, s);
+        if (e != cudaSuccess)
+            return fail(GDN_E_CUDA, "%s: 4-bit projection launch failed (M=%d N=%d K=%d): %s", what, M, N, K,
+                        cudaGetErrorString(e));
+        return GDN_OK;
+    }
     for (int m0 = 0; m0 < M; m0 += gdn::WG_MAX_M) {
         gdn::WgGemm g;
         g.tiles = reinterpret_cast<const uint8_t*>(tiles);
@@ -556,7 +573,8 @@ static int projection(gdn_pool* p, int M, int N, int K, const uint16_t* x, long 
         if (!wg_rows_ok(K, x, ldx, w_q4) || K % 64 != 0)
             return fail(GDN_E_INVALID, "%s: 4-bit projection needs K %% 64 == 0 and 16-byte aligned rows", what);
         const bool whole_slabs = (N + 7) / 8 >= 8 * p->n_sm;
-        if ((M > gdn::WG_MAX_M || !whole_slabs) && (size_t)N * K <= p->wdq_elems) {
+        const bool tmem_kernel = gdn::wq16_supported(M, N, K);   // <= 16 tokens: any row count
+        if ((M > gdn::WG_MAX_M || (!whole_slabs && !tmem_kernel)) && (size_t)N * K <= p->wdq_elems) {
             const cudaError_t e = gdn::launch_wq_untile(w_q4, N, K, p->wdq, s);
             if (e != cudaSuccess) return cuda_fail(e, "4-bit weight expansion");
             if (gdn::gemm_bf16_nt(p->gemm, M, N, K, x, ldx, p->wdq, y, ldy, s))

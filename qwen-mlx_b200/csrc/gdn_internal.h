@@ -76,6 +76,7 @@ struct RecurArgs {
     uint8_t* wy_tiles;           // per (chunk, v-head) tile sets of the chunk-parallel pass [wy_cap_chunks][Hv][48 KiB]
     long long wy_cap_chunks;     // chunks the tile scratch holds
     int32_t* wy_cb;              // [n_seq] chunk prefix per sequence (plan kernel)
+    int2* wy_chunks;             // [wy_cap_chunks] (first token row, tokens) of every chunk (plan kernel)
     int32_t* wy_plan;            // [0] chunks, [1] qualifying sequences, [2..] them longest first
 };
 
@@ -141,6 +142,10 @@ cudaError_t launch_wg_tile(const uint16_t* w, int N, int K, uint8_t* tiles, cuda
 cudaError_t launch_wq_tile(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases, int N, int K,
                            uint8_t* tiles, cudaStream_t stream);
 cudaError_t launch_wg_gemm(const WgGemm& g, cudaStream_t stream);
+// The 4-bit projection for calls of at most 16 tokens with the dequantized weight in tensor memory
+// (gdn_wq16.cu); same arguments as launch_wg_gemm (q4 tiles).
+bool wq16_supported(int M, int N, int K);
+cudaError_t launch_wq16(const WgGemm& g, cudaStream_t stream);
 // 4-bit tiles (wq_tile_bytes layout, K % 64 == 0) -> row-major bf16 weight w [N][K], 16-byte aligned.
 cudaError_t launch_wq_untile(const void* tiles, int N, int K, uint16_t* w, cudaStream_t stream);
 

@@ -233,6 +233,9 @@ __global__ void __launch_bounds__(WP_THREADS, 1) gdn_wy_plan_kernel(const RecurA
         __syncthreads();
         const int excl = s_run + (warp ? s_warp[warp - 1] : 0) + x - nc;
         if (i < a.n_seq) a.wy_cb[i] = excl;
+        // the chunk table of the chunk-parallel pass: (first token row, tokens) of every chunk
+        for (int c = 0; c < nc && excl + c < a.wy_cap_chunks; ++c)
+            a.wy_chunks[excl + c] = make_int2(t0 + c * WC, (T - c * WC) < WC ? (T - c * WC) : WC);
         __syncthreads();
         if (tid == 0) s_run += s_warp[WP_THREADS / 32 - 1];
         __syncthreads();
@@ -461,19 +464,9 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
 
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
         const int g = it / a.hk, hk = it - g * a.hk;
-        // the sequence holding chunk g: the last one whose chunk prefix is <= g
-        int lo = 0, hi = a.n_seq;
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (__ldg(a.wy_cb + mid) <= g) lo = mid; else hi = mid;
-        }
-        const int seq = lo;
-        const int cb = __ldg(a.wy_cb + seq);
-        const int c = g - cb;
-        int t0, T, slot;
-        if (!wy_qualifies(a, seq, t0, T, slot) || c < 0 || c * WC >= T) continue;   // not reached
-        const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
-        const long long row = (long long)t0 + (long long)c * WC;
+        const int2 chunk = __ldg(a.wy_chunks + g);   // (first token row, tokens) from the plan
+        const int nv = chunk.y;
+        const long long row = chunk.x;
         const uint8_t* recq = a.recs + ((long long)(hk * ratio) * a.rec_cap + row) * REC_BYTES;
         load_field(sb + A_QK, recq, 0, nv, tid);
         load_field(sb + A_QK + 16384, recq, 256, nv, tid);
@@ -500,7 +493,7 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
             const int j = j0 + grp;
             if (j < ratio) {
                 const int hv = hk * ratio + j;
-                uint8_t* out = a.wy_tiles + ((size_t)(cb + c) * a.hv + hv) * TILESET;
+                uint8_t* out = a.wy_tiles + ((size_t)g * a.hv + hv) * TILESET;
                 wa_head(a, out, fT, fN, s_lg + j * WC, s_gam + j * WC, s_beta + j * WC, tcol, gt, 1 + grp);
             }
         }
@@ -667,10 +660,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
             {
                 const float g_last = gamc[WC - 1];
+                uint32_t sr[4][16];   // the thread's 64 state columns: four loads in flight, one wait
+#pragma unroll
+                for (int j = 0; j < 4; ++j) tmem_ld16_async(tmem + lane_base + TM_S + hh * 64 + j * 16, sr[j]);
+                tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     float sv[16];
-                    tmem_ld16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) sv[e] = __uint_as_float(sr[j][e]);
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
                         uint4 hi, lo;
@@ -701,12 +699,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             cp_async_commit();
 
             // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
+            uint32_t wr[2][16];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_W + hh * 32 + j * 16, wr[j]);
+            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 float wv[16];
-                tmem_ld16(tmem + lane_base + TM_W + hh * 32 + j * 16, wv);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) wv[e] = -wv[e];
+                for (int e = 0; e < 16; ++e) wv[e] = -__uint_as_float(wr[j][e]);
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     uint4 hi, lo;
@@ -737,10 +738,15 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
             // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
+            uint32_t dr[2][16];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_U + hh * 32 + j * 16, dr[j]);
+            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 float dv[16];
-                tmem_ld16(tmem + lane_base + TM_U + hh * 32 + j * 16, dv);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) dv[e] = __uint_as_float(dr[j][e]);
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     uint4 hi, lo;
@@ -797,16 +803,21 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
 
             // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
             // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
+            {
+                uint32_t qr[2][16], pr[2][16];
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                float qs[16], pd[16];
-                tmem_ld16(tmem + lane_base + TM_QS + hh * 32 + j * 16, qs);
-                tmem_ld16(tmem + lane_base + TM_PD + hh * 32 + j * 16, pd);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int t = hh * 32 + j * 16 + e;
-                    s_yt[t * LDY + L] = f2bf(gamc[t] * qs[e] + pd[e]);
+                for (int j = 0; j < 2; ++j) {
+                    tmem_ld16_async(tmem + lane_base + TM_QS + hh * 32 + j * 16, qr[j]);
+                    tmem_ld16_async(tmem + lane_base + TM_PD + hh * 32 + j * 16, pr[j]);
                 }
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int t = hh * 32 + j * 16 + e;
+                        s_yt[t * LDY + L] = f2bf(gamc[t] * __uint_as_float(qr[j][e]) + __uint_as_float(pr[j][e]));
+                    }
             }
             cp_async_wait_group1();   // the next chunk's Q, K and gates (only its V may still be in flight)
             __syncthreads();
@@ -917,7 +928,7 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!r.wy_counter || !r.wy_tiles || !r.wy_cb || !r.wy_plan) return cudaErrorInvalidValue;
+    if (!r.wy_counter || !r.wy_tiles || !r.wy_cb || !r.wy_plan || !r.wy_chunks) return cudaErrorInvalidValue;
     if (g_wy_sms[dev] == 0) {
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

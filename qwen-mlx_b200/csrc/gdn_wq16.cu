@@ -1,0 +1,352 @@
+// gdn_wq16.cu -- the MLX 4-bit projection (quantized_matmul with transpose, bits 4, group 64;
+// qwen3_5.rs:572-586 in_proj_*, :668 out_proj on the reference's quantized checkpoint) for calls of at
+// most 16 tokens (decode), on tcgen05 tensor cores with the weight operand in tensor memory.
+//
+// y[m][n] = bf16(sum_k x[m][k] * w[n][k]), w = bf16(scale * q + bias) (one rounding per weight, as MLX's
+// quantized-matmul tile loader writes it), f32 accumulation.
+//
+// A decode call moves each 4-bit weight once for 2 * M flops, so the kernel is a stream over the codes.
+// Dequantizing into shared memory and letting the tensor core read the bf16 weight from there caps the
+// stream: the tensor core takes its A operand from shared memory at ~45 B/cycle, 4x the bytes of the
+// codes.  Here the dequantized weight goes into TENSOR MEMORY instead (tcgen05.st from the registers of the
+// thread that decoded it) and the MMA reads A from there (tcgen05.mma ... [a_tmem]); shared memory holds
+// only the codes and the tokens.
+//
+// Layout: the 4-bit tiles of gdn_weight_tile_q4 (block (kt, rg) = 8 rows x one 64-column group, 288 B at
+// (kt * NRG + rg) * 288: code word (c, r) at c*32 + r*4, 8 scales at 256, 8 biases at 272).  A CTA owns a
+// slab of at most 16 row groups (128 rows, one M = 128 MMA; rows past the slab are never written) and a range
+// of k-tiles; per k-tile its blocks are one contiguous bulk copy.  When the row groups allow >= 8 per SM (the
+// in-projection) every CTA takes a whole slab over all k-tiles; otherwise (the out-projection) 128-row slabs
+// are split along k and the last CTA of a slab to finish adds the f32 partials in split order (per-slab
+// arrival counter), so the output repeats bit for bit.
+//
+// Roles (320 threads): warp 0 lane 0 streams the slab's codes (issued before the dependency wait: the weight
+// does not depend on earlier kernels); warp 1 allocates tensor memory and lane 0 issues the MMAs; warps 2-9
+// load the tokens into shared memory, then decode: warp 2 + q and 6 + q take TMEM lane quarter q (rows
+// 32q..32q+31, one row per lane), even and odd k-tiles respectively, each k-tile into one of 4 A buffers of
+// 32 TMEM columns (64 bf16 per row), and afterwards warps 2-5 drain the accumulator.  Every wait is bounded
+// (2 s; ERR_TIMEOUT, the CTA winds down).
+#include <cuda_runtime.h>
+
+#include "gdn_device.cuh"
+#include "gdn_internal.h"
+#include "gdn_umma.cuh"
+
+namespace gdn {
+
+namespace {
+
+constexpr int Q16_THREADS = 32 * 10;
+constexpr int Q16_BLK = 288;               // 4-bit block: 8 rows x 64 columns (codes, scales, biases)
+constexpr int Q16_MP = 16;                 // tokens (MMA N), zero-padded
+constexpr int Q16_NA = 4;                  // A buffers in TMEM (32 columns each)
+constexpr uint32_t Q16_TM_D = 0;           // accumulator [128 rows][16 tokens] f32
+constexpr uint32_t Q16_TM_A = 32;          // A buffers: columns [32, 160)
+constexpr uint32_t Q16_TM_COLS = 256;
+constexpr uint64_t Q16_WAIT_NS = 2000000000ull;
+constexpr int Q16_MAX_KT = 64;             // k-tiles a CTA holds at once (one barrier each)
+constexpr int Q16_SMEM_MAX = 220 * 1024;
+
+struct Q16Args {
+    const uint8_t* tiles;
+    const uint16_t* x;
+    long long ldx;
+    uint16_t* y;
+    long long ldy;
+    int M, N, K;
+    int NRG, KT;          // row groups, k-tiles
+    int NS, splits, ktc;  // slabs, k splits per slab, k-tiles per split
+    int wbytes;           // shared-memory bytes of one k-tile's codes (nrg_max * 288)
+    float* ws;            // [NS][splits][128][16] f32 partial sums (splits > 1)
+    int* cnt;             // [NS] arrival counters (zero between launches)
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t q16_bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// D (TMEM) (+)= A (TMEM, K-major) * B (smem)^T: one k-step issued by a single thread.
+__device__ __forceinline__ void umma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+__global__ void __launch_bounds__(Q16_THREADS, 1) gdn_wq16_kernel(const Q16Args a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int slab = (int)blockIdx.x / a.splits, split = (int)blockIdx.x - slab * a.splits;
+    const int rg0 = (int)(((long long)slab * a.NRG) / a.NS), rg1 = (int)(((long long)(slab + 1) * a.NRG) / a.NS);
+    const int nrg = rg1 - rg0;
+    const int kt0 = split * a.ktc;
+    const int nkt = (a.KT - kt0) < a.ktc ? (a.KT - kt0) : a.ktc;
+    const int KL = nkt * 64;                                  // the CTA's k range
+    uint8_t* s_w = smem;                                      // [nkt][wbytes] codes
+    uint8_t* s_x = smem + (size_t)a.ktc * a.wbytes;           // tokens [16][KL] bf16, K-major core matrices
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_x + (size_t)a.ktc * 64 * Q16_MP * 2);
+    uint64_t* wfull = bars;                                   // [Q16_MAX_KT] codes of k-tile i landed
+    uint64_t* afull = wfull + Q16_MAX_KT;                     // [NA] A buffer written (128 threads)
+    uint64_t* afree = afull + Q16_NA;                         // [NA] A buffer read by its MMAs
+    uint64_t* xfull = afree + Q16_NA;                         // tokens stored (256 threads)
+    uint64_t* dfull = xfull + 1;                              // accumulator complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_last = const_cast<int*>(s_abort + 1);
+
+    if (tid == 0) {
+        for (int i = 0; i < Q16_MAX_KT; ++i) mbar_init(wfull + i, 1);
+        for (int i = 0; i < Q16_NA; ++i) {
+            mbar_init(afull + i, 128);
+            mbar_init(afree + i, 1);
+        }
+        mbar_init(xfull, 256);
+        mbar_init(dfull, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, Q16_TM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- codes of the slab's k-tiles (static weight: before the dependency wait)
+        if (lane == 0) {
+            const uint32_t bytes = (uint32_t)nrg * Q16_BLK;
+            for (int i = 0; i < nkt; ++i) {
+                mbar_arrive_expect_tx(wfull + i, bytes);
+                bulk_g2s(s_w + (size_t)i * a.wbytes, a.tiles + ((size_t)(kt0 + i) * a.NRG + rg0) * Q16_BLK, bytes,
+                         wfull + i);
+            }
+        }
+        pdl_wait();
+    } else if (warp == 1) {
+        pdl_wait();
+        // ---- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_bf16(128, Q16_MP);
+            bool ok = mbar_wait_bounded(xfull, 0, Q16_WAIT_NS);
+            for (int i = 0; ok && i < nkt; ++i) {
+                const int b = i % Q16_NA;
+                if (!mbar_wait_bounded(afull + b, (uint32_t)(i / Q16_NA) & 1u, Q16_WAIT_NS)) { ok = false; break; }
+                tc_fence_after();
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t bd = umma_desc(smem_u32(s_x), KL, i * 4 + s);
+                    umma_bf16_ta(tmem + Q16_TM_D, tmem + Q16_TM_A + b * 32 + s * 8, bd, idesc, (i | s) != 0);
+                }
+                umma_commit(afree + b);
+            }
+            if (!ok) {
+                atomicOr(a.err, ERR_TIMEOUT);
+                *s_abort = 1;
+            }
+            // dfull completes when every MMA issued above has: the epilogue reads the accumulator after it,
+            // and after a timeout this thread waits for it so no MMA is in flight when the CTA ends
+            umma_commit(dfull);
+            if (!ok) mbar_wait_bounded(dfull, 0, Q16_WAIT_NS);
+        }
+    } else {
+        // ---- tokens into shared memory: rows >= M zero (16-byte chunks of 8 columns)
+        pdl_wait();
+        const int dt = tid - 64;                               // 0..255
+        const int chunks = Q16_MP * (KL / 8);
+        for (int q = dt; q < chunks; q += 256) {
+            const int r = q / (KL / 8), c8 = q - r * (KL / 8);
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (r < a.M) v = *reinterpret_cast<const uint4*>(a.x + (long long)r * a.ldx + (long long)kt0 * 64 + c8 * 8);
+            *reinterpret_cast<uint4*>(s_x + umma_tile_off(r, c8 * 8, KL)) = v;
+        }
+        fence_async_shared();
+        mbar_arrive(xfull);
+        // ---- decode: quarter qd (rows 32 qd + lane), k-tiles of parity par
+        const int dw = warp - 2, qd = dw & 3, par = dw >> 2;
+        const int r = 32 * qd + lane;                          // row within the slab
+        const bool row_ok = r < nrg * 8;
+        const int rg = r >> 3, r8 = r & 7;
+        const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + Q16_TM_A;
+        bool ok = true;
+        for (int i = par; i < nkt; i += 2) {
+            const int b = i % Q16_NA;
+            bool w_ok = true;
+            if (i >= Q16_NA) w_ok = mbar_wait_bounded(afree + b, (uint32_t)((i - Q16_NA) / Q16_NA) & 1u, Q16_WAIT_NS);
+            w_ok = w_ok && mbar_wait_bounded(wfull + i, 0, Q16_WAIT_NS);
+            if (!w_ok) { ok = false; break; }
+            tc_fence_after();
+            uint32_t v[32];
+            if (row_ok) {
+                const uint8_t* blk = s_w + (size_t)i * a.wbytes + rg * Q16_BLK;
+                const uint16_t s1 = *reinterpret_cast<const uint16_t*>(blk + 256 + 2 * r8);
+                const uint16_t b1 = *reinterpret_cast<const uint16_t*>(blk + 272 + 2 * r8);
+                const uint32_t s2 = (uint32_t)s1 | ((uint32_t)s1 << 16), b2 = (uint32_t)b1 | ((uint32_t)b1 << 16);
+                const uint32_t one2 = 0x3F803F80u, m128 = 0xC300C300u;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + c * 32 + r8 * 4);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        // (nib | 0x4300) is the bf16 of 128 + q exactly; -128 is exact; then scale * q + bias
+                        // rounded once: columns 8c + 2j, 8c + 2j + 1
+                        const uint32_t t = ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+                        v[c * 4 + j] = q16_bf16x2_fma(q16_bf16x2_fma(t, one2, m128), s2, b2);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) v[c] = 0u;
+            }
+            tmem_st32(ta + b * 32, v);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(afull + b);
+        }
+        if (!ok) {
+            atomicOr(a.err, ERR_TIMEOUT);
+            *s_abort = 1;
+        }
+        // ---- epilogue (warps 2-5): the accumulator rows of this quarter
+        if (par == 0) {
+            const bool d_ok = ok && mbar_wait_bounded(dfull, 0, Q16_WAIT_NS) && !*s_abort;
+            tc_fence_after();
+            float d[16];
+            if (d_ok) {
+                tmem_ld16(tmem + ((uint32_t)(qd * 32) << 16) + Q16_TM_D, d);
+            } else {
+#pragma unroll
+                for (int m = 0; m < 16; ++m) d[m] = 0.f;
+            }
+            const int n = rg0 * 8 + r;
+            if (a.splits == 1) {
+                if (d_ok && row_ok && n < a.N)
+                    for (int m = 0; m < a.M; ++m) a.y[(long long)m * a.ldy + n] = f2bf(d[m]);
+            } else {
+                // partial sums of this split; the slab's last split to arrive adds them in split order
+                float* part = a.ws + (((size_t)slab * a.splits + split) * 128 + r) * Q16_MP;
+#pragma unroll
+                for (int m = 0; m < 16; m += 4)
+                    *reinterpret_cast<float4*>(part + m) = make_float4(d[m], d[m + 1], d[m + 2], d[m + 3]);
+                __threadfence();
+                named_bar_sync(1, 128);
+                if (tid == 64) *s_last = atomicAdd(a.cnt + slab, 1) == a.splits - 1;
+                named_bar_sync(1, 128);
+                if (*s_last) {
+                    __threadfence();
+                    float acc[16];
+#pragma unroll
+                    for (int m = 0; m < 16; ++m) acc[m] = 0.f;
+                    for (int sp = 0; sp < a.splits; ++sp) {
+                        const float* p = a.ws + (((size_t)slab * a.splits + sp) * 128 + r) * Q16_MP;
+#pragma unroll
+                        for (int m = 0; m < 16; m += 4) {
+                            const float4 q4 = __ldcg(reinterpret_cast<const float4*>(p + m));
+                            acc[m] += q4.x; acc[m + 1] += q4.y; acc[m + 2] += q4.z; acc[m + 3] += q4.w;
+                        }
+                    }
+                    if (row_ok && n < a.N)
+                        for (int m = 0; m < a.M; ++m) a.y[(long long)m * a.ldy + n] = f2bf(acc[m]);
+                    if (tid == 64) a.cnt[slab] = 0;   // zero at rest for the next launch
+                }
+            }
+        }
+    }
+    // no code copy may land after the CTA ends: every k-tile's copy was waited for by its decoder unless a
+    // wait gave up, in which case thread 0 waits (bounded) for the rest
+    __syncthreads();
+    if (tid == 0 && *s_abort)
+        for (int i = 0; i < nkt; ++i) mbar_wait_bounded(wfull + i, 0, Q16_WAIT_NS);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, Q16_TM_COLS);
+}
+
+static bool g_q16_attr[64] = {};
+
+}  // namespace
+
+// Whether gdn_wq16_kernel serves a call: at most 16 tokens, K a multiple of 64, and a k-split whose codes and
+// tokens fit in shared memory.
+bool wq16_supported(int M, int N, int K) { return M >= 1 && M <= Q16_MP && K % 64 == 0 && N > 0; }
+
+cudaError_t launch_wq16(const WgGemm& g, cudaStream_t stream) {
+    if (!wq16_supported(g.M, g.N, g.K)) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    Q16Args a;
+    a.tiles = g.tiles;
+    a.x = g.x;
+    a.ldx = g.ldx;
+    a.y = g.y;
+    a.ldy = g.ldy;
+    a.M = g.M;
+    a.N = g.N;
+    a.K = g.K;
+    a.NRG = (g.N + 7) / 8;
+    a.KT = g.K / 64;
+    if (a.NRG >= 8 * g.n_sm) {
+        // whole slabs: one per SM when they stay within 16 row groups
+        a.NS = g.n_sm * ((a.NRG + 16 * g.n_sm - 1) / (16 * g.n_sm));
+        a.splits = 1;
+    } else {
+        // 128-row slabs split along k so that the CTAs cover the SMs
+        a.NS = (a.NRG + 15) / 16;
+        a.splits = g.n_sm / a.NS > 1 ? g.n_sm / a.NS : 1;
+        if (a.splits > a.KT) a.splits = a.KT;
+    }
+    int nrg_max = (a.NRG + a.NS - 1) / a.NS;
+    a.ktc = (a.KT + a.splits - 1) / a.splits;
+    a.wbytes = nrg_max * Q16_BLK;
+    // more splits while a split's codes and tokens exceed the shared-memory budget or the barrier count
+    while ((size_t)a.ktc * (a.wbytes + 64 * Q16_MP * 2) > (size_t)Q16_SMEM_MAX || a.ktc > Q16_MAX_KT) {
+        ++a.splits;
+        a.ktc = (a.KT + a.splits - 1) / a.splits;
+    }
+    a.splits = (a.KT + a.ktc - 1) / a.ktc;   // no empty split
+    if (a.splits > 1 && (long long)a.NS * a.splits * 128 * Q16_MP > wg_workspace_floats(g.n_sm))
+        return cudaErrorInvalidValue;
+    if (a.NS > 4096) return cudaErrorInvalidValue;   // arrival counters of the pool
+    a.ws = g.ws;
+    a.cnt = g.cnt;
+    a.err = g.err;
+    const size_t smem = (size_t)a.ktc * (a.wbytes + 64 * Q16_MP * 2) + (Q16_MAX_KT + 2 * Q16_NA + 2) * 8 + 16;
+    if (!g_q16_attr[dev]) {
+        e = cudaFuncSetAttribute(gdn_wq16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        g_q16_attr[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.NS * a.splits));
+    cfg.blockDim = dim3(Q16_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gdn_wq16_kernel, a);
+}
+
+}  // namespace gdn
