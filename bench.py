@@ -811,6 +811,8 @@ def run_ours(args):
     tr_per_seq, _ = profiled_traffic()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                 "traffic": (tr_per_seq * B if tr_per_seq else None), "peak_kind": peak_kind,
+                "traffic_source": "profiles/gdn_layer_step_decode.txt: per-sequence DRAM reads + the bytes the SMs "
+                                  "write into L2 (all of which reach DRAM) of one K1 + K2 pair at B=63, x B",
                 "kernel": "gdn_layer_step = gdn_prep_kernel + gdn_recur_kernel (PDL-chained)",
                 "launch_us": launch_ms * 1e3,
                 "alg_bytes_per_launch": alg_bytes,

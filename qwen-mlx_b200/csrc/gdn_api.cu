@@ -539,10 +539,11 @@ static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, 
         g.M = M; g.N = N; g.K = K;
         g.n_sm = p->n_sm; g.ws = p->wg_ws; g.cnt = p->wg_cnt; g.err = p->err;
         const cudaError_t e = gdn::launch_wq16(g, s);
-        if (e != cudaSuccess)
+        if (e == cudaSuccess) return GDN_OK;
+        if (e != cudaErrorNotSupported)
             return fail(GDN_E_CUDA, "%s: 4-bit projection launch failed (M=%d N=%d K=%d): %s", what, M, N, K,
                         cudaGetErrorString(e));
-        return GDN_OK;
+        // K too long for the tensor-memory kernel's k-splits: stream the weight below
     }
     for (int m0 = 0; m0 < M; m0 += gdn::WG_MAX_M) {
         gdn::WgGemm g;

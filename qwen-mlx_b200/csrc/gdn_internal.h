@@ -2,6 +2,7 @@
 // kernels (.cu) and the C ABI implementation (gdn_api.cu).  Not installed.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -142,6 +143,11 @@ cudaError_t launch_wg_tile(const uint16_t* w, int N, int K, uint8_t* tiles, cuda
 cudaError_t launch_wq_tile(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases, int N, int K,
                            uint8_t* tiles, cudaStream_t stream);
 cudaError_t launch_wg_gemm(const WgGemm& g, cudaStream_t stream);
+// Tiled TMA tensor map over a row-major bf16 matrix [rows][cols] (row stride ld_bytes, a multiple of 16; base
+// 16-byte aligned): box of box_cols (<= 64) x box_rows with 128-byte swizzle, out-of-range elements read as zero.
+// False when the driver's encoder is unavailable or rejects the arguments (gdn_tmap.cu).
+bool tmap_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
+                        uint32_t box_cols, uint32_t box_rows);
 // The 4-bit projection for calls of at most 16 tokens with the dequantized weight in tensor memory
 // (gdn_wq16.cu); same arguments as launch_wg_gemm (q4 tiles).
 bool wq16_supported(int M, int N, int K);

@@ -71,6 +71,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Tiled tensor load (TMA) of a 2-D box at coordinates (c0 innermost, c1) through the tensor map at `tmap`
+// (a __grid_constant__ kernel parameter), completing on `bar` (tx bytes = the whole box, out-of-range
+// elements written as zero).  c0 * element size must be a multiple of 16 bytes; no multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later async-proxy accesses.
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
@@ -89,6 +100,19 @@ __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bu
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 // Programmatic dependent launch.
+// One lane of the (fully active) warp gets true: issue a single-thread instruction from warp-uniform code.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n"
+        " .reg .pred P;\n"
+        " elect.sync _|P, 0xffffffff;\n"
+        " selp.b32 %0, 1, 0, P;\n"
+        "}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
@@ -156,6 +180,19 @@ __device__ __forceinline__ void st_cluster_f32(const void* local, uint32_t rank,
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
     asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(remote), "f"(v) : "memory");
+}
+
+// Load four f32 from the shared memory of CTA `rank` of this cluster, at the address `local` has in this CTA
+// (distributed shared memory; 16-byte aligned).
+__device__ __forceinline__ float4 ld_cluster_f32x4(const void* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
 }
 
 }  // namespace gdn

@@ -35,6 +35,18 @@ __device__ __forceinline__ uint64_t umma_desc_raw(uint32_t start, uint32_t lbo, 
     return d;
 }
 
+// Descriptor of a 128-byte-swizzled K-major tile (the layout a SWIZZLE_128B tensor load writes): rows of 64 bf16
+// (128 B) whose 16-byte chunks are permuted by row % 8, 8-row atoms of 1024 B (SBO), atom-aligned base.  A k-step
+// of 16 elements within the 64-element row advances the start address by 32 B.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;          // LBO: not used by swizzled K-major layouts
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;          // descriptor version of sm_100
+    d |= (uint64_t)2 << 61;          // SWIZZLE_128B
+    return d;
+}
+
 // Descriptor of a tile [R][KT] read K-major (the MMA's K runs along the tile's columns),
 // advanced by `kstep` k-steps of 16 elements: LBO 128 B, SBO KT*16 B, step 256 B.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, int KT, int kstep) {
