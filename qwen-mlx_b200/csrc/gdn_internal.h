@@ -148,6 +148,12 @@ cudaError_t launch_wg_gemm(const WgGemm& g, cudaStream_t stream);
 // False when the driver's encoder is unavailable or rejects the arguments (gdn_tmap.cu).
 bool tmap_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
                         uint32_t box_cols, uint32_t box_rows);
+// TMA tensor map over the token records [n_heads][rec_cap][rec_bytes] as 4-D u16 elements (e: 8 per 16-byte
+// chunk, t: token row < n_tokens, c: 16-byte chunk of the record, h: head), box {8, box_tokens, box_chunks, 1}:
+// a box lands as offset(t, c, e) = c * box_tokens * 16 + t * 16 + e * 2, the no-swizzle core-matrix layout with
+// token rows 16 bytes apart; rows >= n_tokens read as zero (gdn_tmap.cu).
+bool tmap_records(CUtensorMap* map, const void* recs, int n_tokens, long long rec_cap, int n_heads, int rec_bytes,
+                  uint32_t box_tokens, uint32_t box_chunks);
 // The 4-bit projection for calls of at most 16 tokens with the dequantized weight in tensor memory
 // (gdn_wq16.cu); same arguments as launch_wg_gemm (q4 tiles).
 bool wq16_supported(int M, int N, int K);

@@ -67,8 +67,9 @@ static_assert(R_N + 6 * 256 * 4 <= R_TB, "prefill shared memory layout");
 static_assert(R_P == R_TB + 32768, "the chunk tile set lands in one bulk copy");
 constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
 static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
-constexpr int SMALL_FLOATS = 2 * 64 + 2 * 64 + 3 * 2 * 64 + 128;
-constexpr int WY_SMEM = R_SMALL + SMALL_FLOATS * 4 + 96;
+constexpr int SMALL_FLOATS = 3 * 2 * 64 + 128;
+constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 96 + 1023) / 1024) * 1024;   // gate boxes [2][64 t][16 B]
+constexpr int WY_SMEM = R_G + 2 * WC * 16;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
 constexpr uint32_t TM_S = 0, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
 constexpr uint64_t WY_WAIT_NS = 2000000000ull;
@@ -149,9 +150,9 @@ __device__ __forceinline__ void wy_sync_for_mma() {
     tc_fence_after();
 }
 
-// Inclusive scan of one chunk's log g (log2 units), gamma_t = exp(lg_t) and exp(lg_last - lg_t) (one warp).
-__device__ __forceinline__ void wy_scan(const float* lgr, float* lg, float* gam, float* tail, int lane) {
-    float x0 = lgr[lane], x1 = lgr[32 + lane];
+// Inclusive scan of one chunk's log g (log2 units), gamma_t = exp(lg_t) and exp(lg_last - lg_t) (one warp;
+// lane holds tokens lane and 32 + lane).
+__device__ __forceinline__ void wy_scan_core(float x0, float x1, float* lg, float* gam, float* tail, int lane) {
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
@@ -169,6 +170,16 @@ __device__ __forceinline__ void wy_scan(const float* lgr, float* lg, float* gam,
     gam[32 + lane] = exp2f(x1);
     tail[lane] = exp2f(last - x0);
     tail[32 + lane] = exp2f(last - x1);
+}
+
+__device__ __forceinline__ void wy_scan(const float* lgr, float* lg, float* gam, float* tail, int lane) {
+    wy_scan_core(lgr[lane], lgr[32 + lane], lg, gam, tail, lane);
+}
+
+// The same from a chunk's gate box (per token 16 bytes: g, beta, log g, pad); tokens >= nv count as log g = 0.
+__device__ __forceinline__ void wy_scan_g4(const float* g4, int nv, float* lg, float* gam, float* tail, int lane) {
+    wy_scan_core(lane < nv ? g4[lane * 4 + 2] : 0.0f, 32 + lane < nv ? g4[(32 + lane) * 4 + 2] : 0.0f, lg, gam, tail,
+                 lane);
 }
 
 __device__ __forceinline__ bool wy_qualifies(const RecurArgs& a, int seq, int& t0, int& T, int& slot) {
@@ -507,11 +518,20 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
 }
 
 // ------------------------------------------------------------------ sequential pass
-__global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a) {
+
+// Q, K and V tiles of the sequential pass arrive by TMA token-major: element (t, f) of a [64 t][128 f] tile at
+// (f / 8) * 1024 + t * 16 + (f % 8) * 2.  Read MN-major (K = t, M or N = f): 8-token groups 128 B apart (LBO),
+// 8-feature groups 1024 B apart (SBO), a k-step of 16 tokens advances 256 B.  Read K-major (K = f, M or N = t):
+// 8-feature groups 1024 B apart (LBO), 8-token groups 128 B apart (SBO), a k-step of 16 features advances 2048 B.
+__device__ __forceinline__ uint64_t tok_desc_mn(uint32_t saddr) { return umma_desc_raw(saddr, 128u, 1024u); }
+__device__ __forceinline__ uint64_t tok_desc_k(uint32_t saddr) { return umma_desc_raw(saddr, 1024u, 128u); }
+constexpr uint64_t TOK_KSTEP_MN = 256u >> 4, TOK_KSTEP_K = 2048u >> 4;
+__global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a,
+                                                                const __grid_constant__ CUtensorMap tm_rec,
+                                                                const __grid_constant__ CUtensorMap tm_gate) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* s_beta = reinterpret_cast<float*>(smem + R_SMALL);  // [2][64] (chunk parity)
-    float* s_lgr = s_beta + 2 * WC;                               // [2][64] log g per token
-    float* s_lg = s_lgr + 2 * WC;                                 // [2][64] cumulative, log2 units
+    const float* s_g4 = reinterpret_cast<const float*>(smem + R_G);   // [2][64][4]: g, beta, log g, pad per token
+    float* s_lg = reinterpret_cast<float*>(smem + R_SMALL);       // [2][64] cumulative, log2 units
     float* s_gam = s_lg + 2 * WC;                                 // [2][64] exp(lg_t)
     float* s_tail = s_gam + 2 * WC;                               // [2][64] exp(lg_last - lg_t)
     float* s_nw = s_tail + 2 * WC;                                // norm_w [128]
@@ -519,7 +539,9 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     uint64_t* bar_qs = bar + 1;                                   // (Q S0^T)^T, issued early
     uint64_t* bar_s = bar + 2;                                    // state update, waited when S is next used
     uint64_t* bar_tb = bar + 3;                                   // the chunk's tile set (bulk copy)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+    uint64_t* bar_in = bar + 4;                                   // [2] Q, K and gates of the chunk of that parity
+    uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 7);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
@@ -535,6 +557,9 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         mbar_init(bar_qs, 1);
         mbar_init(bar_s, 1);
         mbar_init(bar_tb, 1);
+        mbar_init(bar_in, 1);
+        mbar_init(bar_in + 1, 1);
+        mbar_init(bar_v, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -545,8 +570,11 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0;
+    uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0, ph_v = 0;
+    uint32_t ph_in = 0;        // bit b: the phase of bar_in[b] to wait for next
     bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
+    uint32_t in_pending = 0;   // (thread 0) bit b: a bar_in[b] load issued and not yet waited for
+    bool v_pending = false;    // (thread 0) the same for bar_v
     pdl_wait();
 
     const int total = __ldg(a.wy_plan);
@@ -579,13 +607,23 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             bulk_g2s(smem + R_TB, tiles, TILESET, bar_tb);
             tb_pending = true;
         }
-        {
-            const int nv = T < WC ? T : WC;
-            load_field(sb + R_QK, recb, 0, nv, tid);
-            load_field(sb + R_QK + 16384, recb, 256, nv, tid);
-            load_field(sb + R_V, recb, 512, nv, tid);
-            load_gates(s_beta, s_lgr, recb, nv, tid);
-            cp_async_commit();
+        // Q, K and the gates of chunk cc into buffer b, V of chunk cc: TMA boxes of 64 token rows from the records
+        // (record chunks 0-15 Q, 16-31 K, 32-47 V, 64 the gates), landing token-major with rows 16 bytes apart
+        auto issue_qkg = [&](int cc, int b) {
+            mbar_arrive_expect_tx(bar_in + b, 2 * 16384 + WC * 16);
+            tma_load_4d(smem + R_QK + b * 32768, &tm_rec, 0, t0 + cc * WC, 0, hv, bar_in + b);
+            tma_load_4d(smem + R_QK + b * 32768 + 16384, &tm_rec, 0, t0 + cc * WC, 16, hv, bar_in + b);
+            tma_load_4d(smem + R_G + b * WC * 16, &tm_gate, 0, t0 + cc * WC, 64, hv, bar_in + b);
+            in_pending |= 1u << b;
+        };
+        auto issue_v = [&](int cc) {
+            mbar_arrive_expect_tx(bar_v, 16384);
+            tma_load_4d(smem + R_V, &tm_rec, 0, t0 + cc * WC, 32, hv, bar_v);
+            v_pending = true;
+        };
+        if (tid == 0) {
+            issue_qkg(0, 0);
+            issue_v(0);
         }
         // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
         {
@@ -608,7 +646,6 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
             const uint8_t* rec0 = recb + (size_t)c * WC * REC_BYTES;
             const bool has_next = c + 1 < n_chunks;
-            const uint8_t* rec1 = rec0 + (size_t)WC * REC_BYTES;
             const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
             const uint32_t sQ = sb + R_QK + kb * 32768;    // Q [64][128], then K [64][128] at +16384
             const uint32_t sK = sQ + 16384;
@@ -616,7 +653,17 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             const float* tailc = s_tail + kb * WC;
 
             // ---- phase A: this chunk's inputs and tile set landed; next chunk's Q, K and gates in flight
-            cp_async_wait_all();
+            {
+                const bool ok_q = mbar_wait_bounded(bar_in + kb, (ph_in >> kb) & 1u, WY_WAIT_NS);
+                const bool ok_v = mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
+                if (ok_q) ph_in ^= 1u << kb;   // a phase that did not complete is still waited for at the exit
+                if (ok_v) ph_v ^= 1u;
+                if (tid == 0) {
+                    if (ok_q) in_pending &= ~(1u << kb);
+                    if (ok_v) v_pending = false;
+                }
+                if (!(ok_q && ok_v)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            }
             if (c > 0) {
                 // the previous chunk's state update still reads the K buffer refilled below
                 if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
@@ -630,30 +677,36 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             }
             __syncthreads();
             if (*s_abort) break;
-            if (has_next) {
-                load_field(sb + R_QK + (kb ^ 1) * 32768, rec1, 0, nv1, tid);
-                load_field(sb + R_QK + (kb ^ 1) * 32768 + 16384, rec1, 256, nv1, tid);
-                load_gates(s_beta + (kb ^ 1) * WC, s_lgr + (kb ^ 1) * WC, rec1, nv1, tid);
+            // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
+            // state update, are complete)
+            if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
+            // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
+            // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
+            if (nv < WC) {
+                const int rows = WC - nv;
+                for (int idx = tid; idx < rows * 32; idx += WY_THREADS) {
+                    const int tile = idx / (rows * 16), rem = idx - tile * rows * 16;
+                    uint8_t* base = tile ? smem + R_V : smem + R_QK + kb * 32768 + 16384;
+                    *reinterpret_cast<uint4*>(base + (rem & 15) * 1024 + (nv + (rem >> 4)) * 16) = make_uint4(0, 0, 0, 0);
+                }
             }
-            cp_async_commit();
-            if (c == 0 && warp == 0) wy_scan(s_lgr, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
+            if (c == 0 && warp == 0) wy_scan_g4(s_g4, nv, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
             wy_sync_for_mma();
 
             // ---- phase B: U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major);
             // they need only the chunk's own inputs and overlap the state split below
             if (tid == 0) {
                 const uint32_t id = umma_idesc_bf16(128, 64, true, false);
-                const uint64_t dv = umma_desc_mn(sb + R_V, 128, 0), dk = umma_desc_mn(sK, 128, 0);
-                constexpr uint64_t kmn = umma_kstep_mn(128);
+                const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
                 for (int h = 0; h < 2; ++h) {
                     const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_U, dv + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                        umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
                 }
                 for (int h = 0; h < 2; ++h) {
                     const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_W, dk + ks * kmn, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                        umma_bf16(tmem + TM_W, dk + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
                 }
                 umma_commit(bar);
             }
@@ -686,17 +739,16 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             // (Q S0^T)^T = S0 Q^T -> QS, off the critical path (read in H)
             if (tid == 0) {
                 const uint32_t idq = umma_idesc_bf16(128, 64);
-                const uint64_t dq = umma_desc(sQ, 128, 0);
+                const uint64_t dq = tok_desc_k(sQ);
                 for (int h = 0; h < 2; ++h) {
                     const uint64_t ds = umma_desc(sb + R_X + h * 32768, 128, 0);
                     for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * KSTEP_K, idq, (h | ks) != 0);
+                        umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * TOK_KSTEP_K, idq, (h | ks) != 0);
                 }
                 umma_commit(bar_qs);
             }
             if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            if (has_next) load_field(sb + R_V, rec1, 512, nv1, tid);   // V is free
-            cp_async_commit();
+            if (tid == 0 && has_next) issue_v(c + 1);   // V is free
 
             // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
             uint32_t wr[2][16];
@@ -777,11 +829,11 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                 }
                 umma_commit(bar);
                 const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
-                const uint64_t dk = umma_desc_mn(sK, 128, 0);
-                constexpr uint64_t kmn = umma_kstep_mn(128);
+                const uint64_t dk = tok_desc_mn(sK);
                 for (int h = 0; h < 2; ++h) {
                     const uint64_t dd = umma_desc(sb + R_X + 32768 + h * 16384, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks) umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * kmn, ids, 1u);
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * TOK_KSTEP_MN, ids, 1u);
                 }
                 umma_commit(bar_s);
             }
@@ -819,10 +871,16 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
                         s_yt[t * LDY + L] = f2bf(gamc[t] * __uint_as_float(qr[j][e]) + __uint_as_float(pr[j][e]));
                     }
             }
-            cp_async_wait_group1();   // the next chunk's Q, K and gates (only its V may still be in flight)
             __syncthreads();
-            if (has_next && warp == 7)
-                wy_scan(s_lgr + (kb ^ 1) * WC, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC, s_tail + (kb ^ 1) * WC, lane);
+            if (has_next && warp == 7) {
+                // the next chunk's decay scan, from its gate box (the same barrier phase is waited again in phase A)
+                if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
+                    atomicOr(a.err, ERR_TIMEOUT);
+                    *s_abort = 1;
+                }
+                wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
+                           s_tail + (kb ^ 1) * WC, lane);
+            }
             {
                 const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
                 uint32_t yw[16];
@@ -873,7 +931,6 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
             __syncthreads();
             tc_fence_after();
         }
-        cp_async_wait_all();
         if (n_chunks > 0 && !*s_abort) {
             if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
             ph_s ^= 1u;
@@ -914,8 +971,12 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         tc_fence_after();
     }
 
-    cp_async_wait_all();
-    if (tid == 0 && tb_pending) mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS);   // no copy lands after the CTA ends
+    if (tid == 0) {   // no copy lands after the CTA ends (only after a wait gave up can one be outstanding)
+        if (tb_pending) mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS);
+        for (int b = 0; b < 2; ++b)
+            if ((in_pending >> b) & 1u) mbar_wait_bounded(bar_in + b, (ph_in >> b) & 1u, WY_WAIT_NS);
+        if (v_pending) mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
@@ -957,10 +1018,15 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     c.dynamicSmemBytes = A_SMEM;
     e = cudaLaunchKernelEx(&c, gdn_wy_chunk_kernel, r);
     if (e != cudaSuccess) return e;
+    // the sequential pass reads each chunk's Q, K, V and gates from the records by TMA
+    CUtensorMap tm_rec, tm_gate;
+    if (!tmap_records(&tm_rec, r.recs, r.n_tokens, r.rec_cap, r.hv, REC_BYTES, WC, 16) ||
+        !tmap_records(&tm_gate, r.recs, r.n_tokens, r.rec_cap, r.hv, REC_BYTES, WC, 1))
+        return cudaErrorNotSupported;
     c.gridDim = dim3((unsigned)(n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev]), 1, 1);
     c.blockDim = dim3(WY_THREADS, 1, 1);
     c.dynamicSmemBytes = WY_SMEM;
-    return cudaLaunchKernelEx(&c, gdn_wy_kernel, r);
+    return cudaLaunchKernelEx(&c, gdn_wy_kernel, r, tm_rec, tm_gate);
 }
 
 }  // namespace gdn

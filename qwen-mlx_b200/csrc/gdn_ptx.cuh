@@ -82,6 +82,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0,
         : "memory");
 }
 
+// Tiled tensor load (TMA) of a 4-D box at coordinates (c0 innermost .. c3); as tma_load_2d.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later async-proxy accesses.
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
