@@ -59,7 +59,8 @@
 namespace gdn {
 
 constexpr int WC = 64;                 // tokens per chunk
-constexpr int WY_THREADS = 256;
+constexpr int WY_THREADS = 256;       // compute threads of the sequential pass (and of the chunk pass)
+constexpr int WY_BLOCK = WY_THREADS + 32;   // the sequential pass adds one MMA-issuing warp
 constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
 constexpr int R_QK = 0, R_V = 65536, R_X = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
               R_P = 204800, R_SMALL = 221184;
@@ -68,7 +69,7 @@ static_assert(R_P == R_TB + 32768, "the chunk tile set lands in one bulk copy");
 constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
 static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
 constexpr int SMALL_FLOATS = 3 * 2 * 64 + 128;
-constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 96 + 1023) / 1024) * 1024;   // gate boxes [2][64 t][16 B]
+constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 160 + 1023) / 1024) * 1024;   // gate boxes [2][64 t][16 B]
 constexpr int WY_SMEM = R_G + 2 * WC * 16;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
 constexpr uint32_t TM_S = 0, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
@@ -519,6 +520,14 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
 
 // ------------------------------------------------------------------ sequential pass
 
+// A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
+__device__ __forceinline__ void ct_ready(uint64_t* rdy, int lane) {
+    fence_async_shared();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(rdy);
+}
+
 // Q, K and V tiles of the sequential pass arrive by TMA token-major: element (t, f) of a [64 t][128 f] tile at
 // (f / 8) * 1024 + t * 16 + (f % 8) * 2.  Read MN-major (K = t, M or N = f): 8-token groups 128 B apart (LBO),
 // 8-feature groups 1024 B apart (SBO), a k-step of 16 tokens advances 256 B.  Read K-major (K = f, M or N = t):
@@ -526,7 +535,7 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
 __device__ __forceinline__ uint64_t tok_desc_mn(uint32_t saddr) { return umma_desc_raw(saddr, 128u, 1024u); }
 __device__ __forceinline__ uint64_t tok_desc_k(uint32_t saddr) { return umma_desc_raw(saddr, 1024u, 128u); }
 constexpr uint64_t TOK_KSTEP_MN = 256u >> 4, TOK_KSTEP_K = 2048u >> 4;
-__global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a,
+__global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                                                                 const __grid_constant__ CUtensorMap tm_rec,
                                                                 const __grid_constant__ CUtensorMap tm_gate) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -541,7 +550,9 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     uint64_t* bar_tb = bar + 3;                                   // the chunk's tile set (bulk copy)
     uint64_t* bar_in = bar + 4;                                   // [2] Q, K and gates of the chunk of that parity
     uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 7);
+    uint64_t* rdy = bar + 7;       // [4] operands of an MMA batch written: U/W, QS, D, P D + state update
+    uint64_t* bar_fin = bar + 11;  // every MMA of the issuing warp complete (kernel exit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
@@ -560,6 +571,9 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         mbar_init(bar_in, 1);
         mbar_init(bar_in + 1, 1);
         mbar_init(bar_v, 1);
+        mbar_init(rdy, 1);               // thread 0, after a barrier of the compute warps
+        for (int i = 1; i < 4; ++i) mbar_init(rdy + i, WY_THREADS / 32);   // one arrival per compute warp
+        mbar_init(bar_fin, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -572,6 +586,7 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0, ph_v = 0;
     uint32_t ph_in = 0;        // bit b: the phase of bar_in[b] to wait for next
+    uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
     bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
     uint32_t in_pending = 0;   // (thread 0) bit b: a bar_in[b] load issued and not yet waited for
     bool v_pending = false;    // (thread 0) the same for bar_v
@@ -601,369 +616,397 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         const size_t tile_step = (size_t)a.hv * TILESET;   // next chunk of the same head
         const int n_chunks = (T + WC - 1) / WC;
 
-        // chunk 0's inputs
-        if (tid == 0) {
-            mbar_arrive_expect_tx(bar_tb, TILESET);
-            bulk_g2s(smem + R_TB, tiles, TILESET, bar_tb);
-            tb_pending = true;
-        }
-        // Q, K and the gates of chunk cc into buffer b, V of chunk cc: TMA boxes of 64 token rows from the records
-        // (record chunks 0-15 Q, 16-31 K, 32-47 V, 64 the gates), landing token-major with rows 16 bytes apart
-        auto issue_qkg = [&](int cc, int b) {
-            mbar_arrive_expect_tx(bar_in + b, 2 * 16384 + WC * 16);
-            tma_load_4d(smem + R_QK + b * 32768, &tm_rec, 0, t0 + cc * WC, 0, hv, bar_in + b);
-            tma_load_4d(smem + R_QK + b * 32768 + 16384, &tm_rec, 0, t0 + cc * WC, 16, hv, bar_in + b);
-            tma_load_4d(smem + R_G + b * WC * 16, &tm_gate, 0, t0 + cc * WC, 64, hv, bar_in + b);
-            in_pending |= 1u << b;
-        };
-        auto issue_v = [&](int cc) {
-            mbar_arrive_expect_tx(bar_v, 16384);
-            tma_load_4d(smem + R_V, &tm_rec, 0, t0 + cc * WC, 32, hv, bar_v);
-            v_pending = true;
-        };
-        if (tid == 0) {
-            issue_qkg(0, 0);
-            issue_v(0);
-        }
-        // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
-        {
-            const float* src = st_in + (size_t)L * DK + hh * 64;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float v[16];
-#pragma unroll
-                for (int e = 0; e < 16; e += 4) {
-                    const float4 f = __ldcs(reinterpret_cast<const float4*>(src + j * 16 + e));
-                    v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
-                }
-                tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
-            }
-            tmem_st_wait();
-        }
-
-        for (int c = 0; c < n_chunks; ++c) {
-            const int kb = c & 1;
-            const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
-            const uint8_t* rec0 = recb + (size_t)c * WC * REC_BYTES;
-            const bool has_next = c + 1 < n_chunks;
-            const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
-            const uint32_t sQ = sb + R_QK + kb * 32768;    // Q [64][128], then K [64][128] at +16384
-            const uint32_t sK = sQ + 16384;
-            const float* gamc = s_gam + kb * WC;
-            const float* tailc = s_tail + kb * WC;
-
-            // ---- phase A: this chunk's inputs and tile set landed; next chunk's Q, K and gates in flight
-            {
-                const bool ok_q = mbar_wait_bounded(bar_in + kb, (ph_in >> kb) & 1u, WY_WAIT_NS);
-                const bool ok_v = mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
-                if (ok_q) ph_in ^= 1u << kb;   // a phase that did not complete is still waited for at the exit
-                if (ok_v) ph_v ^= 1u;
-                if (tid == 0) {
-                    if (ok_q) in_pending &= ~(1u << kb);
-                    if (ok_v) v_pending = false;
-                }
-                if (!(ok_q && ok_v)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            }
-            if (c > 0) {
-                // the previous chunk's state update still reads the K buffer refilled below
-                if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                ph_s ^= 1u;
-                tc_fence_after();
-            }
+        if (warp < WY_THREADS / 32) {
+            // chunk 0's inputs
             if (tid == 0) {
-                if (!mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                else tb_pending = false;
-                ph_tb ^= 1u;
+                mbar_arrive_expect_tx(bar_tb, TILESET);
+                bulk_g2s(smem + R_TB, tiles, TILESET, bar_tb);
+                tb_pending = true;
             }
-            __syncthreads();
-            if (*s_abort) break;
-            // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
-            // state update, are complete)
-            if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
-            // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
-            // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
-            if (nv < WC) {
-                const int rows = WC - nv;
-                for (int idx = tid; idx < rows * 32; idx += WY_THREADS) {
-                    const int tile = idx / (rows * 16), rem = idx - tile * rows * 16;
-                    uint8_t* base = tile ? smem + R_V : smem + R_QK + kb * 32768 + 16384;
-                    *reinterpret_cast<uint4*>(base + (rem & 15) * 1024 + (nv + (rem >> 4)) * 16) = make_uint4(0, 0, 0, 0);
-                }
-            }
-            if (c == 0 && warp == 0) wy_scan_g4(s_g4, nv, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
-            wy_sync_for_mma();
-
-            // ---- phase B: U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major);
-            // they need only the chunk's own inputs and overlap the state split below
+            // Q, K and the gates of chunk cc into buffer b, V of chunk cc: TMA boxes of 64 token rows from the records
+            // (record chunks 0-15 Q, 16-31 K, 32-47 V, 64 the gates), landing token-major with rows 16 bytes apart
+            auto issue_qkg = [&](int cc, int b) {
+                mbar_arrive_expect_tx(bar_in + b, 2 * 16384 + WC * 16);
+                tma_load_4d(smem + R_QK + b * 32768, &tm_rec, 0, t0 + cc * WC, 0, hv, bar_in + b);
+                tma_load_4d(smem + R_QK + b * 32768 + 16384, &tm_rec, 0, t0 + cc * WC, 16, hv, bar_in + b);
+                tma_load_4d(smem + R_G + b * WC * 16, &tm_gate, 0, t0 + cc * WC, 64, hv, bar_in + b);
+                in_pending |= 1u << b;
+            };
+            auto issue_v = [&](int cc) {
+                mbar_arrive_expect_tx(bar_v, 16384);
+                tma_load_4d(smem + R_V, &tm_rec, 0, t0 + cc * WC, 32, hv, bar_v);
+                v_pending = true;
+            };
             if (tid == 0) {
-                const uint32_t id = umma_idesc_bf16(128, 64, true, false);
-                const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
-                }
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_W, dk + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
-                }
-                umma_commit(bar);
+                issue_qkg(0, 0);
+                issue_v(0);
             }
-            // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
+            // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
             {
-                const float g_last = gamc[WC - 1];
-                uint32_t sr[4][16];   // the thread's 64 state columns: four loads in flight, one wait
-#pragma unroll
-                for (int j = 0; j < 4; ++j) tmem_ld16_async(tmem + lane_base + TM_S + hh * 64 + j * 16, sr[j]);
-                tmem_ld_wait();
+                const float* src = st_in + (size_t)L * DK + hh * 64;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float sv[16];
+                    float v[16];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) sv[e] = __uint_as_float(sr[j][e]);
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        uint4 hi, lo;
-                        split8(sv + 8 * u, hi, lo);
-                        st_tile<128>(smem + R_X, L, hh * 8 + j * 2 + u, hi);
-                        st_tile<128>(smem + R_X + 32768, L, hh * 8 + j * 2 + u, lo);
+                    for (int e = 0; e < 16; e += 4) {
+                        const float4 f = __ldcs(reinterpret_cast<const float4*>(src + j * 16 + e));
+                        v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
                     }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) sv[e] *= g_last;
-                    tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
+                    tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
                 }
                 tmem_st_wait();
             }
-            wy_sync_for_mma();
-            // (Q S0^T)^T = S0 Q^T -> QS, off the critical path (read in H)
-            if (tid == 0) {
-                const uint32_t idq = umma_idesc_bf16(128, 64);
-                const uint64_t dq = tok_desc_k(sQ);
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t ds = umma_desc(sb + R_X + h * 32768, 128, 0);
-                    for (int ks = 0; ks < 8; ++ks)
-                        umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * TOK_KSTEP_K, idq, (h | ks) != 0);
-                }
-                umma_commit(bar_qs);
-            }
-            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            if (tid == 0 && has_next) issue_v(c + 1);   // V is free
 
-            // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
-            uint32_t wr[2][16];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_W + hh * 32 + j * 16, wr[j]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                float wv[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) wv[e] = -__uint_as_float(wr[j][e]);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    uint4 hi, lo;
-                    split8(wv + 8 * u, hi, lo);
-                    st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, hi);
-                    st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
-                }
-            }
-            wy_sync_for_mma();
-            if (tid == 0) {
-                const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
-                const uint32_t as0[3] = {R_X, R_X + 32768, R_X}, bw[3] = {R_TB, R_TB, R_TB + 16384};
-                constexpr uint64_t kmn = umma_kstep_mn(64);
-                for (int p = 0; p < 3; ++p) {
-                    const uint64_t da = umma_desc(sb + as0[p], 128, 0), db = umma_desc_mn(sb + bw[p], 64, 0);
-                    for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem + TM_U, da + ks * KSTEP_K, db + ks * kmn, idd, 1u);
-                }
-                umma_commit(bar);
-            }
-            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
-            // P tiles follow once P D has read R_P)
-            if (tid == 0 && has_next && !*s_abort) {
-                mbar_arrive_expect_tx(bar_tb, TILESET);
-                bulk_g2s(smem + R_TB, tiles + (size_t)(c + 1) * tile_step, R_P - R_TB, bar_tb);
-                tb_pending = true;
-            }
-            if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            for (int c = 0; c < n_chunks; ++c) {
+                const int kb = c & 1;
+                const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
+                const uint8_t* rec0 = recb + (size_t)c * WC * REC_BYTES;
+                const bool has_next = c + 1 < n_chunks;
+                const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
+                const float* gamc = s_gam + kb * WC;
+                const float* tailc = s_tail + kb * WC;
 
-            // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
-            uint32_t dr[2][16];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_U + hh * 32 + j * 16, dr[j]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                float dv[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) dv[e] = __uint_as_float(dr[j][e]);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    uint4 hi, lo;
-                    split8(dv + 8 * u, hi, lo);
-                    st_tile<64>(smem + R_X, L, hh * 4 + j * 2 + u, hi);
-                    st_tile<64>(smem + R_X + 16384, L, hh * 4 + j * 2 + u, lo);
+                // ---- phase A: this chunk's inputs and tile set landed; next chunk's Q, K and gates in flight
+                {
+                    const bool ok_q = mbar_wait_bounded(bar_in + kb, (ph_in >> kb) & 1u, WY_WAIT_NS);
+                    const bool ok_v = mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
+                    if (ok_q) ph_in ^= 1u << kb;   // a phase that did not complete is still waited for at the exit
+                    if (ok_v) ph_v ^= 1u;
+                    if (tid == 0) {
+                        if (ok_q) in_pending &= ~(1u << kb);
+                        if (ok_v) v_pending = false;
+                    }
+                    if (!(ok_q && ok_v)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 }
-#pragma unroll
-                for (int e = 0; e < 16; ++e) dv[e] *= tailc[hh * 32 + j * 16 + e];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    uint4 hi, lo;
-                    split8(dv + 8 * u, hi, lo);
-                    st_tile<64>(smem + R_X + 32768, L, hh * 4 + j * 2 + u, hi);
-                    st_tile<64>(smem + R_X + 49152, L, hh * 4 + j * 2 + u, lo);
+                if (c > 0) {
+                    // the previous chunk's state update still reads the K buffer refilled below
+                    if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                    ph_s ^= 1u;
+                    tc_fence_after();
                 }
-            }
-            wy_sync_for_mma();
-            // ---- phase G: (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (K read MN-major; waited
-            // when the state or the K buffer is next touched)
-            if (tid == 0) {
-                const uint32_t idp = umma_idesc_bf16(128, 64);
-                const uint32_t ad[3] = {R_X, R_X + 16384, R_X}, bp[3] = {R_P, R_P, R_P + 8192};
-                for (int p = 0; p < 3; ++p) {
-                    const uint64_t da = umma_desc(sb + ad[p], 64, 0), db = umma_desc(sb + bp[p], 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_PD, da + ks * KSTEP_K, db + ks * KSTEP_K, idp, (p | ks) != 0);
+                if (tid == 0) {
+                    if (!mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                    else tb_pending = false;
+                    ph_tb ^= 1u;
                 }
-                umma_commit(bar);
-                const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
-                const uint64_t dk = tok_desc_mn(sK);
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t dd = umma_desc(sb + R_X + 32768 + h * 16384, 64, 0);
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * TOK_KSTEP_MN, ids, 1u);
+                // (the issuing warp may raise the abort flag at any time: the decision is taken once, by barrier)
+                if (named_bar_or(1, WY_THREADS, *s_abort != 0)) break;
+                // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
+                // state update, are complete)
+                if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
+                // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
+                // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
+                if (nv < WC) {
+                    const int rows = WC - nv;
+                    for (int idx = tid; idx < rows * 32; idx += WY_THREADS) {
+                        const int tile = idx / (rows * 16), rem = idx - tile * rows * 16;
+                        uint8_t* base = tile ? smem + R_V : smem + R_QK + kb * 32768 + 16384;
+                        *reinterpret_cast<uint4*>(base + (rem & 15) * 1024 + (nv + (rem >> 4)) * 16) = make_uint4(0, 0, 0, 0);
+                    }
                 }
-                umma_commit(bar_s);
-            }
-            // silu(z) of the epilogue's row and quarter, loaded while the MMAs run
-            const int yt = tid >> 2, yq = tid & 3;
-            const bool valid = yt < nv;
-            uint4 zr[4];
+                if (c == 0 && warp == 0) wy_scan_g4(s_g4, nv, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
+                // ---- phase B (issuing warp): U^T = V^T (T beta)^T, W^T = K^T (T beta gamma)^T; they need only the
+                // chunk's own inputs and overlap the state split below
+                fence_async_shared();
+                tc_fence_before();
+                named_bar_sync(1, WY_THREADS);   // the decays and the cleared rows are visible to every compute thread
+                if (tid == 0) mbar_arrive(rdy);
+                // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
+                {
+                    const float g_last = gamc[WC - 1];
+                    uint32_t sr[4][16];   // the thread's 64 state columns: four loads in flight, one wait
 #pragma unroll
-            for (int i = 0; i < 4; ++i) zr[i] = make_uint4(0, 0, 0, 0);
-            if (valid) {
-                const uint8_t* zp = rec0 + (size_t)yt * REC_BYTES + 768 + yq * 64;
+                    for (int j = 0; j < 4; ++j) tmem_ld16_async(tmem + lane_base + TM_S + hh * 64 + j * 16, sr[j]);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 4; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
-            }
-            if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            // P (R_P) is read: the rest of the next chunk's tile set (its P tiles) streams in during the epilogue
-            if (tid == 0 && tb_pending && has_next)
-                bulk_g2s(smem + R_P, tiles + (size_t)(c + 1) * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
+                    for (int j = 0; j < 4; ++j) {
+                        float sv[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) sv[e] = __uint_as_float(sr[j][e]);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint4 hi, lo;
+                            split8(sv + 8 * u, hi, lo);
+                            st_tile<128>(smem + R_X, L, hh * 8 + j * 2 + u, hi);
+                            st_tile<128>(smem + R_X + 32768, L, hh * 8 + j * 2 + u, lo);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) sv[e] *= g_last;
+                        tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
+                    }
+                    tmem_st_wait();
+                }
+                // (Q S0^T)^T = S0 Q^T -> QS by the issuing warp, off the critical path (read in H)
+                ct_ready(rdy + 1, lane);
+                if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                if (tid == 0 && has_next) issue_v(c + 1);   // V is free
 
-            // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
-            // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
-            {
-                uint32_t qr[2][16], pr[2][16];
+                // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
+                uint32_t wr[2][16];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    tmem_ld16_async(tmem + lane_base + TM_QS + hh * 32 + j * 16, qr[j]);
-                    tmem_ld16_async(tmem + lane_base + TM_PD + hh * 32 + j * 16, pr[j]);
-                }
+                for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_W + hh * 32 + j * 16, wr[j]);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < 2; ++j) {
+                    float wv[16];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int t = hh * 32 + j * 16 + e;
-                        s_yt[t * LDY + L] = f2bf(gamc[t] * __uint_as_float(qr[j][e]) + __uint_as_float(pr[j][e]));
+                    for (int e = 0; e < 16; ++e) wv[e] = -__uint_as_float(wr[j][e]);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        uint4 hi, lo;
+                        split8(wv + 8 * u, hi, lo);
+                        st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, hi);
+                        st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
                     }
-            }
-            __syncthreads();
-            if (has_next && warp == 7) {
-                // the next chunk's decay scan, from its gate box (the same barrier phase is waited again in phase A)
-                if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
-                    atomicOr(a.err, ERR_TIMEOUT);
-                    *s_abort = 1;
                 }
-                wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
-                           s_tail + (kb ^ 1) * WC, lane);
-            }
-            {
-                const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
-                uint32_t yw[16];
+                ct_ready(rdy + 2, lane);   // D^T = U^T - S0 W^T onto U by the issuing warp
+                if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
+                // P tiles follow once P D has read R_P)
+                if (tid == 0 && has_next && !*s_abort) {
+                    mbar_arrive_expect_tx(bar_tb, TILESET);
+                    bulk_g2s(smem + R_TB, tiles + (size_t)(c + 1) * tile_step, R_P - R_TB, bar_tb);
+                    tb_pending = true;
+                }
+                if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+
+                // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
+                uint32_t dr[2][16];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 q = yr[i];
-                    yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
-                }
-                float ss = 0.f;
+                for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_U + hh * 32 + j * 16, dr[j]);
+                tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
-                    ss += y0 * y0 + y1 * y1;
+                for (int j = 0; j < 2; ++j) {
+                    float dv[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) dv[e] = __uint_as_float(dr[j][e]);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        uint4 hi, lo;
+                        split8(dv + 8 * u, hi, lo);
+                        st_tile<64>(smem + R_X, L, hh * 4 + j * 2 + u, hi);
+                        st_tile<64>(smem + R_X + 16384, L, hh * 4 + j * 2 + u, lo);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) dv[e] *= tailc[hh * 32 + j * 16 + e];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        uint4 hi, lo;
+                        split8(dv + 8 * u, hi, lo);
+                        st_tile<64>(smem + R_X + 32768, L, hh * 4 + j * 2 + u, hi);
+                        st_tile<64>(smem + R_X + 49152, L, hh * 4 + j * 2 + u, lo);
+                    }
                 }
-                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                // ---- phase G (issuing warp): (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (waited when
+                // the state or the K buffer is next touched)
+                ct_ready(rdy + 3, lane);
+                // silu(z) of the epilogue's row and quarter, loaded while the MMAs run
+                const int yt = tid >> 2, yq = tid & 3;
+                const bool valid = yt < nv;
+                uint4 zr[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) zr[i] = make_uint4(0, 0, 0, 0);
                 if (valid) {
-                    const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
-                    uint16_t* dst = a.out + (long long)(t0 + c * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
-                    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
-                    const float* nw = s_nw + yq * 32;
+                    const uint8_t* zp = rec0 + (size_t)yt * REC_BYTES + 768 + yq * 64;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
+                }
+                if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                // P (R_P) is read: the rest of the next chunk's tile set (its P tiles) streams in during the epilogue
+                if (tid == 0 && tb_pending && has_next)
+                    bulk_g2s(smem + R_P, tiles + (size_t)(c + 1) * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
+
+                // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
+                // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
+                {
+                    uint32_t qr[2][16], pr[2][16];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        tmem_ld16_async(tmem + lane_base + TM_QS + hh * 32 + j * 16, qr[j]);
+                        tmem_ld16_async(tmem + lane_base + TM_PD + hh * 32 + j * 16, pr[j]);
+                    }
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const int t = hh * 32 + j * 16 + e;
+                            s_yt[t * LDY + L] = f2bf(gamc[t] * __uint_as_float(qr[j][e]) + __uint_as_float(pr[j][e]));
+                        }
+                }
+                named_bar_sync(1, WY_THREADS);
+                if (has_next && warp == 7) {
+                    // the next chunk's decay scan, from its gate box (the same barrier phase is waited again in phase A)
+                    if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
+                        atomicOr(a.err, ERR_TIMEOUT);
+                        *s_abort = 1;
+                    }
+                    wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
+                               s_tail + (kb ^ 1) * WC, lane);
+                }
+                {
+                    const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
+                    uint32_t yw[16];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const uint32_t zw[4] = {zr[i].x, zr[i].y, zr[i].z, zr[i].w};
-                        uint32_t o[4];
+                        const uint4 q = yr[i];
+                        yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
+                    }
+                    float ss = 0.f;
 #pragma unroll
-                        for (int e2 = 0; e2 < 4; ++e2) {
-                            const int col = i * 8 + 2 * e2;
-                            const uint32_t yv = yw[col >> 1];
-                            const float yn0 = rbf(rbf(__uint_as_float(yv << 16) * nrm) * nw[col]);
-                            const float yn1 = rbf(rbf(__uint_as_float(yv & 0xFFFF0000u) * nrm) * nw[col + 1]);
-                            const float z0 = __uint_as_float(zw[e2] << 16), z1 = __uint_as_float(zw[e2] & 0xFFFF0000u);
-                            o[e2] = (uint32_t)f2bf(z0 * yn0) | ((uint32_t)f2bf(z1 * yn1) << 16);
-                        }
-                        if (vec) {
-                            *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
-                        } else {
+                    for (int i = 0; i < 16; ++i) {
+                        const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
+                        ss += y0 * y0 + y1 * y1;
+                    }
+                    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                    if (valid) {
+                        const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
+                        uint16_t* dst = a.out + (long long)(t0 + c * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
+                        const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+                        const float* nw = s_nw + yq * 32;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t zw[4] = {zr[i].x, zr[i].y, zr[i].z, zr[i].w};
+                            uint32_t o[4];
 #pragma unroll
                             for (int e2 = 0; e2 < 4; ++e2) {
-                                dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
-                                dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
+                                const int col = i * 8 + 2 * e2;
+                                const uint32_t yv = yw[col >> 1];
+                                const float yn0 = rbf(rbf(__uint_as_float(yv << 16) * nrm) * nw[col]);
+                                const float yn1 = rbf(rbf(__uint_as_float(yv & 0xFFFF0000u) * nrm) * nw[col + 1]);
+                                const float z0 = __uint_as_float(zw[e2] << 16), z1 = __uint_as_float(zw[e2] & 0xFFFF0000u);
+                                o[e2] = (uint32_t)f2bf(z0 * yn0) | ((uint32_t)f2bf(z1 * yn1) << 16);
+                            }
+                            if (vec) {
+                                *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+                            } else {
+#pragma unroll
+                                for (int e2 = 0; e2 < 4; ++e2) {
+                                    dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
+                                    dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
+                                }
                             }
                         }
                     }
                 }
+                tc_fence_before();
+                named_bar_sync(1, WY_THREADS);
+                tc_fence_after();
             }
-            tc_fence_before();
-            __syncthreads();
-            tc_fence_after();
-        }
-        if (n_chunks > 0 && !*s_abort) {
-            if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-            ph_s ^= 1u;
-            tc_fence_after();
-        }
+            if (n_chunks > 0 && !*s_abort) {
+                if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                ph_s ^= 1u;
+                tc_fence_after();
+            }
 
-        // ---- state back to the pool (row v, columns [64 half, +64))
-        {
-            float* dst = st + (size_t)L * DK + hh * 64;
+            // ---- state back to the pool (row v, columns [64 half, +64))
+            {
+                float* dst = st + (size_t)L * DK + hh * 64;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float v[16];
-                tmem_ld16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
+                for (int j = 0; j < 4; ++j) {
+                    float v[16];
+                    tmem_ld16(tmem + lane_base + TM_S + hh * 64 + j * 16, v);
 #pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    __stcs(reinterpret_cast<float4*>(dst + j * 16 + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
-            }
-        }
-        // ---- conv-state windows: the last K-1 rows of [old window; tokens]
-        {
-            uint16_t* cs = a.conv + (size_t)slot * (KC - 1) * a.D;
-            const int hk = hv / ratio;
-            for (int idx = tid; idx < DV + ((hv % ratio == 0) ? 2 * DK : 0); idx += WY_THREADS) {
-                const int ch = idx < DV ? 2 * a.hk * DK + hv * DV + idx
-                                        : ((idx - DV) < DK ? hk * DK + (idx - DV) : a.hk * DK + hk * DK + (idx - DV - DK));
-                uint16_t w[KC - 1];
-#pragma unroll
-                for (int j = 0; j < KC - 1; ++j) {
-                    const int p = T + j;
-                    w[j] = p < KC - 1 ? cs[(size_t)p * a.D + ch] : a.qkv[(long long)(t0 + p - (KC - 1)) * a.ld_qkv + ch];
+                    for (int e = 0; e < 16; e += 4)
+                        __stcs(reinterpret_cast<float4*>(dst + j * 16 + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
                 }
+            }
+            // ---- conv-state windows: the last K-1 rows of [old window; tokens]
+            {
+                uint16_t* cs = a.conv + (size_t)slot * (KC - 1) * a.D;
+                const int hk = hv / ratio;
+                for (int idx = tid; idx < DV + ((hv % ratio == 0) ? 2 * DK : 0); idx += WY_THREADS) {
+                    const int ch = idx < DV ? 2 * a.hk * DK + hv * DV + idx
+                                            : ((idx - DV) < DK ? hk * DK + (idx - DV) : a.hk * DK + hk * DK + (idx - DV - DK));
+                    uint16_t w[KC - 1];
 #pragma unroll
-                for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = w[j];
+                    for (int j = 0; j < KC - 1; ++j) {
+                        const int p = T + j;
+                        w[j] = p < KC - 1 ? cs[(size_t)p * a.D + ch] : a.qkv[(long long)(t0 + p - (KC - 1)) * a.ld_qkv + ch];
+                    }
+#pragma unroll
+                    for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = w[j];
+                }
+            }
+        } else {
+            // ---- the issuing warp: each MMA batch once the compute warps report its operands written
+            auto ready = [&](int i) -> bool {
+                const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(rdy + i, (ph_rdy >> i) & 1u, WY_WAIT_NS));
+                if (ok) ph_rdy ^= 1u << i;
+                else if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                tc_fence_after();
+                return ok;
+            };
+            for (int c = 0; c < n_chunks; ++c) {
+                const uint32_t sQ = sb + R_QK + (c & 1) * 32768;    // Q [64][128], then K [64][128] at +16384
+                const uint32_t sK = sQ + 16384;
+                // U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major)
+                if (!ready(0)) break;
+                if (elect_one()) {
+                    const uint32_t id = umma_idesc_bf16(128, 64, true, false);
+                    const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
+                        for (int ks = 0; ks < 4; ++ks)
+                            umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                    }
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
+                        for (int ks = 0; ks < 4; ++ks)
+                            umma_bf16(tmem + TM_W, dk + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                    }
+                    umma_commit(bar);
+                }
+                __syncwarp();
+                // (Q S0^T)^T = S0 Q^T -> QS
+                if (!ready(1)) break;
+                if (elect_one()) {
+                    const uint32_t idq = umma_idesc_bf16(128, 64);
+                    const uint64_t dq = tok_desc_k(sQ);
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t ds = umma_desc(sb + R_X + h * 32768, 128, 0);
+                        for (int ks = 0; ks < 8; ++ks)
+                            umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * TOK_KSTEP_K, idq, (h | ks) != 0);
+                    }
+                    umma_commit(bar_qs);
+                }
+                __syncwarp();
+                // D^T = U^T - S0 W^T onto U (S0 and -W^T as hi/lo pairs, lo x lo dropped)
+                if (!ready(2)) break;
+                if (elect_one()) {
+                    const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
+                    const uint32_t as0[3] = {R_X, R_X + 32768, R_X}, bw[3] = {R_TB, R_TB, R_TB + 16384};
+                    constexpr uint64_t kmn = umma_kstep_mn(64);
+                    for (int p = 0; p < 3; ++p) {
+                        const uint64_t da = umma_desc(sb + as0[p], 128, 0), db = umma_desc_mn(sb + bw[p], 64, 0);
+                        for (int ks = 0; ks < 8; ++ks)
+                            umma_bf16(tmem + TM_U, da + ks * KSTEP_K, db + ks * kmn, idd, 1u);
+                    }
+                    umma_commit(bar);
+                }
+                __syncwarp();
+                // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major)
+                if (!ready(3)) break;
+                if (elect_one()) {
+                    const uint32_t idp = umma_idesc_bf16(128, 64);
+                    const uint32_t ad[3] = {R_X, R_X + 16384, R_X}, bp[3] = {R_P, R_P, R_P + 8192};
+                    for (int p = 0; p < 3; ++p) {
+                        const uint64_t da = umma_desc(sb + ad[p], 64, 0), db = umma_desc(sb + bp[p], 64, 0);
+                        for (int ks = 0; ks < 4; ++ks)
+                            umma_bf16(tmem + TM_PD, da + ks * KSTEP_K, db + ks * KSTEP_K, idp, (p | ks) != 0);
+                    }
+                    umma_commit(bar);
+                    const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
+                    const uint64_t dk = tok_desc_mn(sK);
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t dd = umma_desc(sb + R_X + 32768 + h * 16384, 64, 0);
+                        for (int ks = 0; ks < 4; ++ks)
+                            umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * TOK_KSTEP_MN, ids, 1u);
+                    }
+                    umma_commit(bar_s);
+                }
+                __syncwarp();
             }
         }
         tc_fence_before();
@@ -971,6 +1014,11 @@ __global__ void __launch_bounds__(WY_THREADS, 1) gdn_wy_kernel(const RecurArgs a
         tc_fence_after();
     }
 
+    if (warp == WY_THREADS / 32) {   // no MMA of the issuing warp is in flight when the CTA ends
+        if (elect_one()) umma_commit(bar_fin);
+        __syncwarp();
+        mbar_wait_bounded(bar_fin, 0, WY_WAIT_NS);
+    }
     if (tid == 0) {   // no copy lands after the CTA ends (only after a wait gave up can one be outstanding)
         if (tb_pending) mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS);
         for (int b = 0; b < 2; ++b)
@@ -1024,7 +1072,7 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
         !tmap_records(&tm_gate, r.recs, r.n_tokens, r.rec_cap, r.hv, REC_BYTES, WC, 1))
         return cudaErrorNotSupported;
     c.gridDim = dim3((unsigned)(n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev]), 1, 1);
-    c.blockDim = dim3(WY_THREADS, 1, 1);
+    c.blockDim = dim3(WY_BLOCK, 1, 1);
     c.dynamicSmemBytes = WY_SMEM;
     return cudaLaunchKernelEx(&c, gdn_wy_kernel, r, tm_rec, tm_gate);
 }
