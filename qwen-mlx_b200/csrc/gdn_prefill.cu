@@ -42,15 +42,16 @@
 // product, and U, W, D, Q S0^T and P D are formed transposed (U^T = V^T (T beta)^T,
 // W^T = K^T (T beta gamma)^T, D^T = U^T - S0 W^T, (Q S0^T)^T = S0 Q^T, (P D)^T = D^T P^T).
 //
-// Shared memory of gdn_wy_kernel (bytes); bf16 tiles in the layout of gdn_umma.cuh:
-//   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity)
-//   R_V   16K  V [64 s][128 v]
-//   R_X   64K  S0 hi, lo [128 v][128 d]  -> D^T hi, D^T lo, Dd^T hi, Dd^T lo [128 v][64 s]
+// Shared memory of gdn_wy_kernel (bytes):
+//   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity), token-major TMA boxes
+//   R_V   16K  V [64 s][128 v], token-major TMA box
+//   R_Z   32K  silu(z) [64 t][128 v] x 2 (chunk parity), token-major TMA boxes for the epilogue
 //   R_T   17K  y [64 t][128 v] bf16 (row stride LDY), the epilogue's transpose
 //   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] (bulk copy) -> -W^T hi, -W^T lo [128 d][64 t]
 //   R_P   16K  (P (.) QK) hi, lo [64 t][64 s] (same bulk copy)
 // TMEM (cta_group::1, all 128 lanes): S [0,128) = state [v][d]; U [192,256) = U^T then D^T;
-// W [256,320) = W^T; QS [320,384) = (Q S0^T)^T; PD [384,448) = (P D)^T.
+// W [256,320) = W^T; QS [320,384) = (Q S0^T)^T; PD [384,448) = (P D)^T; the hi/lo A operands of Q S0^T, D,
+// P D and the state update (S0, then D^T and Dd^T) in [128,192) and [448,512).
 #include "gdn_device.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
@@ -62,10 +63,11 @@ constexpr int WC = 64;                 // tokens per chunk
 constexpr int WY_THREADS = 256;       // compute threads of the sequential pass (and of the chunk pass)
 constexpr int WY_BLOCK = WY_THREADS + 32;   // the sequential pass adds one MMA-issuing warp
 constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
-constexpr int R_QK = 0, R_V = 65536, R_X = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
+constexpr int R_QK = 0, R_V = 65536, R_Z = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
               R_P = 204800, R_SMALL = 221184;
 static_assert(R_N + 6 * 256 * 4 <= R_TB, "prefill shared memory layout");
 static_assert(R_P == R_TB + 32768, "the chunk tile set lands in one bulk copy");
+static_assert(R_Z + 2 * 16384 <= R_T, "two silu(z) boxes");
 constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
 static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
 constexpr int SMALL_FLOATS = 3 * 2 * 64 + 128;
@@ -73,6 +75,10 @@ constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 160 + 1023) / 1024) * 1024;  
 constexpr int WY_SMEM = R_G + 2 * WC * 16;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
 constexpr uint32_t TM_S = 0, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
+// A operands of the sequential pass in tensor memory (row v = lane, two bf16 per column): S0 hi [128, 192) and lo
+// [448, 512) from the state split until Q S0^T and D have read them, then D hi [128, 160), D lo [160, 192),
+// Dd hi [448, 480), Dd lo [480, 512)
+constexpr uint32_t TM_AH = 128, TM_AL = 448;
 constexpr uint64_t WY_WAIT_NS = 2000000000ull;
 constexpr uint32_t TILESET = WY_TILESET_BYTES;   // T beta hi, lo | T beta gamma hi, lo | P (.) QK hi, lo
 static_assert(TILESET == 6 * 8192, "tile set layout");
@@ -520,6 +526,18 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
 
 // ------------------------------------------------------------------ sequential pass
 
+// bf16x2 helpers of the epilogue: (lo, hi) rounded to one bf16x2 word; a bf16x2 product rounded once.
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;\n" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
 __device__ __forceinline__ void ct_ready(uint64_t* rdy, int lane) {
     fence_async_shared();
@@ -543,7 +561,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     float* s_lg = reinterpret_cast<float*>(smem + R_SMALL);       // [2][64] cumulative, log2 units
     float* s_gam = s_lg + 2 * WC;                                 // [2][64] exp(lg_t)
     float* s_tail = s_gam + 2 * WC;                               // [2][64] exp(lg_last - lg_t)
-    float* s_nw = s_tail + 2 * WC;                                // norm_w [128]
+    float* s_nw = s_tail + 2 * WC;                                // 128 floats of room; holds norm_w as bf16 pairs
+    uint32_t* s_nw2 = reinterpret_cast<uint32_t*>(s_nw);          // [64] norm_w (2c, 2c+1) as a bf16x2 word
     uint64_t* bar = reinterpret_cast<uint64_t*>(s_nw + DV);       // MMA batches waited in order
     uint64_t* bar_qs = bar + 1;                                   // (Q S0^T)^T, issued early
     uint64_t* bar_s = bar + 2;                                    // state update, waited when S is next used
@@ -552,7 +571,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
     uint64_t* rdy = bar + 7;       // [4] operands of an MMA batch written: U/W, QS, D, P D + state update
     uint64_t* bar_fin = bar + 11;  // every MMA of the issuing warp complete (kernel exit)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+    uint64_t* bar_z = bar + 12;    // [2] silu(z) box of the chunk of that parity
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
@@ -574,10 +594,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         mbar_init(rdy, 1);               // thread 0, after a barrier of the compute warps
         for (int i = 1; i < 4; ++i) mbar_init(rdy + i, WY_THREADS / 32);   // one arrival per compute warp
         mbar_init(bar_fin, 1);
+        mbar_init(bar_z, 1);
+        mbar_init(bar_z + 1, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
-    for (int i = tid; i < DV; i += WY_THREADS) s_nw[i] = bf2f(a.norm_w[i]);
+    for (int i = tid; i < DV / 2; i += WY_THREADS)
+        s_nw2[i] = (uint32_t)a.norm_w[2 * i] | ((uint32_t)a.norm_w[2 * i + 1] << 16);
     if (warp == 0) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
@@ -589,6 +612,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
     bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
     uint32_t in_pending = 0;   // (thread 0) bit b: a bar_in[b] load issued and not yet waited for
+    uint32_t ph_z = 0;         // bit b: the phase of bar_z[b] to wait for next
+    uint32_t z_pending = 0;    // (thread 0) bit b: a bar_z[b] load issued and not yet waited for
     bool v_pending = false;    // (thread 0) the same for bar_v
     pdl_wait();
 
@@ -611,7 +636,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         if (!wy_qualifies(a, seq, t0, T, slot)) continue;
         float* st = a.rec + ((size_t)slot * a.hv + hv) * (DV * DK);
         const float* st_in = (a.rec_in ? a.rec_in : a.rec) + ((size_t)slot * a.hv + hv) * (DV * DK);
-        const uint8_t* recb = a.recs + ((long long)hv * a.rec_cap + t0) * REC_BYTES;
         const uint8_t* tiles = a.wy_tiles + ((size_t)__ldg(a.wy_cb + seq) * a.hv + hv) * TILESET;
         const size_t tile_step = (size_t)a.hv * TILESET;   // next chunk of the same head
         const int n_chunks = (T + WC - 1) / WC;
@@ -657,10 +681,75 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tmem_st_wait();
             }
 
+            // the per-token epilogue of chunk cc: gated RMSNorm of its y rows (transposed in s_yt), times silu(z),
+            // stored.  It feeds nothing in the chain, so a chunk's epilogue runs during the next chunk's wait for D:
+            // s_yt is rewritten only in that chunk's phase H, after P D, which needs every warp's phase F.
+            const int yt = tid >> 2, yq = tid & 3;
+            int pend_c = -1, pend_nv = 0;
+            auto epilogue = [&](int cc, int nvv) {
+                // silu(z) of this thread's row and quarter, from the chunk's z box (feature f of token t at
+                // (f / 8) * 1024 + t * 16)
+                const int zb = cc & 1;
+                if (!mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS)) {
+                    atomicOr(a.err, ERR_TIMEOUT);
+                    *s_abort = 1;
+                } else {
+                    ph_z ^= 1u << zb;
+                    if (tid == 0) z_pending &= ~(1u << zb);
+                }
+                uint4 z[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    z[i] = *reinterpret_cast<const uint4*>(smem + R_Z + zb * 16384 + (yq * 4 + i) * 1024 + yt * 16);
+                const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
+                uint32_t yw[16];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 q = yr[i];
+                    yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
+                }
+                float ss = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
+                    ss += y0 * y0 + y1 * y1;
+                }
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                if (yt < nvv) {
+                    const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
+                    uint16_t* dst = a.out + (long long)(t0 + cc * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
+                    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+                    const uint32_t* nw2 = s_nw2 + yq * 16;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t zw[4] = {z[i].x, z[i].y, z[i].z, z[i].w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            // bf16(bf16(bf16(y * nrm) * w) * z), two columns at once: the products of two bf16
+                            // values are exact in f32, so one bf16x2 multiply rounds exactly as f32 then bf16 does
+                            const uint32_t yv = yw[i * 4 + e2];
+                            const uint32_t yn = bf2_pack(__uint_as_float(yv << 16) * nrm,
+                                                         __uint_as_float(yv & 0xFFFF0000u) * nrm);
+                            o[e2] = bf2_mul(zw[e2], bf2_mul(yn, nw2[i * 4 + e2]));
+                        }
+                        if (vec) {
+                            *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+                        } else {
+#pragma unroll
+                            for (int e2 = 0; e2 < 4; ++e2) {
+                                dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
+                                dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
+                            }
+                        }
+                    }
+                }
+            };
+
             for (int c = 0; c < n_chunks; ++c) {
                 const int kb = c & 1;
                 const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
-                const uint8_t* rec0 = recb + (size_t)c * WC * REC_BYTES;
                 const bool has_next = c + 1 < n_chunks;
                 const int nv1 = has_next ? ((T - (c + 1) * WC) < WC ? (T - (c + 1) * WC) : WC) : 0;
                 const float* gamc = s_gam + kb * WC;
@@ -694,6 +783,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
                 // state update, are complete)
                 if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
+                // this chunk's silu(z) box for its epilogue (which runs during the next chunk); the buffer's previous
+                // chunk had its epilogue before the last barrier
+                if (tid == 0) {
+                    mbar_arrive_expect_tx(bar_z + kb, 16384);
+                    tma_load_4d(smem + R_Z + kb * 16384, &tm_rec, 0, t0 + c * WC, 48, hv, bar_z + kb);
+                    z_pending |= 1u << kb;
+                }
                 // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
                 // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
                 if (nv < WC) {
@@ -723,13 +819,11 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         float sv[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) sv[e] = __uint_as_float(sr[j][e]);
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            uint4 hi, lo;
-                            split8(sv + 8 * u, hi, lo);
-                            st_tile<128>(smem + R_X, L, hh * 8 + j * 2 + u, hi);
-                            st_tile<128>(smem + R_X + 32768, L, hh * 8 + j * 2 + u, lo);
-                        }
+                        uint4 hi0, lo0, hi1, lo1;
+                        split8(sv, hi0, lo0);
+                        split8(sv + 8, hi1, lo1);
+                        tmem_st8(tmem + lane_base + TM_AH + hh * 32 + j * 8, hi0, hi1);
+                        tmem_st8(tmem + lane_base + TM_AL + hh * 32 + j * 8, lo0, lo1);
 #pragma unroll
                         for (int e = 0; e < 16; ++e) sv[e] *= g_last;
                         tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
@@ -760,6 +854,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                 }
                 ct_ready(rdy + 2, lane);   // D^T = U^T - S0 W^T onto U by the issuing warp
+                if (pend_c >= 0) {   // the previous chunk's epilogue while D runs
+                    epilogue(pend_c, pend_nv);
+                    pend_c = -1;
+                }
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
                 // P tiles follow once P D has read R_P)
@@ -780,37 +878,27 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     float dv[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) dv[e] = __uint_as_float(dr[j][e]);
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        uint4 hi, lo;
-                        split8(dv + 8 * u, hi, lo);
-                        st_tile<64>(smem + R_X, L, hh * 4 + j * 2 + u, hi);
-                        st_tile<64>(smem + R_X + 16384, L, hh * 4 + j * 2 + u, lo);
+                    {
+                        uint4 hi0, lo0, hi1, lo1;
+                        split8(dv, hi0, lo0);
+                        split8(dv + 8, hi1, lo1);
+                        tmem_st8(tmem + lane_base + TM_AH + hh * 16 + j * 8, hi0, hi1);
+                        tmem_st8(tmem + lane_base + TM_AH + 32 + hh * 16 + j * 8, lo0, lo1);
                     }
 #pragma unroll
                     for (int e = 0; e < 16; ++e) dv[e] *= tailc[hh * 32 + j * 16 + e];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        uint4 hi, lo;
-                        split8(dv + 8 * u, hi, lo);
-                        st_tile<64>(smem + R_X + 32768, L, hh * 4 + j * 2 + u, hi);
-                        st_tile<64>(smem + R_X + 49152, L, hh * 4 + j * 2 + u, lo);
+                    {
+                        uint4 hi0, lo0, hi1, lo1;
+                        split8(dv, hi0, lo0);
+                        split8(dv + 8, hi1, lo1);
+                        tmem_st8(tmem + lane_base + TM_AL + hh * 16 + j * 8, hi0, hi1);
+                        tmem_st8(tmem + lane_base + TM_AL + 32 + hh * 16 + j * 8, lo0, lo1);
                     }
                 }
                 // ---- phase G (issuing warp): (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (waited when
                 // the state or the K buffer is next touched)
+                tmem_st_wait();
                 ct_ready(rdy + 3, lane);
-                // silu(z) of the epilogue's row and quarter, loaded while the MMAs run
-                const int yt = tid >> 2, yq = tid & 3;
-                const bool valid = yt < nv;
-                uint4 zr[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) zr[i] = make_uint4(0, 0, 0, 0);
-                if (valid) {
-                    const uint8_t* zp = rec0 + (size_t)yt * REC_BYTES + 768 + yq * 64;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) zr[i] = *reinterpret_cast<const uint4*>(zp + 16 * i);
-                }
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 // P (R_P) is read: the rest of the next chunk's tile set (its P tiles) streams in during the epilogue
                 if (tid == 0 && tb_pending && has_next)
@@ -844,51 +932,11 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
                                s_tail + (kb ^ 1) * WC, lane);
                 }
-                {
-                    const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
-                    uint32_t yw[16];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint4 q = yr[i];
-                        yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
-                    }
-                    float ss = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
-                        ss += y0 * y0 + y1 * y1;
-                    }
-                    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-                    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-                    if (valid) {
-                        const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
-                        uint16_t* dst = a.out + (long long)(t0 + c * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
-                        const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
-                        const float* nw = s_nw + yq * 32;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t zw[4] = {zr[i].x, zr[i].y, zr[i].z, zr[i].w};
-                            uint32_t o[4];
-#pragma unroll
-                            for (int e2 = 0; e2 < 4; ++e2) {
-                                const int col = i * 8 + 2 * e2;
-                                const uint32_t yv = yw[col >> 1];
-                                const float yn0 = rbf(rbf(__uint_as_float(yv << 16) * nrm) * nw[col]);
-                                const float yn1 = rbf(rbf(__uint_as_float(yv & 0xFFFF0000u) * nrm) * nw[col + 1]);
-                                const float z0 = __uint_as_float(zw[e2] << 16), z1 = __uint_as_float(zw[e2] & 0xFFFF0000u);
-                                o[e2] = (uint32_t)f2bf(z0 * yn0) | ((uint32_t)f2bf(z1 * yn1) << 16);
-                            }
-                            if (vec) {
-                                *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
-                            } else {
-#pragma unroll
-                                for (int e2 = 0; e2 < 4; ++e2) {
-                                    dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
-                                    dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
-                                }
-                            }
-                        }
-                    }
+                if (has_next) {   // this chunk's epilogue runs while the next chunk waits for D
+                    pend_c = c;
+                    pend_nv = nv;
+                } else {
+                    epilogue(c, nv);
                 }
                 tc_fence_before();
                 named_bar_sync(1, WY_THREADS);
@@ -964,11 +1012,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (elect_one()) {
                     const uint32_t idq = umma_idesc_bf16(128, 64);
                     const uint64_t dq = tok_desc_k(sQ);
-                    for (int h = 0; h < 2; ++h) {
-                        const uint64_t ds = umma_desc(sb + R_X + h * 32768, 128, 0);
+                    for (int h = 0; h < 2; ++h)
                         for (int ks = 0; ks < 8; ++ks)
-                            umma_bf16(tmem + TM_QS, ds + ks * KSTEP_K, dq + ks * TOK_KSTEP_K, idq, (h | ks) != 0);
-                    }
+                            umma_bf16_ta(tmem + TM_QS, tmem + (h ? TM_AL : TM_AH) + ks * 8, dq + ks * TOK_KSTEP_K, idq,
+                                         (h | ks) != 0);
                     umma_commit(bar_qs);
                 }
                 __syncwarp();
@@ -976,12 +1023,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (!ready(2)) break;
                 if (elect_one()) {
                     const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
-                    const uint32_t as0[3] = {R_X, R_X + 32768, R_X}, bw[3] = {R_TB, R_TB, R_TB + 16384};
+                    const uint32_t as0[3] = {TM_AH, TM_AL, TM_AH}, bw[3] = {R_TB, R_TB, R_TB + 16384};
                     constexpr uint64_t kmn = umma_kstep_mn(64);
                     for (int p = 0; p < 3; ++p) {
-                        const uint64_t da = umma_desc(sb + as0[p], 128, 0), db = umma_desc_mn(sb + bw[p], 64, 0);
+                        const uint64_t db = umma_desc_mn(sb + bw[p], 64, 0);
                         for (int ks = 0; ks < 8; ++ks)
-                            umma_bf16(tmem + TM_U, da + ks * KSTEP_K, db + ks * kmn, idd, 1u);
+                            umma_bf16_ta(tmem + TM_U, tmem + as0[p] + ks * 8, db + ks * kmn, idd, 1u);
                     }
                     umma_commit(bar);
                 }
@@ -990,20 +1037,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (!ready(3)) break;
                 if (elect_one()) {
                     const uint32_t idp = umma_idesc_bf16(128, 64);
-                    const uint32_t ad[3] = {R_X, R_X + 16384, R_X}, bp[3] = {R_P, R_P, R_P + 8192};
+                    const uint32_t ad[3] = {TM_AH, TM_AH + 32, TM_AH}, bp[3] = {R_P, R_P, R_P + 8192};
                     for (int p = 0; p < 3; ++p) {
-                        const uint64_t da = umma_desc(sb + ad[p], 64, 0), db = umma_desc(sb + bp[p], 64, 0);
+                        const uint64_t db = umma_desc(sb + bp[p], 64, 0);
                         for (int ks = 0; ks < 4; ++ks)
-                            umma_bf16(tmem + TM_PD, da + ks * KSTEP_K, db + ks * KSTEP_K, idp, (p | ks) != 0);
+                            umma_bf16_ta(tmem + TM_PD, tmem + ad[p] + ks * 8, db + ks * KSTEP_K, idp, (p | ks) != 0);
                     }
                     umma_commit(bar);
                     const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
                     const uint64_t dk = tok_desc_mn(sK);
-                    for (int h = 0; h < 2; ++h) {
-                        const uint64_t dd = umma_desc(sb + R_X + 32768 + h * 16384, 64, 0);
+                    for (int h = 0; h < 2; ++h)
                         for (int ks = 0; ks < 4; ++ks)
-                            umma_bf16(tmem + TM_S, dd + ks * KSTEP_K, dk + ks * TOK_KSTEP_MN, ids, 1u);
-                    }
+                            umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);
                     umma_commit(bar_s);
                 }
                 __syncwarp();
@@ -1024,6 +1069,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         for (int b = 0; b < 2; ++b)
             if ((in_pending >> b) & 1u) mbar_wait_bounded(bar_in + b, (ph_in >> b) & 1u, WY_WAIT_NS);
         if (v_pending) mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
+        for (int b = 0; b < 2; ++b)
+            if ((z_pending >> b) & 1u) mbar_wait_bounded(bar_z + b, (ph_z >> b) & 1u, WY_WAIT_NS);
     }
     tc_fence_before();
     __syncthreads();

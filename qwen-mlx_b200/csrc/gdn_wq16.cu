@@ -78,19 +78,6 @@ __device__ __forceinline__ uint32_t q16_bf16x2_fma(uint32_t a, uint32_t b, uint3
     return d;
 }
 
-// D (TMEM) (+)= A (TMEM, K-major) * B (smem)^T: one k-step issued by a single thread.
-__device__ __forceinline__ void umma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-    asm volatile(
-        "{\n"
-        " .reg .pred p;\n"
-        " setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
-        "}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 // 32 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
