@@ -61,7 +61,10 @@ namespace gdn {
 
 constexpr int WC = 64;                 // tokens per chunk
 constexpr int WY_THREADS = 256;       // compute threads of the sequential pass (and of the chunk pass)
-constexpr int WY_BLOCK = WY_THREADS + 32;   // the sequential pass adds one MMA-issuing warp
+constexpr int WY_ISSUER_WARP = WY_THREADS / 32;        // the sequential pass: warp 8 issues the MMAs,
+constexpr int WY_EPI_WARP = WY_ISSUER_WARP + 1;         // warps 9 and 10 run the per-token epilogue
+constexpr int WY_EPI_THREADS = 64;
+constexpr int WY_BLOCK = WY_THREADS + 32 + WY_EPI_THREADS;
 constexpr int LDT = 68;                // padded f32 row stride of M / T (conflict-free float4 rows)
 constexpr int R_QK = 0, R_V = 65536, R_Z = 81920, R_T = 147456, R_N = R_T + WC * LDT * 4, R_TB = 172032,
               R_P = 204800, R_SMALL = 221184;
@@ -71,7 +74,7 @@ static_assert(R_Z + 2 * 16384 <= R_T, "two silu(z) boxes");
 constexpr int LDY = DV + 8;            // padded bf16 row stride of the y transpose (rows 272 B apart)
 static_assert(WC * LDY * 2 <= WC * LDT * 4, "y transpose fits the T region");
 constexpr int SMALL_FLOATS = 3 * 2 * 64 + 128;
-constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 160 + 1023) / 1024) * 1024;   // gate boxes [2][64 t][16 B]
+constexpr int R_G = ((R_SMALL + SMALL_FLOATS * 4 + 192 + 1023) / 1024) * 1024;   // gate boxes [2][64 t][16 B]
 constexpr int WY_SMEM = R_G + 2 * WC * 16;
 static_assert(WY_SMEM <= 232448, "prefill shared memory budget");
 constexpr uint32_t TM_S = 0, TM_U = 192, TM_W = 256, TM_QS = 320, TM_PD = 384;
@@ -572,7 +575,9 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* rdy = bar + 7;       // [4] operands of an MMA batch written: U/W, QS, D, P D + state update
     uint64_t* bar_fin = bar + 11;  // every MMA of the issuing warp complete (kernel exit)
     uint64_t* bar_z = bar + 12;    // [2] silu(z) box of the chunk of that parity
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+    uint64_t* epi_full = bar + 14;  // a chunk's y is transposed into s_yt (thread 0 of the compute warps)
+    uint64_t* epi_free = bar + 15;  // the epilogue warps are done with s_yt and the chunk's z box
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
@@ -596,6 +601,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         mbar_init(bar_fin, 1);
         mbar_init(bar_z, 1);
         mbar_init(bar_z + 1, 1);
+        mbar_init(epi_full, 1);
+        mbar_init(epi_free, WY_EPI_THREADS / 32);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -612,8 +619,9 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
     bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
     uint32_t in_pending = 0;   // (thread 0) bit b: a bar_in[b] load issued and not yet waited for
-    uint32_t ph_z = 0;         // bit b: the phase of bar_z[b] to wait for next
-    uint32_t z_pending = 0;    // (thread 0) bit b: a bar_z[b] load issued and not yet waited for
+    uint32_t ph_z = 0;         // (epilogue warps) bit b: the phase of bar_z[b] to wait for next
+    uint32_t z_any = 0, z_next = 0;   // (thread 0) bit b: a z box was issued into buffer b / parity of the next
+    uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
     bool v_pending = false;    // (thread 0) the same for bar_v
     pdl_wait();
 
@@ -681,72 +689,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tmem_st_wait();
             }
 
-            // the per-token epilogue of chunk cc: gated RMSNorm of its y rows (transposed in s_yt), times silu(z),
-            // stored.  It feeds nothing in the chain, so a chunk's epilogue runs during the next chunk's wait for D:
-            // s_yt is rewritten only in that chunk's phase H, after P D, which needs every warp's phase F.
-            const int yt = tid >> 2, yq = tid & 3;
-            int pend_c = -1, pend_nv = 0;
-            auto epilogue = [&](int cc, int nvv) {
-                // silu(z) of this thread's row and quarter, from the chunk's z box (feature f of token t at
-                // (f / 8) * 1024 + t * 16)
-                const int zb = cc & 1;
-                if (!mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS)) {
-                    atomicOr(a.err, ERR_TIMEOUT);
-                    *s_abort = 1;
-                } else {
-                    ph_z ^= 1u << zb;
-                    if (tid == 0) z_pending &= ~(1u << zb);
-                }
-                uint4 z[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    z[i] = *reinterpret_cast<const uint4*>(smem + R_Z + zb * 16384 + (yq * 4 + i) * 1024 + yt * 16);
-                const uint4* yr = reinterpret_cast<const uint4*>(s_yt + yt * LDY + yq * 32);
-                uint32_t yw[16];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 q = yr[i];
-                    yw[4 * i] = q.x; yw[4 * i + 1] = q.y; yw[4 * i + 2] = q.z; yw[4 * i + 3] = q.w;
-                }
-                float ss = 0.f;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float y0 = __uint_as_float(yw[i] << 16), y1 = __uint_as_float(yw[i] & 0xFFFF0000u);
-                    ss += y0 * y0 + y1 * y1;
-                }
-                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-                if (yt < nvv) {
-                    const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
-                    uint16_t* dst = a.out + (long long)(t0 + cc * WC + yt) * a.ld_out + (long long)hv * DV + yq * 32;
-                    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
-                    const uint32_t* nw2 = s_nw2 + yq * 16;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t zw[4] = {z[i].x, z[i].y, z[i].z, z[i].w};
-                        uint32_t o[4];
-#pragma unroll
-                        for (int e2 = 0; e2 < 4; ++e2) {
-                            // bf16(bf16(bf16(y * nrm) * w) * z), two columns at once: the products of two bf16
-                            // values are exact in f32, so one bf16x2 multiply rounds exactly as f32 then bf16 does
-                            const uint32_t yv = yw[i * 4 + e2];
-                            const uint32_t yn = bf2_pack(__uint_as_float(yv << 16) * nrm,
-                                                         __uint_as_float(yv & 0xFFFF0000u) * nrm);
-                            o[e2] = bf2_mul(zw[e2], bf2_mul(yn, nw2[i * 4 + e2]));
-                        }
-                        if (vec) {
-                            *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
-                        } else {
-#pragma unroll
-                            for (int e2 = 0; e2 < 4; ++e2) {
-                                dst[i * 8 + 2 * e2] = (uint16_t)(o[e2] & 0xFFFFu);
-                                dst[i * 8 + 2 * e2 + 1] = (uint16_t)(o[e2] >> 16);
-                            }
-                        }
-                    }
-                }
-            };
-
             for (int c = 0; c < n_chunks; ++c) {
                 const int kb = c & 1;
                 const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
@@ -783,12 +725,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
                 // state update, are complete)
                 if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
-                // this chunk's silu(z) box for its epilogue (which runs during the next chunk); the buffer's previous
-                // chunk had its epilogue before the last barrier
+                // this chunk's silu(z) box for the epilogue warps (which take the chunk during the next one); the
+                // buffer's previous chunk was released (epi_free) before the previous chunk's y was written
                 if (tid == 0) {
                     mbar_arrive_expect_tx(bar_z + kb, 16384);
                     tma_load_4d(smem + R_Z + kb * 16384, &tm_rec, 0, t0 + c * WC, 48, hv, bar_z + kb);
-                    z_pending |= 1u << kb;
+                    z_any |= 1u << kb;
+                    z_next ^= 1u << kb;
                 }
                 // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
                 // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
@@ -854,10 +797,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                 }
                 ct_ready(rdy + 2, lane);   // D^T = U^T - S0 W^T onto U by the issuing warp
-                if (pend_c >= 0) {   // the previous chunk's epilogue while D runs
-                    epilogue(pend_c, pend_nv);
-                    pend_c = -1;
-                }
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
                 // P tiles follow once P D has read R_P)
@@ -904,8 +843,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (tid == 0 && tb_pending && has_next)
                     bulk_g2s(smem + R_P, tiles + (size_t)(c + 1) * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
 
-                // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem;
-                // then per token: gated RMSNorm over the 128 v of its row (4 threads per row)
+                // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
+                // the epilogue warps (gated RMSNorm per token), once they are done with the previous chunk's y
+                if (n_yt > 0 && !mbar_wait_bounded(epi_free, (n_yt - 1) & 1u, WY_WAIT_NS)) {
+                    atomicOr(a.err, ERR_TIMEOUT);
+                    *s_abort = 1;
+                }
                 {
                     uint32_t qr[2][16], pr[2][16];
 #pragma unroll
@@ -923,6 +866,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         }
                 }
                 named_bar_sync(1, WY_THREADS);
+                if (tid == 0) mbar_arrive(epi_full);
+                ++n_yt;
                 if (has_next && warp == 7) {
                     // the next chunk's decay scan, from its gate box (the same barrier phase is waited again in phase A)
                     if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
@@ -931,12 +876,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                     wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
                                s_tail + (kb ^ 1) * WC, lane);
-                }
-                if (has_next) {   // this chunk's epilogue runs while the next chunk waits for D
-                    pend_c = c;
-                    pend_nv = nv;
-                } else {
-                    epilogue(c, nv);
                 }
                 tc_fence_before();
                 named_bar_sync(1, WY_THREADS);
@@ -977,7 +916,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     for (int j = 0; j < KC - 1; ++j) cs[(size_t)j * a.D + ch] = w[j];
                 }
             }
-        } else {
+        } else if (warp == WY_ISSUER_WARP) {
             // ---- the issuing warp: each MMA batch once the compute warps report its operands written
             auto ready = [&](int i) -> bool {
                 const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(rdy + i, (ph_rdy >> i) & 1u, WY_WAIT_NS));
@@ -1053,13 +992,83 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 __syncwarp();
             }
+        } else {
+            // ---- the epilogue warps: each chunk once its y is in s_yt (and its z box landed): per token, gated
+            // RMSNorm over the 128 v of the row times silu(z), stored; one token row per thread.  The sum of
+            // squares adds four quarter sums as the compute warps' epilogue did (same bits).
+            const int et = tid - WY_EPI_WARP * 32;   // token row of the chunk
+            for (int c = 0; c < n_chunks; ++c) {
+                const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
+                const int zb = c & 1;
+                const bool ok = mbar_wait_bounded(epi_full, n_yt & 1u, WY_WAIT_NS) &&
+                                mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS);
+                if (!ok) {
+                    if (lane == 0) {
+                        atomicOr(a.err, ERR_TIMEOUT);
+                        *s_abort = 1;
+                    }
+                    break;
+                }
+                ph_z ^= 1u << zb;
+                ++n_yt;
+                if (et < nv) {
+                    const uint4* yr = reinterpret_cast<const uint4*>(s_yt + et * LDY);
+                    float part[4];
+#pragma unroll
+                    for (int qd = 0; qd < 4; ++qd) {
+                        float ss = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint4 q = yr[qd * 4 + i];
+                            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float y0 = __uint_as_float(w4[e] << 16), y1 = __uint_as_float(w4[e] & 0xFFFF0000u);
+                                ss += y0 * y0 + y1 * y1;
+                            }
+                        }
+                        part[qd] = ss;
+                    }
+                    const float ss = (part[0] + part[1]) + (part[2] + part[3]);
+                    const float nrm = 1.0f / sqrtf(ss / (float)DV + a.eps);
+                    uint16_t* dst = a.out + (long long)(t0 + c * WC + et) * a.ld_out + (long long)hv * DV;
+                    const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+                    const uint8_t* zrow = smem + R_Z + zb * 16384 + et * 16;   // feature chunk i at i * 1024
+#pragma unroll 4
+                    for (int i = 0; i < 16; ++i) {   // columns v = 8 i .. 8 i + 7
+                        const uint4 q = yr[i];
+                        const uint4 zz = *reinterpret_cast<const uint4*>(zrow + i * 1024);
+                        const uint32_t yw[4] = {q.x, q.y, q.z, q.w}, zw[4] = {zz.x, zz.y, zz.z, zz.w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            // bf16(bf16(bf16(y * nrm) * w) * z), two columns at once: the product of two bf16 values
+                            // is exact in f32, so one bf16x2 multiply rounds exactly as f32 then bf16 does
+                            const uint32_t yn = bf2_pack(__uint_as_float(yw[e] << 16) * nrm,
+                                                         __uint_as_float(yw[e] & 0xFFFF0000u) * nrm);
+                            o[e] = bf2_mul(zw[e], bf2_mul(yn, s_nw2[i * 4 + e]));
+                        }
+                        if (vec) {
+                            *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                dst[i * 8 + 2 * e] = (uint16_t)(o[e] & 0xFFFFu);
+                                dst[i * 8 + 2 * e + 1] = (uint16_t)(o[e] >> 16);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_free);
+            }
         }
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
     }
 
-    if (warp == WY_THREADS / 32) {   // no MMA of the issuing warp is in flight when the CTA ends
+    if (warp == WY_ISSUER_WARP) {   // no MMA of the issuing warp is in flight when the CTA ends
         if (elect_one()) umma_commit(bar_fin);
         __syncwarp();
         mbar_wait_bounded(bar_fin, 0, WY_WAIT_NS);
@@ -1069,8 +1078,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         for (int b = 0; b < 2; ++b)
             if ((in_pending >> b) & 1u) mbar_wait_bounded(bar_in + b, (ph_in >> b) & 1u, WY_WAIT_NS);
         if (v_pending) mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
-        for (int b = 0; b < 2; ++b)
-            if ((z_pending >> b) & 1u) mbar_wait_bounded(bar_z + b, (ph_z >> b) & 1u, WY_WAIT_NS);
+        for (int b = 0; b < 2; ++b)   // the last z box of each buffer has landed (a no-op when it was consumed)
+            if ((z_any >> b) & 1u) mbar_wait_bounded(bar_z + b, ((z_next >> b) & 1u) ^ 1u, WY_WAIT_NS);
     }
     tc_fence_before();
     __syncthreads();
