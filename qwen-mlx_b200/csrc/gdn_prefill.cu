@@ -617,12 +617,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0, ph_v = 0;
     uint32_t ph_in = 0;        // bit b: the phase of bar_in[b] to wait for next
     uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
-    bool tb_pending = false;   // (thread 0) a tile-set copy issued and not yet waited for
-    uint32_t in_pending = 0;   // (thread 0) bit b: a bar_in[b] load issued and not yet waited for
+    uint32_t nb = 0;           // (issuing warp) completions of bar before the current chunk
+    // copies of the chunk inputs, issued by the MMA-issuing warp (bar_in[0], bar_in[1], bar_v, bar_tb: bits 0-3) and the
+    // z boxes by the epilogue warps (bar_z[0], bar_z[1]: bits 4-5): a phase issued on that barrier / the parity of the
+    // next issue, for the bounded drain at the exit
+    uint32_t cp_any = 0, cp_next = 0;
     uint32_t ph_z = 0;         // (epilogue warps) bit b: the phase of bar_z[b] to wait for next
-    uint32_t z_any = 0, z_next = 0;   // (thread 0) bit b: a z box was issued into buffer b / parity of the next
     uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
-    bool v_pending = false;    // (thread 0) the same for bar_v
     pdl_wait();
 
     const int total = __ldg(a.wy_plan);
@@ -648,31 +649,41 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         const size_t tile_step = (size_t)a.hv * TILESET;   // next chunk of the same head
         const int n_chunks = (T + WC - 1) / WC;
 
+        // Copies of a chunk's inputs (one thread issues each; the compute warps wait for them).  Q, K and the gates
+        // of chunk cc into buffer b and V: TMA boxes of 64 token rows from the records (record chunks 0-15 Q, 16-31
+        // K, 32-47 V, 48-63 silu(z), 64 the gates), landing token-major with rows 16 bytes apart.  The tile set of
+        // chunk cc (T beta, T beta gamma | P (.) QK) by two bulk copies on one barrier phase.
+        auto note_copy = [&](int bit) {
+            cp_any |= 1u << bit;
+            cp_next ^= 1u << bit;
+        };
+        auto issue_qkg = [&](int cc, int b) {
+            mbar_arrive_expect_tx(bar_in + b, 2 * 16384 + WC * 16);
+            tma_load_4d(smem + R_QK + b * 32768, &tm_rec, 0, t0 + cc * WC, 0, hv, bar_in + b);
+            tma_load_4d(smem + R_QK + b * 32768 + 16384, &tm_rec, 0, t0 + cc * WC, 16, hv, bar_in + b);
+            tma_load_4d(smem + R_G + b * WC * 16, &tm_gate, 0, t0 + cc * WC, 64, hv, bar_in + b);
+            note_copy(b);
+        };
+        auto issue_v = [&](int cc) {
+            mbar_arrive_expect_tx(bar_v, 16384);
+            tma_load_4d(smem + R_V, &tm_rec, 0, t0 + cc * WC, 32, hv, bar_v);
+            note_copy(2);
+        };
+        auto issue_tiles_tb = [&](int cc) {   // T beta / T beta gamma: R_TB must be free
+            mbar_arrive_expect_tx(bar_tb, TILESET);
+            bulk_g2s(smem + R_TB, tiles + (size_t)cc * tile_step, R_P - R_TB, bar_tb);
+            note_copy(3);
+        };
+        auto issue_tiles_p = [&](int cc) {    // P (.) QK: R_P must be free
+            bulk_g2s(smem + R_P, tiles + (size_t)cc * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
+        };
+        auto issue_z = [&](int cc) {          // silu(z) of chunk cc into buffer cc & 1
+            mbar_arrive_expect_tx(bar_z + (cc & 1), 16384);
+            tma_load_4d(smem + R_Z + (cc & 1) * 16384, &tm_rec, 0, t0 + cc * WC, 48, hv, bar_z + (cc & 1));
+            note_copy(4 + (cc & 1));
+        };
+
         if (warp < WY_THREADS / 32) {
-            // chunk 0's inputs
-            if (tid == 0) {
-                mbar_arrive_expect_tx(bar_tb, TILESET);
-                bulk_g2s(smem + R_TB, tiles, TILESET, bar_tb);
-                tb_pending = true;
-            }
-            // Q, K and the gates of chunk cc into buffer b, V of chunk cc: TMA boxes of 64 token rows from the records
-            // (record chunks 0-15 Q, 16-31 K, 32-47 V, 64 the gates), landing token-major with rows 16 bytes apart
-            auto issue_qkg = [&](int cc, int b) {
-                mbar_arrive_expect_tx(bar_in + b, 2 * 16384 + WC * 16);
-                tma_load_4d(smem + R_QK + b * 32768, &tm_rec, 0, t0 + cc * WC, 0, hv, bar_in + b);
-                tma_load_4d(smem + R_QK + b * 32768 + 16384, &tm_rec, 0, t0 + cc * WC, 16, hv, bar_in + b);
-                tma_load_4d(smem + R_G + b * WC * 16, &tm_gate, 0, t0 + cc * WC, 64, hv, bar_in + b);
-                in_pending |= 1u << b;
-            };
-            auto issue_v = [&](int cc) {
-                mbar_arrive_expect_tx(bar_v, 16384);
-                tma_load_4d(smem + R_V, &tm_rec, 0, t0 + cc * WC, 32, hv, bar_v);
-                v_pending = true;
-            };
-            if (tid == 0) {
-                issue_qkg(0, 0);
-                issue_v(0);
-            }
             // ---- state -> TMEM S (thread (v, half) owns row v, columns [64 half, 64 half + 64))
             {
                 const float* src = st_in + (size_t)L * DK + hh * 64;
@@ -703,10 +714,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     const bool ok_v = mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
                     if (ok_q) ph_in ^= 1u << kb;   // a phase that did not complete is still waited for at the exit
                     if (ok_v) ph_v ^= 1u;
-                    if (tid == 0) {
-                        if (ok_q) in_pending &= ~(1u << kb);
-                        if (ok_v) v_pending = false;
-                    }
                     if (!(ok_q && ok_v)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 }
                 if (c > 0) {
@@ -717,22 +724,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 if (tid == 0) {
                     if (!mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                    else tb_pending = false;
                     ph_tb ^= 1u;
                 }
                 // (the issuing warp may raise the abort flag at any time: the decision is taken once, by barrier)
                 if (named_bar_or(1, WY_THREADS, *s_abort != 0)) break;
-                // the next chunk's Q, K and gates into the other buffer (its last readers, the previous chunk's QS and
-                // state update, are complete)
-                if (tid == 0 && has_next) issue_qkg(c + 1, kb ^ 1);
-                // this chunk's silu(z) box for the epilogue warps (which take the chunk during the next one); the
-                // buffer's previous chunk was released (epi_free) before the previous chunk's y was written
-                if (tid == 0) {
-                    mbar_arrive_expect_tx(bar_z + kb, 16384);
-                    tma_load_4d(smem + R_Z + kb * 16384, &tm_rec, 0, t0 + c * WC, 48, hv, bar_z + kb);
-                    z_any |= 1u << kb;
-                    z_next ^= 1u << kb;
-                }
                 // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
                 // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
                 if (nv < WC) {
@@ -776,7 +771,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 // (Q S0^T)^T = S0 Q^T -> QS by the issuing warp, off the critical path (read in H)
                 ct_ready(rdy + 1, lane);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                if (tid == 0 && has_next) issue_v(c + 1);   // V is free
 
                 // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
                 uint32_t wr[2][16];
@@ -798,13 +792,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 ct_ready(rdy + 2, lane);   // D^T = U^T - S0 W^T onto U by the issuing warp
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                // -W^T (R_TB) is read: the next chunk's T beta / T beta gamma tiles stream in from here on (its
-                // P tiles follow once P D has read R_P)
-                if (tid == 0 && has_next && !*s_abort) {
-                    mbar_arrive_expect_tx(bar_tb, TILESET);
-                    bulk_g2s(smem + R_TB, tiles + (size_t)(c + 1) * tile_step, R_P - R_TB, bar_tb);
-                    tb_pending = true;
-                }
                 if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase F: D^T and Dd^T = D^T diag(exp(lg_last - lg_s)) as hi/lo tiles [v][s]
@@ -839,9 +826,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tmem_st_wait();
                 ct_ready(rdy + 3, lane);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                // P (R_P) is read: the rest of the next chunk's tile set (its P tiles) streams in during the epilogue
-                if (tid == 0 && tb_pending && has_next)
-                    bulk_g2s(smem + R_P, tiles + (size_t)(c + 1) * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
 
                 // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
                 // the epilogue warps (gated RMSNorm per token), once they are done with the previous chunk's y
@@ -925,11 +909,37 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tc_fence_after();
                 return ok;
             };
+            // the item's first chunk inputs (every buffer's last reader, in the previous item, is complete)
+            if (elect_one()) {
+                issue_tiles_tb(0);
+                issue_tiles_p(0);
+                issue_qkg(0, 0);
+                issue_v(0);
+            }
+            __syncwarp();
+            bool done = true;
             for (int c = 0; c < n_chunks; ++c) {
                 const uint32_t sQ = sb + R_QK + (c & 1) * 32768;    // Q [64][128], then K [64][128] at +16384
                 const uint32_t sK = sQ + 16384;
+                const bool has_next = c + 1 < n_chunks;
+                if (c > 0) {
+                    // the previous chunk's state update, and so its P D, is complete: its K buffer and R_P are free
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS));
+                    if (!ok) {
+                        if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                        done = false;
+                        break;
+                    }
+                    ph_s ^= 1u;
+                    if (elect_one()) issue_tiles_p(c);
+                    __syncwarp();
+                }
+                if (has_next) {
+                    if (elect_one()) issue_qkg(c + 1, (c + 1) & 1);
+                    __syncwarp();
+                }
                 // U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major)
-                if (!ready(0)) break;
+                if (!ready(0)) { done = false; break; }
                 if (elect_one()) {
                     const uint32_t id = umma_idesc_bf16(128, 64, true, false);
                     const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
@@ -947,7 +957,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 __syncwarp();
                 // (Q S0^T)^T = S0 Q^T -> QS
-                if (!ready(1)) break;
+                if (!ready(1)) { done = false; break; }
                 if (elect_one()) {
                     const uint32_t idq = umma_idesc_bf16(128, 64);
                     const uint64_t dq = tok_desc_k(sQ);
@@ -958,8 +968,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     umma_commit(bar_qs);
                 }
                 __syncwarp();
+                if (has_next) {   // U has read V: the next chunk's V streams in
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, nb & 1u, WY_WAIT_NS));
+                    if (!ok) {
+                        if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                        done = false;
+                        break;
+                    }
+                    if (elect_one()) issue_v(c + 1);
+                    __syncwarp();
+                }
                 // D^T = U^T - S0 W^T onto U (S0 and -W^T as hi/lo pairs, lo x lo dropped)
-                if (!ready(2)) break;
+                if (!ready(2)) { done = false; break; }
                 if (elect_one()) {
                     const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
                     const uint32_t as0[3] = {TM_AH, TM_AL, TM_AH}, bw[3] = {R_TB, R_TB, R_TB + 16384};
@@ -973,7 +993,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 __syncwarp();
                 // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major)
-                if (!ready(3)) break;
+                if (!ready(3)) { done = false; break; }
                 if (elect_one()) {
                     const uint32_t idp = umma_idesc_bf16(128, 64);
                     const uint32_t ad[3] = {TM_AH, TM_AH + 32, TM_AH}, bp[3] = {R_P, R_P, R_P + 8192};
@@ -989,21 +1009,33 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);
                     umma_commit(bar_s);
+                    // D has read -W^T (the compute warps waited for it before reporting phase F): the next chunk's
+                    // T beta / T beta gamma tiles stream into R_TB
+                    if (has_next) issue_tiles_tb(c + 1);
                 }
                 __syncwarp();
+                nb += 3;   // U/W, D and P D completed on bar this chunk
             }
+            if (done && n_chunks > 0) ph_s ^= 1u;   // the last state update is waited for by the compute warps only
         } else {
             // ---- the epilogue warps: each chunk once its y is in s_yt (and its z box landed): per token, gated
             // RMSNorm over the 128 v of the row times silu(z), stored; one token row per thread.  The sum of
             // squares adds four quarter sums as the compute warps' epilogue did (same bits).
             const int et = tid - WY_EPI_WARP * 32;   // token row of the chunk
+            if (warp == WY_EPI_WARP) {   // the first two chunks' silu(z) boxes (both buffers are free)
+                if (elect_one()) {
+                    issue_z(0);
+                    if (n_chunks > 1) issue_z(1);
+                }
+                __syncwarp();
+            }
             for (int c = 0; c < n_chunks; ++c) {
                 const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
                 const int zb = c & 1;
                 const bool ok = mbar_wait_bounded(epi_full, n_yt & 1u, WY_WAIT_NS) &&
                                 mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS);
-                if (!ok) {
-                    if (lane == 0) {
+                if (named_bar_or(2, WY_EPI_THREADS, !ok)) {   // one decision for both epilogue warps
+                    if (et == 0) {
                         atomicOr(a.err, ERR_TIMEOUT);
                         *s_abort = 1;
                     }
@@ -1061,6 +1093,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(epi_free);
+                // both epilogue warps are done with chunk c's z box: chunk c + 2's streams into it
+                named_bar_sync(2, WY_EPI_THREADS);
+                if (warp == WY_EPI_WARP && c + 2 < n_chunks) {
+                    if (elect_one()) issue_z(c + 2);
+                    __syncwarp();
+                }
             }
         }
         tc_fence_before();
@@ -1073,14 +1111,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         __syncwarp();
         mbar_wait_bounded(bar_fin, 0, WY_WAIT_NS);
     }
-    if (tid == 0) {   // no copy lands after the CTA ends (only after a wait gave up can one be outstanding)
-        if (tb_pending) mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS);
-        for (int b = 0; b < 2; ++b)
-            if ((in_pending >> b) & 1u) mbar_wait_bounded(bar_in + b, (ph_in >> b) & 1u, WY_WAIT_NS);
-        if (v_pending) mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
-        for (int b = 0; b < 2; ++b)   // the last z box of each buffer has landed (a no-op when it was consumed)
-            if ((z_any >> b) & 1u) mbar_wait_bounded(bar_z + b, ((z_next >> b) & 1u) ^ 1u, WY_WAIT_NS);
-    }
+    // no copy lands after the CTA ends: each issuing thread waits (bounded) for the last phase it issued on each
+    // barrier, which has long completed unless a wait gave up
+    for (int bit = 0; bit < 6; ++bit)
+        if ((cp_any >> bit) & 1u) {
+            uint64_t* b = bit < 2 ? bar_in + bit : bit == 2 ? bar_v : bit == 3 ? bar_tb : bar_z + (bit - 4);
+            mbar_wait_bounded(b, ((cp_next >> bit) & 1u) ^ 1u, WY_WAIT_NS);
+        }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
