@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* bar = reinterpret_cast<uint64_t*>(s_nw + DV);       // MMA batches waited in order
     uint64_t* bar_qs = bar + 1;                                   // (Q S0^T)^T, issued early
     uint64_t* bar_s = bar + 2;                                    // state update, waited when S is next used
-    uint64_t* bar_tb = bar + 3;                                   // the chunk's tile set (bulk copy)
+    uint64_t* bar_tb = bar + 3;   // the chunk's T beta / T beta gamma tiles (bulk copy; U and W wait for them)
     uint64_t* bar_in = bar + 4;                                   // [2] Q, K and gates of the chunk of that parity
     uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
     uint64_t* rdy = bar + 7;       // [4] operands of an MMA batch written: U/W, QS, D, P D + state update
@@ -577,7 +577,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* bar_z = bar + 12;    // [2] silu(z) box of the chunk of that parity
     uint64_t* epi_full = bar + 14;  // a chunk's y is transposed into s_yt (thread 0 of the compute warps)
     uint64_t* epi_free = bar + 15;  // the epilogue warps are done with s_yt and the chunk's z box
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+    uint64_t* bar_tp = bar + 16;    // the chunk's P (.) QK tiles (bulk copy; only P D waits for them)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 17);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* s_ticket = s_abort + 1;
     uint16_t* s_yt = reinterpret_cast<uint16_t*>(smem + R_T);    // y [64 t][LDY] bf16, the epilogue's transpose
@@ -602,6 +603,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         mbar_init(bar_z, 1);
         mbar_init(bar_z + 1, 1);
         mbar_init(epi_full, 1);
+        mbar_init(bar_tp, 1);
         mbar_init(epi_free, WY_EPI_THREADS / 32);
         *s_abort = 0;
         fence_mbar_init();
@@ -618,9 +620,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t ph_in = 0;        // bit b: the phase of bar_in[b] to wait for next
     uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
     uint32_t nb = 0;           // (issuing warp) completions of bar before the current chunk
-    // copies of the chunk inputs, issued by the MMA-issuing warp (bar_in[0], bar_in[1], bar_v, bar_tb: bits 0-3) and the
-    // z boxes by the epilogue warps (bar_z[0], bar_z[1]: bits 4-5): a phase issued on that barrier / the parity of the
-    // next issue, for the bounded drain at the exit
+    uint32_t ph_tp = 0;        // (issuing warp) the phase of bar_tp to wait for next
+    // copies of the chunk inputs, issued by the MMA-issuing warp (bar_in[0], bar_in[1], bar_v, bar_tb: bits 0-3;
+    // bar_tp: bit 6) and the z boxes by the epilogue warps (bar_z[0], bar_z[1]: bits 4-5): a phase issued on that
+    // barrier / the parity of the next issue, for the bounded drain at the exit
     uint32_t cp_any = 0, cp_next = 0;
     uint32_t ph_z = 0;         // (epilogue warps) bit b: the phase of bar_z[b] to wait for next
     uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
@@ -670,12 +673,14 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
             note_copy(2);
         };
         auto issue_tiles_tb = [&](int cc) {   // T beta / T beta gamma: R_TB must be free
-            mbar_arrive_expect_tx(bar_tb, TILESET);
+            mbar_arrive_expect_tx(bar_tb, R_P - R_TB);
             bulk_g2s(smem + R_TB, tiles + (size_t)cc * tile_step, R_P - R_TB, bar_tb);
             note_copy(3);
         };
         auto issue_tiles_p = [&](int cc) {    // P (.) QK: R_P must be free
-            bulk_g2s(smem + R_P, tiles + (size_t)cc * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tb);
+            mbar_arrive_expect_tx(bar_tp, TILESET - (R_P - R_TB));
+            bulk_g2s(smem + R_P, tiles + (size_t)cc * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tp);
+            note_copy(6);
         };
         auto issue_z = [&](int cc) {          // silu(z) of chunk cc into buffer cc & 1
             mbar_arrive_expect_tx(bar_z + (cc & 1), 16384);
@@ -992,8 +997,14 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     umma_commit(bar);
                 }
                 __syncwarp();
-                // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major)
+                // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major); the P tiles landed
                 if (!ready(3)) { done = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_tp, ph_tp, WY_WAIT_NS))) {
+                    if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                    done = false;
+                    break;
+                }
+                ph_tp ^= 1u;
                 if (elect_one()) {
                     const uint32_t idp = umma_idesc_bf16(128, 64);
                     const uint32_t ad[3] = {TM_AH, TM_AH + 32, TM_AH}, bp[3] = {R_P, R_P, R_P + 8192};
@@ -1113,9 +1124,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     }
     // no copy lands after the CTA ends: each issuing thread waits (bounded) for the last phase it issued on each
     // barrier, which has long completed unless a wait gave up
-    for (int bit = 0; bit < 6; ++bit)
+    for (int bit = 0; bit < 7; ++bit)
         if ((cp_any >> bit) & 1u) {
-            uint64_t* b = bit < 2 ? bar_in + bit : bit == 2 ? bar_v : bit == 3 ? bar_tb : bar_z + (bit - 4);
+            uint64_t* b = bit < 2    ? bar_in + bit
+                          : bit == 2 ? bar_v
+                          : bit == 3 ? bar_tb
+                          : bit == 6 ? bar_tp
+                                     : bar_z + (bit - 4);
             mbar_wait_bounded(b, ((cp_next >> bit) & 1u) ^ 1u, WY_WAIT_NS);
         }
     tc_fence_before();
