@@ -542,11 +542,16 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
 }
 
 // A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
-__device__ __forceinline__ void ct_ready(uint64_t* rdy, int lane) {
+// Batch i of a chunk's MMAs (0: U/W, 1: Q S0^T, 2: D, 3: P D + state update) may go: the compute threads' shared-
+// and tensor-memory writes for it are done.  A hardware named barrier of the 256 compute threads (arriving without
+// waiting) and the issuing warp (waiting): it wakes the issuer within tens of cycles, where an mbarrier poll took
+// hundreds.  Every compute thread arrives on each of the four once per chunk, and on batch 0's before leaving a
+// chunk loop early, so the issuer never waits on one that does not come.
+constexpr int WY_RDY_BAR = 3;   // named barriers 3..6 (1: compute warps, 2: epilogue warps)
+__device__ __forceinline__ void ct_ready(int i) {
     fence_async_shared();
     tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(rdy);
+    named_bar_arrive(WY_RDY_BAR + i, WY_THREADS + 32);
 }
 
 // Q, K and V tiles of the sequential pass arrive by TMA token-major: element (t, f) of a [64 t][128 f] tile at
@@ -572,7 +577,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* bar_tb = bar + 3;   // the chunk's T beta / T beta gamma tiles (bulk copy; U and W wait for them)
     uint64_t* bar_in = bar + 4;                                   // [2] Q, K and gates of the chunk of that parity
     uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
-    uint64_t* rdy = bar + 7;       // [4] operands of an MMA batch written: U/W, QS, D, P D + state update
+    // bar + 7 .. bar + 10: unused
     uint64_t* bar_fin = bar + 11;  // every MMA of the issuing warp complete (kernel exit)
     uint64_t* bar_z = bar + 12;    // [2] silu(z) box of the chunk of that parity
     uint64_t* epi_full = bar + 14;  // a chunk's y is transposed into s_yt (thread 0 of the compute warps)
@@ -597,8 +602,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         mbar_init(bar_in, 1);
         mbar_init(bar_in + 1, 1);
         mbar_init(bar_v, 1);
-        mbar_init(rdy, 1);               // thread 0, after a barrier of the compute warps
-        for (int i = 1; i < 4; ++i) mbar_init(rdy + i, WY_THREADS / 32);   // one arrival per compute warp
         mbar_init(bar_fin, 1);
         mbar_init(bar_z, 1);
         mbar_init(bar_z + 1, 1);
@@ -618,7 +621,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     uint32_t ph = 0, ph_qs = 0, ph_s = 0, ph_tb = 0, ph_v = 0;
     uint32_t ph_in = 0;        // bit b: the phase of bar_in[b] to wait for next
-    uint32_t ph_rdy = 0;       // (issuing warp) bit i: the phase of rdy[i] to wait for next
     uint32_t nb = 0;           // (issuing warp) completions of bar before the current chunk
     uint32_t ph_tp = 0;        // (issuing warp) the phase of bar_tp to wait for next
     // copies of the chunk inputs, issued by the MMA-issuing warp (bar_in[0], bar_in[1], bar_v, bar_tb: bits 0-3;
@@ -732,7 +734,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     ph_tb ^= 1u;
                 }
                 // (the issuing warp may raise the abort flag at any time: the decision is taken once, by barrier)
-                if (named_bar_or(1, WY_THREADS, *s_abort != 0)) break;
+                if (named_bar_or(1, WY_THREADS, *s_abort != 0)) {
+                    named_bar_arrive(WY_RDY_BAR, WY_THREADS + 32);   // the issuer waits for batch 0, then stops
+                    break;
+                }
                 // a chunk that ends its sequence: the rows past the end hold the next sequence's tokens (or zeros);
                 // K and V rows there are cleared so only exact zeros meet the zero rows of T beta and T beta gamma
                 if (nv < WC) {
@@ -749,7 +754,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 fence_async_shared();
                 tc_fence_before();
                 named_bar_sync(1, WY_THREADS);   // the decays and the cleared rows are visible to every compute thread
-                if (tid == 0) mbar_arrive(rdy);
+                named_bar_arrive(WY_RDY_BAR, WY_THREADS + 32);
                 // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
                 {
                     const float g_last = gamc[WC - 1];
@@ -774,7 +779,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     tmem_st_wait();
                 }
                 // (Q S0^T)^T = S0 Q^T -> QS by the issuing warp, off the critical path (read in H)
-                ct_ready(rdy + 1, lane);
+                ct_ready(1);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
@@ -795,7 +800,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
                     }
                 }
-                ct_ready(rdy + 2, lane);   // D^T = U^T - S0 W^T onto U by the issuing warp
+                ct_ready(2);   // D^T = U^T - S0 W^T onto U by the issuing warp
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
@@ -829,7 +834,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 // ---- phase G (issuing warp): (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (waited when
                 // the state or the K buffer is next touched)
                 tmem_st_wait();
-                ct_ready(rdy + 3, lane);
+                ct_ready(3);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
@@ -907,12 +912,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
             }
         } else if (warp == WY_ISSUER_WARP) {
             // ---- the issuing warp: each MMA batch once the compute warps report its operands written
-            auto ready = [&](int i) -> bool {
-                const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(rdy + i, (ph_rdy >> i) & 1u, WY_WAIT_NS));
-                if (ok) ph_rdy ^= 1u << i;
-                else if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+            auto ready = [&](int i) -> bool {   // batch i's operands are written (false: the compute warps stopped)
+                named_bar_sync(WY_RDY_BAR + i, WY_THREADS + 32);
                 tc_fence_after();
-                return ok;
+                return i != 0 || *s_abort == 0;
             };
             // the item's first chunk inputs (every buffer's last reader, in the previous item, is complete)
             if (elect_one()) {

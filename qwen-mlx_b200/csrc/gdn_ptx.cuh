@@ -134,6 +134,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("barrier.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrive on named barrier `id` (of `nthreads` threads) without waiting: the producer side of a producer /
+// consumer barrier whose consumers use named_bar_sync with the same count.  Release semantics for this thread.
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+    asm volatile("barrier.arrive %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Named barrier `id` over `nthreads` threads that also ORs `pred` over them: every thread
 // gets the same answer, so a decision taken on it is uniform (non-.aligned form).
 __device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
