@@ -715,23 +715,22 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 const float* gamc = s_gam + kb * WC;
                 const float* tailc = s_tail + kb * WC;
 
-                // ---- phase A: this chunk's inputs and tile set landed; next chunk's Q, K and gates in flight
-                {
+                // ---- phase A: the previous state update is complete.  The chunk's inputs are read only by the MMAs,
+                // and the issuing warp waits for them; the compute warps wait only where they touch them: to clear
+                // the rows past a sequence's end and for the first chunk's decay scan (one completion per chunk on
+                // each barrier, so the phase bits advance either way)
+                if (nv < WC || c == 0) {
                     const bool ok_q = mbar_wait_bounded(bar_in + kb, (ph_in >> kb) & 1u, WY_WAIT_NS);
                     const bool ok_v = mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS);
-                    if (ok_q) ph_in ^= 1u << kb;   // a phase that did not complete is still waited for at the exit
-                    if (ok_v) ph_v ^= 1u;
                     if (!(ok_q && ok_v)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 }
+                ph_in ^= 1u << kb;
+                ph_v ^= 1u;
                 if (c > 0) {
                     // the previous chunk's state update still reads the K buffer refilled below
                     if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                     ph_s ^= 1u;
                     tc_fence_after();
-                }
-                if (tid == 0) {
-                    if (!mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-                    ph_tb ^= 1u;
                 }
                 // (the issuing warp may raise the abort flag at any time: the decision is taken once, by barrier)
                 if (named_bar_or(1, WY_THREADS, *s_abort != 0)) {
@@ -948,16 +947,34 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 // U^T = V^T (T beta)^T -> U;  W^T = K^T (T beta gamma)^T -> W   (V, K read MN-major)
                 if (!ready(0)) { done = false; break; }
+                {   // the chunk's Q, K, V and T beta / T beta gamma tiles have landed
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_in + (c & 1), (ph_in >> (c & 1)) & 1u,
+                                                                              WY_WAIT_NS) &&
+                                                                mbar_wait_bounded(bar_v, ph_v, WY_WAIT_NS) &&
+                                                                mbar_wait_bounded(bar_tb, ph_tb, WY_WAIT_NS));
+                    if (!ok) {
+                        if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                        done = false;
+                        break;
+                    }
+                    ph_in ^= 1u << (c & 1);
+                    ph_v ^= 1u;
+                    ph_tb ^= 1u;
+                }
                 if (elect_one()) {
                     const uint32_t id = umma_idesc_bf16(128, 64, true, false);
                     const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
+#pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
+#pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
                     }
+#pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
+#pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16(tmem + TM_W, dk + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
                     }
@@ -969,7 +986,9 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (elect_one()) {
                     const uint32_t idq = umma_idesc_bf16(128, 64);
                     const uint64_t dq = tok_desc_k(sQ);
+#pragma unroll
                     for (int h = 0; h < 2; ++h)
+#pragma unroll
                         for (int ks = 0; ks < 8; ++ks)
                             umma_bf16_ta(tmem + TM_QS, tmem + (h ? TM_AL : TM_AH) + ks * 8, dq + ks * TOK_KSTEP_K, idq,
                                          (h | ks) != 0);
@@ -992,8 +1011,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     const uint32_t idd = umma_idesc_bf16(128, 64, false, true);
                     const uint32_t as0[3] = {TM_AH, TM_AL, TM_AH}, bw[3] = {R_TB, R_TB, R_TB + 16384};
                     constexpr uint64_t kmn = umma_kstep_mn(64);
+#pragma unroll
                     for (int p = 0; p < 3; ++p) {
                         const uint64_t db = umma_desc_mn(sb + bw[p], 64, 0);
+#pragma unroll
                         for (int ks = 0; ks < 8; ++ks)
                             umma_bf16_ta(tmem + TM_U, tmem + as0[p] + ks * 8, db + ks * kmn, idd, 1u);
                     }
@@ -1011,15 +1032,19 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 if (elect_one()) {
                     const uint32_t idp = umma_idesc_bf16(128, 64);
                     const uint32_t ad[3] = {TM_AH, TM_AH + 32, TM_AH}, bp[3] = {R_P, R_P, R_P + 8192};
+#pragma unroll
                     for (int p = 0; p < 3; ++p) {
                         const uint64_t db = umma_desc(sb + bp[p], 64, 0);
+#pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16_ta(tmem + TM_PD, tmem + ad[p] + ks * 8, db + ks * KSTEP_K, idp, (p | ks) != 0);
                     }
                     umma_commit(bar);
                     const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
                     const uint64_t dk = tok_desc_mn(sK);
+#pragma unroll
                     for (int h = 0; h < 2; ++h)
+#pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);
                     umma_commit(bar_s);
