@@ -498,6 +498,11 @@ static int layer_step(gdn_pool* p, int32_t layer, const gdn_layer_weights* w, co
     ra.wy_chunks = reinterpret_cast<int2*>(p->wy_tiles + (size_t)p->wy_cap * p->cfg.n_v_heads * gdn::WY_TILESET_BYTES);
     ra.wy_cb = p->wy_cb;
     ra.wy_plan = p->wy_plan;
+    if (has_long && gdn::wy_z_direct(io->z, io->ld_z)) {   // z to the chunked kernel directly, not via the records
+        ra.z = io->z;
+        ra.ld_z = io->ld_z;
+        pa.z_skip_min_t = gdn::WY_MIN_T;
+    }
     cudaError_t e = gdn::launch_layer_step_v2(pa, ra, (cudaStream_t)stream);
     if (e == cudaSuccess && has_long) e = gdn::launch_wy(ra, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_layer_step launch");

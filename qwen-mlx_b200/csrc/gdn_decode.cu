@@ -751,19 +751,29 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
         else
             prep_vec_conv<false, false>(a, ch, active, n0, ratio, hv0 + half, off, col, ring, w, q_seq, q_t, q_T, q_slot);
     } else {
-        // silu(z) of the lane's 8 columns, 8 rows at a time
+        // silu(z) of the lane's 8 columns, 8 rows at a time; none for the tokens of segments the chunked pass
+        // takes when it reads z itself (z_skip_min_t)
         if (active) {
             const uint16_t* zp = a.z + (long long)n0 * a.ld_z + (hv0 + half) * DV + c8;
+            const int skip_t = a.z_skip_min_t > 0 ? a.z_skip_min_t : 0x7fffffff;
 #pragma unroll 1
             for (int jb = 0; jb < PV_TOK; jb += 8) {
+                bool need[8];
+                bool any = false;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    need[r] = q_seq[jb + r] >= 0 && q_T[jb + r] < skip_t;   // routed tokens lie below n_tokens
+                    any |= need[r];
+                }
+                if (!any) continue;   // uniform over the warp: the routing is per token
                 uint4 zr[8];
 #pragma unroll
                 for (int r = 0; r < 8; ++r)
-                    zr[r] = n0 + jb + r < a.n_tokens ? __ldg(reinterpret_cast<const uint4*>(zp + (long long)(jb + r) * a.ld_z))
-                                                     : make_uint4(0u, 0u, 0u, 0u);
+                    zr[r] = need[r] ? __ldg(reinterpret_cast<const uint4*>(zp + (long long)(jb + r) * a.ld_z))
+                                    : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
                 for (int r = 0; r < 8; ++r) {
-                    if (q_seq[jb + r] < 0) continue;
+                    if (!need[r]) continue;
                     float zv[8];
                     unpack8(zr[r], zv);
                     if (simple) {

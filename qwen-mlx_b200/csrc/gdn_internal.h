@@ -55,6 +55,8 @@ struct PrepArgs {
     int32_t* err;
     int32_t tables_stable;       // routing tables and this layer's conv state may be read before the PDL wait
     int32_t dt_bf16;             // dt_bias is a bf16 parameter: a + dt_bias and its exp round to bf16 (gate_softplus)
+    int32_t z_skip_min_t;        // > 0: tokens of segments at least this long get no silu(z) record (the chunked
+                                 // pass reads z itself); honoured by gdn_prep_vec_kernel, the others write it anyway
 };
 
 struct RecurArgs {
@@ -72,6 +74,8 @@ struct RecurArgs {
     int32_t n_seq, n_slots, n_tokens;
     int32_t hk, hv, D;
     int32_t* err;
+    const uint16_t* z;           // non-null: the chunked kernel reads z [n_tokens][ld_z] and applies SiLU itself
+    long long ld_z;              // (wy_z_direct), else it reads silu(z) from the records
     int32_t wy_min_t;            // > 0: segments of at least this many tokens go to the chunked kernel
     int32_t* wy_counter;         // chunked kernel's work-ticket counter (zeroed by the plan kernel)
     uint8_t* wy_tiles;           // per (chunk, v-head) tile sets of the chunk-parallel pass [wy_cap_chunks][Hv][48 KiB]
@@ -88,6 +92,11 @@ constexpr int WY_PLAN_INTS = 2 + WY_SORT_CAP;
 
 // Sequences of at least this many tokens in one call run the chunked (WY) tensor-core kernel.
 constexpr int WY_MIN_T = 32;
+
+// The chunked kernel can load z rows by TMA straight from the caller's tensor: 16-byte aligned base and rows.
+inline bool wy_z_direct(const void* z, long long ld_z) {
+    return z != nullptr && (reinterpret_cast<uintptr_t>(z) & 15u) == 0 && ld_z > 0 && ld_z % 8 == 0;
+}
 
 cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream);
 cudaError_t launch_layer_step_v2(const PrepArgs& p, const RecurArgs& r, cudaStream_t stream);

@@ -45,7 +45,8 @@
 // Shared memory of gdn_wy_kernel (bytes):
 //   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity), token-major TMA boxes
 //   R_V   16K  V [64 s][128 v], token-major TMA box
-//   R_Z   32K  silu(z) [64 t][128 v] x 2 (chunk parity), token-major TMA boxes for the epilogue
+//   R_Z   32K  z [64 t][128 v] x 2 (chunk parity), token-major TMA boxes for the epilogue: raw rows of the
+//              caller's z (SiLU applied there) or silu(z) from the records when z rows are not 16-byte aligned
 //   R_T   17K  y [64 t][128 v] bf16 (row stride LDY), the epilogue's transpose
 //   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] (bulk copy) -> -W^T hi, -W^T lo [128 d][64 t]
 //   R_P   16K  (P (.) QK) hi, lo [64 t][64 s] (same bulk copy)
@@ -86,11 +87,16 @@ constexpr uint64_t WY_WAIT_NS = 2000000000ull;
 constexpr uint32_t TILESET = WY_TILESET_BYTES;   // T beta hi, lo | T beta gamma hi, lo | P (.) QK hi, lo
 static_assert(TILESET == 6 * 8192, "tile set layout");
 
-// gdn_wy_chunk_kernel shared memory: Q | K tiles, per warp group M / T (f32) and N blocks, per-v-head gates (up
-// to 8 heads)
-constexpr int A_TN = WC * LDT * 4 + 6 * 256 * 4;
-constexpr int A_QK = 0, A_T = 32768, A_SMALL = A_T + 2 * A_TN;
-constexpr int A_SMEM = A_SMALL + 5 * 8 * WC * 4 + 32;
+// gdn_wy_chunk_kernel shared memory: two Q | K buffers (the next item's copies land in the other one; once the
+// item's [Q; K] K^T has been taken, its buffer holds the warp groups' N blocks), per warp group M / T (f32), per
+// v-head gates (up to 8 heads; beta and log g of the item and of the next one)
+constexpr int A_QKB = 32768;                  // one Q | K buffer
+constexpr int A_NB = 6 * 256 * 4;             // one warp group's N blocks
+static_assert(2 * A_NB <= A_QKB, "both groups' N blocks fit a consumed Q | K buffer");
+constexpr int A_TN = WC * LDT * 4;
+constexpr int A_QK = 0, A_T = 2 * A_QKB, A_SMALL = A_T + 2 * A_TN;
+constexpr int A_SMEM = A_SMALL + 7 * 8 * WC * 4 + 32;
+static_assert(2 * (A_SMEM + 1024) <= 233472, "two chunk-pass CTAs per SM");
 constexpr int WA_THREADS = 256;
 constexpr int WP_THREADS = 1024;
 
@@ -451,11 +457,11 @@ __device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float*
 
 __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const RecurArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* s_beta = reinterpret_cast<float*>(smem + A_SMALL);   // [8][64]
-    float* s_lgr = s_beta + 8 * WC;                             // [8][64] log g per token
-    float* s_lg = s_lgr + 8 * WC;                               // [8][64] cumulative, log2 units
-    float* s_gam = s_lg + 8 * WC;                               // [8][64] exp(lg_t)
-    float* s_tail = s_gam + 8 * WC;                             // [8][64] (unused here)
+    float* s_beta2 = reinterpret_cast<float*>(smem + A_SMALL);   // [2 buffers][8][64]
+    float* s_lgr2 = s_beta2 + 2 * 8 * WC;                        // [2 buffers][8][64] log g per token
+    float* s_lg = s_lgr2 + 2 * 8 * WC;                           // [8][64] cumulative, log2 units
+    float* s_gam = s_lg + 8 * WC;                                // [8][64] exp(lg_t)
+    float* s_tail = s_gam + 8 * WC;                              // [8][64] (unused here)
     uint64_t* bar = reinterpret_cast<uint64_t*>(s_tail + 8 * WC);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -465,7 +471,6 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
     const uint32_t sb = smem_u32(smem);
     const int ratio = a.hv / a.hk;
     float* fT = reinterpret_cast<float*>(smem + A_T + grp * A_TN);
-    float* fN = reinterpret_cast<float*>(smem + A_T + grp * A_TN + WC * LDT * 4);
 
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -483,26 +488,38 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
     const int total = __ldg(a.wy_plan);
     const int n_items = total > 0 ? total * a.hk : 0;
 
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-        const int g = it / a.hk, hk = it - g * a.hk;
-        const int2 chunk = __ldg(a.wy_chunks + g);   // (first token row, tokens) from the plan
-        const int nv = chunk.y;
-        const long long row = chunk.x;
-        const uint8_t* recq = a.recs + ((long long)(hk * ratio) * a.rec_cap + row) * REC_BYTES;
-        load_field(sb + A_QK, recq, 0, nv, tid);
-        load_field(sb + A_QK + 16384, recq, 256, nv, tid);
-        for (int j = 0; j < ratio; ++j)
-            load_gates(s_beta + j * WC, s_lgr + j * WC,
-                       a.recs + ((long long)(hk * ratio + j) * a.rec_cap + row) * REC_BYTES, nv, tid);
+    // Q, K and the gates of item `it` into buffer `buf` (cp.async, one commit group per thread and item; an empty
+    // group past the last item keeps the group count uniform)
+    auto fetch = [&](int it, int buf) {
+        if (it < n_items) {
+            const int g = it / a.hk, hk = it - g * a.hk;
+            const int2 chunk = __ldg(a.wy_chunks + g);   // (first token row, tokens) from the plan
+            const uint8_t* recq = a.recs + ((long long)(hk * ratio) * a.rec_cap + chunk.x) * REC_BYTES;
+            const uint32_t dq = sb + A_QK + buf * A_QKB;
+            load_field(dq, recq, 0, chunk.y, tid);
+            load_field(dq + 16384, recq, 256, chunk.y, tid);
+            for (int j = 0; j < ratio; ++j)
+                load_gates(s_beta2 + (buf * 8 + j) * WC, s_lgr2 + (buf * 8 + j) * WC,
+                           a.recs + ((long long)(hk * ratio + j) * a.rec_cap + chunk.x) * REC_BYTES, chunk.y, tid);
+        }
         cp_async_commit();
-        cp_async_wait_all();
+    };
+
+    fetch(blockIdx.x, 0);
+    int buf = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x, buf ^= 1) {
+        const int g = it / a.hk, hk = it - g * a.hk;
+        fetch(it + gridDim.x, buf ^ 1);   // the other buffer was released by the previous item's last barrier
+        cp_async_wait_group<1>();         // this item's group has landed (the next one may still be in flight)
         __syncthreads();
-        if (warp < ratio) wy_scan(s_lgr + warp * WC, s_lg + warp * WC, s_gam + warp * WC, s_tail + warp * WC, lane);
+        const float* s_beta = s_beta2 + buf * 8 * WC;
+        if (warp < ratio) wy_scan(s_lgr2 + (buf * 8 + warp) * WC, s_lg + warp * WC, s_gam + warp * WC, s_tail + warp * WC, lane);
         wy_sync_for_mma();
         // [QK; G] = [Q; K] K^T -> TMEM columns [0, 64) (rows 0..63 QK, rows 64..127 G)
+        const uint32_t dq = sb + A_QK + buf * A_QKB;
         if (tid == 0) {
             const uint32_t id = umma_idesc_bf16(128, 64);
-            const uint64_t da = umma_desc(sb + A_QK, 128, 0), db = umma_desc(sb + A_QK + 16384, 128, 0);
+            const uint64_t da = umma_desc(dq, 128, 0), db = umma_desc(dq + 16384, 128, 0);
             for (int ks = 0; ks < 8; ++ks) umma_bf16(tmem, da + ks * KSTEP_K, db + ks * KSTEP_K, id, ks > 0);
             umma_commit(bar);
         }
@@ -510,6 +527,8 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
         __syncthreads();
         if (*s_abort) break;
 
+        // the MMA has read Q and K: the buffer holds the N blocks of both groups until the item ends
+        float* fN = reinterpret_cast<float*>(smem + A_QK + buf * A_QKB + grp * A_NB);
         for (int j0 = 0; j0 < ratio; j0 += 2) {
             const int j = j0 + grp;
             if (j < ratio) {
@@ -522,6 +541,7 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
         __syncthreads();
         tc_fence_after();
     }
+    cp_async_wait_all();   // no copy lands after the CTA ends (the prefetch of an item that an abort skipped)
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 64);
@@ -539,6 +559,13 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
     return d;
+}
+
+// silu of two bf16 values (a bf16x2 word) with the fast sigmoid 1 / (1 + exp(-x)) from the exponential and
+// divide intrinsics, rounded to bf16 as a pair: the bits the prep kernel's prefill tiles write (silu8_fast).
+__device__ __forceinline__ uint32_t silu2_fast(uint32_t w) {
+    const float x0 = __uint_as_float(w << 16), x1 = __uint_as_float(w & 0xFFFF0000u);
+    return bf2_pack(x0 * __fdividef(1.0f, 1.0f + __expf(-x0)), x1 * __fdividef(1.0f, 1.0f + __expf(-x1)));
 }
 
 // A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
@@ -563,7 +590,8 @@ __device__ __forceinline__ uint64_t tok_desc_k(uint32_t saddr) { return umma_des
 constexpr uint64_t TOK_KSTEP_MN = 256u >> 4, TOK_KSTEP_K = 2048u >> 4;
 __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                                                                 const __grid_constant__ CUtensorMap tm_rec,
-                                                                const __grid_constant__ CUtensorMap tm_gate) {
+                                                                const __grid_constant__ CUtensorMap tm_gate,
+                                                                const __grid_constant__ CUtensorMap tm_z) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const float* s_g4 = reinterpret_cast<const float*>(smem + R_G);   // [2][64][4]: g, beta, log g, pad per token
     float* s_lg = reinterpret_cast<float*>(smem + R_SMALL);       // [2][64] cumulative, log2 units
@@ -684,9 +712,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
             bulk_g2s(smem + R_P, tiles + (size_t)cc * tile_step + (R_P - R_TB), TILESET - (R_P - R_TB), bar_tp);
             note_copy(6);
         };
-        auto issue_z = [&](int cc) {          // silu(z) of chunk cc into buffer cc & 1
+        auto issue_z = [&](int cc) {          // z (or silu(z)) of chunk cc into buffer cc & 1
             mbar_arrive_expect_tx(bar_z + (cc & 1), 16384);
-            tma_load_4d(smem + R_Z + (cc & 1) * 16384, &tm_rec, 0, t0 + cc * WC, 48, hv, bar_z + (cc & 1));
+            if (a.z)   // the caller's z: token rows ld_z apart, v-head hv at 16-byte chunks [16 hv, 16 hv + 16)
+                tma_load_4d(smem + R_Z + (cc & 1) * 16384, &tm_z, 0, t0 + cc * WC, 16 * hv, 0, bar_z + (cc & 1));
+            else
+                tma_load_4d(smem + R_Z + (cc & 1) * 16384, &tm_rec, 0, t0 + cc * WC, 48, hv, bar_z + (cc & 1));
             note_copy(4 + (cc & 1));
         };
 
@@ -1061,18 +1092,41 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
             // RMSNorm over the 128 v of the row times silu(z), stored; one token row per thread.  The sum of
             // squares adds four quarter sums as the compute warps' epilogue did (same bits).
             const int et = tid - WY_EPI_WARP * 32;   // token row of the chunk
-            if (warp == WY_EPI_WARP) {   // the first two chunks' silu(z) boxes (both buffers are free)
+            const bool z_raw = a.z != nullptr;
+            if (warp == WY_EPI_WARP) {   // the first two chunks' z boxes (both buffers are free)
                 if (elect_one()) {
                     issue_z(0);
                     if (n_chunks > 1) issue_z(1);
                 }
                 __syncwarp();
             }
+            // Chunk cc's z box once it landed: with raw z, each thread replaces its own token row by silu(z) in
+            // place (rows past the chunk's tokens are left), then orders those writes before the box's next copy.
+            auto take_z = [&](int cc) -> bool {
+                const int zb = cc & 1;
+                const bool zok = mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS);
+                ph_z ^= 1u << zb;
+                const int nvz = (T - cc * WC) < WC ? (T - cc * WC) : WC;
+                if (zok && z_raw && et < nvz) {
+                    uint8_t* zrow = smem + R_Z + zb * 16384 + et * 16;
+#pragma unroll 4
+                    for (int i = 0; i < 16; ++i) {
+                        uint4 zz = *reinterpret_cast<const uint4*>(zrow + i * 1024);
+                        zz.x = silu2_fast(zz.x);
+                        zz.y = silu2_fast(zz.y);
+                        zz.z = silu2_fast(zz.z);
+                        zz.w = silu2_fast(zz.w);
+                        *reinterpret_cast<uint4*>(zrow + i * 1024) = zz;
+                    }
+                    fence_async_shared();
+                }
+                return zok;
+            };
+            bool z_ok = n_chunks > 0 ? take_z(0) : true;
             for (int c = 0; c < n_chunks; ++c) {
                 const int nv = (T - c * WC) < WC ? (T - c * WC) : WC;
                 const int zb = c & 1;
-                const bool ok = mbar_wait_bounded(epi_full, n_yt & 1u, WY_WAIT_NS) &&
-                                mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS);
+                const bool ok = z_ok && mbar_wait_bounded(epi_full, n_yt & 1u, WY_WAIT_NS);
                 if (named_bar_or(2, WY_EPI_THREADS, !ok)) {   // one decision for both epilogue warps
                     if (et == 0) {
                         atomicOr(a.err, ERR_TIMEOUT);
@@ -1080,7 +1134,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                     break;
                 }
-                ph_z ^= 1u << zb;
                 ++n_yt;
                 if (et < nv) {
                     const uint4* yr = reinterpret_cast<const uint4*>(s_yt + et * LDY);
@@ -1138,6 +1191,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     if (elect_one()) issue_z(c + 2);
                     __syncwarp();
                 }
+                if (c + 1 < n_chunks) z_ok = take_z(c + 1);   // while the compute warps finish chunk c + 1's y
             }
         }
         tc_fence_before();
@@ -1182,6 +1236,9 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(gdn_wy_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A_SMEM);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(gdn_wy_chunk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
         g_wy_sms[dev] = sms;
     }
     const int n_items = r.n_seq * r.hv;
@@ -1202,15 +1259,23 @@ cudaError_t launch_wy(const RecurArgs& r, cudaStream_t stream) {
     c.dynamicSmemBytes = A_SMEM;
     e = cudaLaunchKernelEx(&c, gdn_wy_chunk_kernel, r);
     if (e != cudaSuccess) return e;
-    // the sequential pass reads each chunk's Q, K, V and gates from the records by TMA
-    CUtensorMap tm_rec, tm_gate;
+    // the sequential pass reads each chunk's Q, K, V and gates from the records by TMA, and z from the caller's
+    // tensor (one "record" of ld_z elements per token, one head) when its rows are 16-byte aligned
+    CUtensorMap tm_rec, tm_gate, tm_z;
     if (!tmap_records(&tm_rec, r.recs, r.n_tokens, r.rec_cap, r.hv, REC_BYTES, WC, 16) ||
         !tmap_records(&tm_gate, r.recs, r.n_tokens, r.rec_cap, r.hv, REC_BYTES, WC, 1))
         return cudaErrorNotSupported;
+    if (r.z) {
+        if (!wy_z_direct(r.z, r.ld_z) || r.ld_z < (long long)r.hv * DV ||
+            !tmap_records(&tm_z, r.z, r.n_tokens, r.n_tokens, 1, (int)(r.ld_z * 2), WC, 16))
+            return cudaErrorNotSupported;
+    } else {
+        tm_z = tm_rec;   // not read
+    }
     c.gridDim = dim3((unsigned)(n_items < g_wy_sms[dev] ? n_items : g_wy_sms[dev]), 1, 1);
     c.blockDim = dim3(WY_BLOCK, 1, 1);
     c.dynamicSmemBytes = WY_SMEM;
-    return cudaLaunchKernelEx(&c, gdn_wy_kernel, r, tm_rec, tm_gate);
+    return cudaLaunchKernelEx(&c, gdn_wy_kernel, r, tm_rec, tm_gate, tm_z);
 }
 
 }  // namespace gdn
