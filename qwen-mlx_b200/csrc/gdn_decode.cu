@@ -569,7 +569,7 @@ __device__ __forceinline__ void prep_vec_conv(const PrepArgs& a, int ch, bool ac
 #pragma unroll 1
         for (int jj = 0; jj < PV_RING; ++jj) prefetch(jj);
     }
-#pragma unroll 1
+#pragma unroll (SIMPLE ? 2 : 1)
     for (int j = 0; j < PV_TOK; ++j) {
         float xc[8];
         unpack8(raw[(j + KC - 1) * 32], xc);
