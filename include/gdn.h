@@ -111,7 +111,7 @@ GDN_API int gdn_pool_create(int device, const gdn_config* cfg, int32_t n_slots, 
 GDN_API int gdn_pool_destroy(gdn_pool* pool);
 
 /* Size the pool's step scratch for up to `max_tokens` packed tokens per call
- * (a new pool holds max(n_slots, 1024)).  The scratch holds one 1040-byte record
+ * (a new pool holds max(n_slots, 1024)).  The scratch holds one 1056-byte record
  * per (v-head, token): 33 KiB per token for Hv = 32.  Synchronous; call it before
  * capturing a step into a CUDA graph, never while a step is in flight. */
 GDN_API int gdn_pool_reserve_tokens(gdn_pool* pool, int32_t max_tokens);

@@ -8,7 +8,7 @@
 //    (reference rounding: S=1 -> bf16 products and bf16 sum, qwen3_5.rs:602-610;
 //    S>1 -> f32 conv1d, qwen3_5.rs:617-623), q/k RMSNorm with gains 1/dk and
 //    bf16(dk^-1/2) (qwen3_5.rs:636-639), beta and g (compiled_ops.rs:30-43) and
-//    silu(z) (qwen3_5.rs:664).  It writes one 1040-byte record per (v-head,
+//    silu(z) (qwen3_5.rs:664).  It writes one 1056-byte record per (v-head,
 //    token) into the pool's scratch: q | k | v | silu(z) (bf16 x 128 each) |
 //    g (f32) | beta (f32 holding the bf16 value) | log g (f32) | pad.  K1 reads
 //    the conv state, and shifts the windows of one-token sequences in place.
@@ -796,10 +796,10 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
             const float av = bf2f(a.ab[(long long)n * a.ld_ab + a.hv + hv]);
             const float sp = gate_softplus(av, a.dt_bias[hv], a.dt_bf16);
             const float logdecay = -(expf(a.A_log[hv]) * sp);
-            float* gb = reinterpret_cast<float*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
-            gb[0] = expf(logdecay);
-            gb[1] = rbf(sigmoid_f32(b));
-            gb[2] = logdecay;
+            // the record's last sector whole (gates and zero padding): no partly written sector
+            float4* gb = reinterpret_cast<float4*>(a.rec + ((long long)hv * a.rec_cap + n) * REC_BYTES + 1024);
+            gb[0] = make_float4(expf(logdecay), rbf(sigmoid_f32(b)), logdecay, 0.f);
+            gb[1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 }

@@ -34,8 +34,11 @@ struct StepArgs {
 };
 
 // Per-(v-head, token) record written by the prep kernel and streamed by the
-// recurrence kernels: q | k | v | silu(z) (bf16 x 128 each) | g f32 | beta f32 | log g f32 | pad.
-constexpr int REC_BYTES = 1040;
+// recurrence kernels: q | k | v | silu(z) (bf16 x 128 each) | g f32 | beta f32 | log g f32 | pad (20 bytes).
+// 33 DRAM sectors of 32 bytes, so every field starts on a sector and no store covers part of one (a partly
+// written sector costs the memory a read-modify-write).
+constexpr int REC_BYTES = 1056;
+static_assert(REC_BYTES % 32 == 0, "records sector-aligned");
 constexpr int REC_PER_STAGE = 4;   // token records staged with each state tile
 
 struct PrepArgs {

@@ -7,7 +7,7 @@
 // host framework whose own caching allocator owns all device memory.  Such a
 // caller keeps the recurrent and conv states in memory it already owns and
 // passes them in; this entry point runs the same two kernels as gdn_layer_step
-// (prep + streaming recurrence) and takes their scratch -- one 1040-byte record
+// (prep + streaming recurrence) and takes their scratch -- one 1056-byte record
 // per (v-head, token) -- from the file-scope array below instead of a pool.
 //
 // The array is a fixed NOALLOC_MAX_RECORDS records (4,259,840 bytes) in every
