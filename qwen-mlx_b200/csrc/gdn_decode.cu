@@ -528,11 +528,92 @@ __device__ __forceinline__ uint4 pack8_exact(const float (&f)[8]) {
     return make_uint4(u[0], u[1], u[2], u[3]);
 }
 
-// silu of 8 bf16-exact values with the fast sigmoid of silu_bf_fast, rounded to bf16 in pairs.
+// silu of 8 bf16-exact values (bf2_silu_fast, the same bits as the chunked pass's epilogue), rounded to bf16 in
+// pairs.
 __device__ __forceinline__ void silu8_fast(float (&f)[8]) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) f[c] = f[c] * __fdividef(1.0f, 1.0f + __expf(-f[c]));
-    rbf8(f);
+    for (int c = 0; c < 8; c += 2) {
+        const uint32_t w = bf2_silu_fast((__float_as_uint(f[c]) >> 16) | (__float_as_uint(f[c + 1]) & 0xFFFF0000u));
+        f[c] = __uint_as_float(w << 16);
+        f[c + 1] = __uint_as_float(w & 0xFFFF0000u);
+    }
+}
+
+// The all-interior-token form of prep_vec_conv (every token at position >= 3 of a multi-token sequence: no
+// window taps, no decode rounding), on f32 pairs: the conv as fma.rn.f32x2 in the scalar order (x0 w0 first,
+// then + x1 w1, + x2 w2, + x3 w3), bf16 rounding and SiLU (bf2_silu_fast) per pair, the bf16 words stored as
+// they come out.  QK: the RMSNorm sum of squares in channel order, normalise, round, gain, round, as before.
+template <bool QK>
+__device__ __forceinline__ void prep_vec_simple(const PrepArgs& a, bool active, int n0, int ratio, int hv0,
+                                                int rec_off, const uint4* raw, const float (&w)[8][4],
+                                                const int* s_seq) {
+    const int lane = threadIdx.x & 31;
+    uint64_t W[4][KC];   // [channel pair][tap]
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int k = 0; k < KC; ++k) W[p][k] = f2_pack(w[2 * p][k], w[2 * p + 1][k]);
+    uint64_t xm[KC - 1][4];
+#pragma unroll
+    for (int r = 0; r < KC - 1; ++r) {
+        const uint4 u = raw[r * 32];
+        xm[r][0] = bf2_to_f2(u.x);
+        xm[r][1] = bf2_to_f2(u.y);
+        xm[r][2] = bf2_to_f2(u.z);
+        xm[r][3] = bf2_to_f2(u.w);
+    }
+    const float gain = lane < 16 ? 0.0078125f : 0.08837890625f;  // bf16(1/128), bf16(128^-0.5)
+#pragma unroll 2
+    for (int j = 0; j < PV_TOK; ++j) {
+        const uint4 u = raw[(j + KC - 1) * 32];
+        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+        uint64_t xc[4];
+        uint32_t sw[4];   // silu(bf16(conv)) as bf16x2 words
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            xc[p] = bf2_to_f2(uw[p]);
+            uint64_t acc = f2_mul(xm[0][p], W[p][0]);
+            acc = f2_fma(xm[1][p], W[p][1], acc);
+            acc = f2_fma(xm[2][p], W[p][2], acc);
+            acc = f2_fma(xc[p], W[p][3], acc);
+            sw[p] = bf2_silu_fast(f2_to_bf2(acc));
+        }
+        const bool valid = s_seq[j] >= 0;        // uniform over the warp
+        if (QK) {
+            float o[8];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                o[2 * p] = __uint_as_float(sw[p] << 16);
+                o[2 * p + 1] = __uint_as_float(sw[p] & 0xFFFF0000u);
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) ss += o[c] * o[c];
+#pragma unroll
+            for (int m = 8; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+            if (valid) {
+                const float nrm = 1.0f / sqrtf(ss / (float)DK + 1e-6f);
+                uint32_t vw[4];
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const uint64_t v = bf2_to_f2(f2_to_bf2(f2_mul(f2_pack(o[2 * p], o[2 * p + 1]), f2_pack(nrm, nrm))));
+                    vw[p] = f2_to_bf2(f2_mul(v, f2_pack(gain, gain)));
+                }
+                const uint4 val = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+                for (int r = 0; r < ratio; ++r)
+                    *reinterpret_cast<uint4*>(a.rec + ((long long)(hv0 + r) * a.rec_cap + n0 + j) * REC_BYTES + rec_off) = val;
+            }
+        } else if (valid && active) {
+            *reinterpret_cast<uint4*>(a.rec + ((long long)hv0 * a.rec_cap + n0 + j) * REC_BYTES + rec_off) =
+                make_uint4(sw[0], sw[1], sw[2], sw[3]);
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            xm[0][p] = xm[1][p];
+            xm[1][p] = xm[2][p];
+            xm[2][p] = xc[p];
+        }
+    }
 }
 
 // Conv + SiLU of one lane's 8 channels over the sub-tile's tokens.  raw[32 r] is tap row n0-3+r of the channels
@@ -741,13 +822,13 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
     if (role == 0) {
         const int off = (half ? 256 : 0) + 2 * c8;
         if (simple)
-            prep_vec_conv<true, true>(a, ch, true, n0, ratio, hv0, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+            prep_vec_simple<true>(a, true, n0, ratio, hv0, off, col, w, q_seq);
         else
             prep_vec_conv<false, true>(a, ch, true, n0, ratio, hv0, off, col, ring, w, q_seq, q_t, q_T, q_slot);
     } else if (role == 1) {
         const int off = 512 + 2 * c8;
         if (simple)
-            prep_vec_conv<true, false>(a, ch, active, n0, ratio, hv0 + half, off, col, ring, w, q_seq, q_t, q_T, q_slot);
+            prep_vec_simple<false>(a, active, n0, ratio, hv0 + half, off, col, w, q_seq);
         else
             prep_vec_conv<false, false>(a, ch, active, n0, ratio, hv0 + half, off, col, ring, w, q_seq, q_t, q_T, q_slot);
     } else {

@@ -134,4 +134,58 @@ __device__ __forceinline__ float fd_conv_silu(const float (&x)[4], const float (
     return silu_bf(rbf(acc));
 }
 
+// ---- packed f32 pairs (sm_100 f32x2 arithmetic: each lane of the pair rounds as the scalar operation does)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// bf16x2 word (lo in the low half) -> f32 pair, exact
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) {
+    return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+// f32 pair -> bf16x2 word, each rounded to nearest even
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+    float lo, hi;
+    f2_unpack(v, lo, hi);
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+// silu(x) = x / (1 + e^-x) of a pair for the fast (prefill) paths: e^-x = 2^(-x log2 e) and the reciprocal from
+// the PTX approximate instructions (ex2.approx, rcp.approx: a few ulp in f32); x -> -inf gives -0, x -> +inf x.
+__device__ __forceinline__ uint64_t f2_silu_fast(uint64_t x) {
+    const uint64_t t = f2_mul(x, f2_pack(-1.44269504088896341f, -1.44269504088896341f));
+    float t0, t1, e0, e1;
+    f2_unpack(t, t0, t1);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t1));
+    const uint64_t d = f2_add(f2_pack(e0, e1), f2_pack(1.0f, 1.0f));
+    float d0, d1, r0, r1;
+    f2_unpack(d, d0, d1);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+    return f2_mul(x, f2_pack(r0, r1));
+}
+// silu of a bf16x2 word, rounded to bf16 as a pair
+__device__ __forceinline__ uint32_t bf2_silu_fast(uint32_t w) { return f2_to_bf2(f2_silu_fast(bf2_to_f2(w))); }
+
 }  // namespace gdn

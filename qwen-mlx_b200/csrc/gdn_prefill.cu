@@ -561,12 +561,6 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
     return d;
 }
 
-// silu of two bf16 values (a bf16x2 word) with the fast sigmoid 1 / (1 + exp(-x)) from the exponential and
-// divide intrinsics, rounded to bf16 as a pair: the bits the prep kernel's prefill tiles write (silu8_fast).
-__device__ __forceinline__ uint32_t silu2_fast(uint32_t w) {
-    const float x0 = __uint_as_float(w << 16), x1 = __uint_as_float(w & 0xFFFF0000u);
-    return bf2_pack(x0 * __fdividef(1.0f, 1.0f + __expf(-x0)), x1 * __fdividef(1.0f, 1.0f + __expf(-x1)));
-}
 
 // A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
 // Batch i of a chunk's MMAs (0: U/W, 1: Q S0^T, 2: D, 3: P D + state update) may go: the compute threads' shared-
@@ -1112,10 +1106,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
 #pragma unroll 4
                     for (int i = 0; i < 16; ++i) {
                         uint4 zz = *reinterpret_cast<const uint4*>(zrow + i * 1024);
-                        zz.x = silu2_fast(zz.x);
-                        zz.y = silu2_fast(zz.y);
-                        zz.z = silu2_fast(zz.z);
-                        zz.w = silu2_fast(zz.w);
+                        zz.x = bf2_silu_fast(zz.x);   // the bits the prep kernel's prefill tiles write
+                        zz.y = bf2_silu_fast(zz.y);
+                        zz.z = bf2_silu_fast(zz.z);
+                        zz.w = bf2_silu_fast(zz.w);
                         *reinterpret_cast<uint4*>(zrow + i * 1024) = zz;
                     }
                     fence_async_shared();
