@@ -117,6 +117,19 @@ __device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// split8 on f32 pairs (the same bits: hi and x - hi rounded per lane as the scalar form does).
+__device__ __forceinline__ void split8_f2(const uint64_t* x, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[i] = f2_to_bf2(x[i]);
+        l[i] = f2_to_bf2(f2_sub(x[i], bf2_to_f2(h[i])));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+__device__ __forceinline__ uint64_t f2_of(const uint32_t* r) { return f2_pack(__uint_as_float(r[0]), __uint_as_float(r[1])); }
+
 // 16-byte vector at row r, column group c8 (8 columns) of a [rows][COLS] bf16 tile.
 template <int COLS>
 __device__ __forceinline__ void st_tile(uint8_t* base, int r, int c8, const uint4& v) {
@@ -786,18 +799,20 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
 #pragma unroll
                     for (int j = 0; j < 4; ++j) tmem_ld16_async(tmem + lane_base + TM_S + hh * 64 + j * 16, sr[j]);
                     tmem_ld_wait();
+                    const uint64_t g2 = f2_pack(g_last, g_last);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        float sv[16];
+                        uint64_t sp[8];
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) sv[e] = __uint_as_float(sr[j][e]);
+                        for (int e = 0; e < 8; ++e) sp[e] = f2_of(&sr[j][2 * e]);
                         uint4 hi0, lo0, hi1, lo1;
-                        split8(sv, hi0, lo0);
-                        split8(sv + 8, hi1, lo1);
+                        split8_f2(sp, hi0, lo0);
+                        split8_f2(sp + 4, hi1, lo1);
                         tmem_st8(tmem + lane_base + TM_AH + hh * 32 + j * 8, hi0, hi1);
                         tmem_st8(tmem + lane_base + TM_AL + hh * 32 + j * 8, lo0, lo1);
+                        float sv[16];
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) sv[e] *= g_last;
+                        for (int e = 0; e < 8; ++e) f2_unpack(f2_mul(sp[e], g2), sv[2 * e], sv[2 * e + 1]);
                         tmem_st16(tmem + lane_base + TM_S + hh * 64 + j * 16, sv);
                     }
                     tmem_st_wait();
@@ -813,13 +828,16 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    float wv[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) wv[e] = -__uint_as_float(wr[j][e]);
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
+                        // split W, then negate both halves (bf16 rounding is symmetric: the bits of the split of -W)
+                        uint64_t wp[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) wp[e] = f2_of(&wr[j][8 * u + 2 * e]);
                         uint4 hi, lo;
-                        split8(wv + 8 * u, hi, lo);
+                        split8_f2(wp, hi, lo);
+                        hi = make_uint4(hi.x ^ 0x80008000u, hi.y ^ 0x80008000u, hi.z ^ 0x80008000u, hi.w ^ 0x80008000u);
+                        lo = make_uint4(lo.x ^ 0x80008000u, lo.y ^ 0x80008000u, lo.z ^ 0x80008000u, lo.w ^ 0x80008000u);
                         st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, hi);
                         st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
                     }
@@ -835,22 +853,26 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    float dv[16];
+                    uint64_t dp[8];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) dv[e] = __uint_as_float(dr[j][e]);
+                    for (int e = 0; e < 8; ++e) dp[e] = f2_of(&dr[j][2 * e]);
                     {
                         uint4 hi0, lo0, hi1, lo1;
-                        split8(dv, hi0, lo0);
-                        split8(dv + 8, hi1, lo1);
+                        split8_f2(dp, hi0, lo0);
+                        split8_f2(dp + 4, hi1, lo1);
                         tmem_st8(tmem + lane_base + TM_AH + hh * 16 + j * 8, hi0, hi1);
                         tmem_st8(tmem + lane_base + TM_AH + 32 + hh * 16 + j * 8, lo0, lo1);
                     }
+                    const float2* tl2 = reinterpret_cast<const float2*>(tailc + hh * 32 + j * 16);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) dv[e] *= tailc[hh * 32 + j * 16 + e];
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 tv = tl2[e];
+                        dp[e] = f2_mul(dp[e], f2_pack(tv.x, tv.y));
+                    }
                     {
                         uint4 hi0, lo0, hi1, lo1;
-                        split8(dv, hi0, lo0);
-                        split8(dv + 8, hi1, lo1);
+                        split8_f2(dp, hi0, lo0);
+                        split8_f2(dp + 4, hi1, lo1);
                         tmem_st8(tmem + lane_base + TM_AL + hh * 16 + j * 8, hi0, hi1);
                         tmem_st8(tmem + lane_base + TM_AL + 32 + hh * 16 + j * 8, lo0, lo1);
                     }
@@ -878,9 +900,13 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
 #pragma unroll
                     for (int j = 0; j < 2; ++j)
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
+                        for (int e = 0; e < 16; e += 2) {
                             const int t = hh * 32 + j * 16 + e;
-                            s_yt[t * LDY + L] = f2bf(gamc[t] * __uint_as_float(qr[j][e]) + __uint_as_float(pr[j][e]));
+                            const float2 g = *reinterpret_cast<const float2*>(gamc + t);
+                            // gamma_t * QS + PD for tokens t, t + 1, each rounded once (an f32 FMA per lane)
+                            const uint32_t yb = f2_to_bf2(f2_fma(f2_pack(g.x, g.y), f2_of(&qr[j][e]), f2_of(&pr[j][e])));
+                            s_yt[t * LDY + L] = (uint16_t)(yb & 0xFFFFu);
+                            s_yt[(t + 1) * LDY + L] = (uint16_t)(yb >> 16);
                         }
                 }
                 named_bar_sync(1, WY_THREADS);
