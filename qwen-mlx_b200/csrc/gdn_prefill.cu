@@ -386,7 +386,7 @@ __device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float*
         const int kk = pi - i * (i - 1) / 2;
         const float* Ti = fT + (16 * i + r) * LDT + 16 * i;
         const float* Mk = fT + 16 * i * LDT + 16 * kk + c4;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint64_t a01 = 0, a23 = 0;   // (x, y) and (z, w) of the four outputs, as f32 pairs (+0)
 #pragma unroll
         for (int m4 = 0; m4 < 16; m4 += 4) {
             const float4 tr = *reinterpret_cast<const float4*>(Ti + m4);
@@ -394,12 +394,14 @@ __device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float*
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float4 mr = *reinterpret_cast<const float4*>(Mk + (m4 + q) * LDT);
-                acc.x = fmaf(tv[q], mr.x, acc.x);
-                acc.y = fmaf(tv[q], mr.y, acc.y);
-                acc.z = fmaf(tv[q], mr.z, acc.z);
-                acc.w = fmaf(tv[q], mr.w, acc.w);
+                const uint64_t t2 = f2_pack(tv[q], tv[q]);
+                a01 = f2_fma(t2, f2_pack(mr.x, mr.y), a01);
+                a23 = f2_fma(t2, f2_pack(mr.z, mr.w), a23);
             }
         }
+        float4 acc;
+        f2_unpack(a01, acc.x, acc.y);
+        f2_unpack(a23, acc.z, acc.w);
         *reinterpret_cast<float4*>(fN + pi * 256 + r * 16 + c4) = acc;
     }
     named_bar_sync(bar_id, 128);
@@ -409,7 +411,7 @@ __device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float*
         for (int task = gt; task < 64 * i; task += 128) {
             const int jb = task >> 6, rem = task & 63;
             const int r = rem >> 2, c4 = (rem & 3) * 4;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            uint64_t a01 = 0, a23 = 0;   // f32 pairs (+0)
             for (int kk = jb; kk < i; ++kk) {
                 const float* Nr = fN + (i * (i - 1) / 2 + kk) * 256 + r * 16;
                 const float* Tc = fT + 16 * kk * LDT + 16 * jb + c4;
@@ -420,13 +422,15 @@ __device__ __forceinline__ void wa_head(const RecurArgs& a, uint8_t* out, float*
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float4 tr = *reinterpret_cast<const float4*>(Tc + (m4 + q) * LDT);
-                        acc.x = fmaf(nv4[q], tr.x, acc.x);
-                        acc.y = fmaf(nv4[q], tr.y, acc.y);
-                        acc.z = fmaf(nv4[q], tr.z, acc.z);
-                        acc.w = fmaf(nv4[q], tr.w, acc.w);
+                        const uint64_t n2 = f2_pack(nv4[q], nv4[q]);
+                        a01 = f2_fma(n2, f2_pack(tr.x, tr.y), a01);
+                        a23 = f2_fma(n2, f2_pack(tr.z, tr.w), a23);
                     }
                 }
             }
+            float4 acc;
+            f2_unpack(a01, acc.x, acc.y);
+            f2_unpack(a23, acc.z, acc.w);
             *reinterpret_cast<float4*>(fT + (16 * i + r) * LDT + 16 * jb + c4) =
                 make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
         }
@@ -501,12 +505,13 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
     const int total = __ldg(a.wy_plan);
     const int n_items = total > 0 ? total * a.hk : 0;
 
-    // Q, K and the gates of item `it` into buffer `buf` (cp.async, one commit group per thread and item; an empty
-    // group past the last item keeps the group count uniform)
-    auto fetch = [&](int it, int buf) {
+    // (first token row, tokens) of item `it`'s chunk from the plan's table; read an item ahead of its fetch
+    auto chunk_of = [&](int it) { return it < n_items ? __ldg(a.wy_chunks + it / a.hk) : make_int2(0, 0); };
+    // Q, K and the gates of item `it` (chunk `chunk`) into buffer `buf` (cp.async, one commit group per thread and
+    // item; an empty group past the last item keeps the group count uniform)
+    auto fetch = [&](int it, int2 chunk, int buf) {
         if (it < n_items) {
-            const int g = it / a.hk, hk = it - g * a.hk;
-            const int2 chunk = __ldg(a.wy_chunks + g);   // (first token row, tokens) from the plan
+            const int hk = it % a.hk;
             const uint8_t* recq = a.recs + ((long long)(hk * ratio) * a.rec_cap + chunk.x) * REC_BYTES;
             const uint32_t dq = sb + A_QK + buf * A_QKB;
             load_field(dq, recq, 0, chunk.y, tid);
@@ -518,11 +523,16 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
         cp_async_commit();
     };
 
-    fetch(blockIdx.x, 0);
+    fetch(blockIdx.x, chunk_of(blockIdx.x), 0);
+    int2 next_chunk = chunk_of(blockIdx.x + gridDim.x);
     int buf = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, buf ^= 1) {
         const int g = it / a.hk, hk = it - g * a.hk;
-        fetch(it + gridDim.x, buf ^ 1);   // the other buffer was released by the previous item's last barrier
+        // the other buffer was released by the previous item's last barrier; the chunk after it is looked up now,
+        // so its table read has an item's time to land
+        const int2 nc = next_chunk;
+        next_chunk = chunk_of(it + 2 * gridDim.x);
+        fetch(it + gridDim.x, nc, buf ^ 1);
         cp_async_wait_group<1>();         // this item's group has landed (the next one may still be in flight)
         __syncthreads();
         const float* s_beta = s_beta2 + buf * 8 * WC;
