@@ -11,6 +11,7 @@
 
 #include "gdn_device.cuh"
 #include "gdn_internal.h"
+#include "gdn_ptx.cuh"
 
 namespace gdn {
 
@@ -19,12 +20,16 @@ namespace gdn {
 // One CTA per row of H bf16 values.  If `o` is non-null the residual is added first
 // (h_out = bf16(h_in + o)); then, unless `hn` is null, hn = MLX fast::rms_norm(h_out, w, eps):
 // the normalised value is rounded to bf16 before the gain multiply, which rounds again.
+// Launched as a programmatic dependent: it lets the next kernel (the in-projection, which streams its static
+// weight before its own dependency wait) launch at once, then waits for the kernel that produced h and o.
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const uint16_t* __restrict__ h_in, long long ld_h,
                                                           const uint16_t* __restrict__ o, long long ld_o,
                                                           uint16_t* h_out, const uint16_t* __restrict__ w,
                                                           uint16_t* __restrict__ hn, long long ld_hn, int H,
                                                           float eps) {
     __shared__ float s_red[8];
+    pdl_launch_dependents();
+    pdl_wait();
     const long long r = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float acc = 0.0f;
@@ -55,8 +60,16 @@ cudaError_t launch_add_rmsnorm(const uint16_t* h_in, long long ld_h, const uint1
                                uint16_t* h_out, const uint16_t* w, uint16_t* hn, long long ld_hn, int rows, int H,
                                float eps, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    add_rmsnorm_kernel<<<rows, 256, 0, stream>>>(h_in, ld_h, o, ld_o, h_out, w, hn, ld_hn, H, eps);
-    return cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)rows, 1, 1);
+    c.blockDim = dim3(256, 1, 1);
+    c.stream = stream;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    return cudaLaunchKernelEx(&c, add_rmsnorm_kernel, h_in, ld_h, o, ld_o, h_out, w, hn, ld_hn, H, eps);
 }
 
 // ------------------------------------------------------------------ GEMM (cuBLASLt)
