@@ -850,7 +850,8 @@ __global__ void __launch_bounds__(PV_THREADS, 6) gdn_prep_vec_kernel(const PrepA
                 uint4 zr[8];
 #pragma unroll
                 for (int r = 0; r < 8; ++r)
-                    zr[r] = need[r] ? __ldg(reinterpret_cast<const uint4*>(zp + (long long)(jb + r) * a.ld_z))
+                    // coherent loads: z is the output of a projection that may release this kernel early
+                    zr[r] = need[r] ? __ldcg(reinterpret_cast<const uint4*>(zp + (long long)(jb + r) * a.ld_z))
                                     : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
                 for (int r = 0; r < 8; ++r) {

@@ -234,6 +234,10 @@ __global__ void __launch_bounds__(WP_THREADS, 1) gdn_wy_plan_kernel(const RecurA
     __shared__ int s_run, s_cnt;
     __shared__ int l_seq[WY_SORT_CAP], l_len[WY_SORT_CAP];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The chunk-parallel pass may launch now and set up.  It (and the sequential pass, which may launch while this
+    // grid still runs) read the tables below only after their dependency wait, and with coherent loads (__ldcg):
+    // the non-coherent path (__ldg) is only for data no running grid writes, and returned stale tables here.
+    pdl_launch_dependents();
     pdl_wait();
     if (tid == 0) {
         s_run = 0;
@@ -501,12 +505,13 @@ __global__ void __launch_bounds__(WA_THREADS, 2) gdn_wy_chunk_kernel(const Recur
     const uint32_t tmem = *tmem_slot;
     const uint32_t tcol = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     uint32_t ph = 0;
+    pdl_launch_dependents();   // the sequential pass may take SMs as this grid's CTAs leave them
     pdl_wait();
-    const int total = __ldg(a.wy_plan);
+    const int total = __ldcg(a.wy_plan);   // the plan tables: coherent loads (see gdn_wy_plan_kernel)
     const int n_items = total > 0 ? total * a.hk : 0;
 
     // (first token row, tokens) of item `it`'s chunk from the plan's table; read an item ahead of its fetch
-    auto chunk_of = [&](int it) { return it < n_items ? __ldg(a.wy_chunks + it / a.hk) : make_int2(0, 0); };
+    auto chunk_of = [&](int it) { return it < n_items ? __ldcg(a.wy_chunks + it / a.hk) : make_int2(0, 0); };
     // Q, K and the gates of item `it` (chunk `chunk`) into buffer `buf` (cp.async, one commit group per thread and
     // item; an empty group past the last item keeps the group count uniform)
     auto fetch = [&](int it, int2 chunk, int buf) {
@@ -676,8 +681,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
     pdl_wait();
 
-    const int total = __ldg(a.wy_plan);
-    const int m_seq = __ldg(a.wy_plan + 1);
+    const int total = __ldcg(a.wy_plan);   // the plan tables: coherent loads (see gdn_wy_plan_kernel)
+    const int m_seq = __ldcg(a.wy_plan + 1);
     const bool ranked = m_seq <= WY_SORT_CAP;
     const int n_work = total < 0 ? 0 : (ranked ? m_seq : a.n_seq) * a.hv;
 
@@ -690,12 +695,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         if (stop) break;
         const int si = k / a.hv;
         const int hv = k - si * a.hv;
-        const int seq = ranked ? __ldg(a.wy_plan + 2 + si) : si;
+        const int seq = ranked ? __ldcg(a.wy_plan + 2 + si) : si;
         int t0, T, slot;
         if (!wy_qualifies(a, seq, t0, T, slot)) continue;
         float* st = a.rec + ((size_t)slot * a.hv + hv) * (DV * DK);
         const float* st_in = (a.rec_in ? a.rec_in : a.rec) + ((size_t)slot * a.hv + hv) * (DV * DK);
-        const uint8_t* tiles = a.wy_tiles + ((size_t)__ldg(a.wy_cb + seq) * a.hv + hv) * TILESET;
+        const uint8_t* tiles = a.wy_tiles + ((size_t)__ldcg(a.wy_cb + seq) * a.hv + hv) * TILESET;
         const size_t tile_step = (size_t)a.hv * TILESET;   // next chunk of the same head
         const int n_chunks = (T + WC - 1) / WC;
 

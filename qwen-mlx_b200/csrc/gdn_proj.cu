@@ -21,9 +21,11 @@ namespace gdn {
 // (h_out = bf16(h_in + o)); then, unless `hn` is null, hn = MLX fast::rms_norm(h_out, w, eps):
 // the normalised value is rounded to bf16 before the gain multiply, which rounds again.
 // Launched as a programmatic dependent: it lets the next kernel (the in-projection, which streams its static
-// weight before its own dependency wait) launch at once, then waits for the kernel that produced h and o.
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const uint16_t* __restrict__ h_in, long long ld_h,
-                                                          const uint16_t* __restrict__ o, long long ld_o,
+// weight before its own dependency wait) launch at once, then waits for the kernel that produced h and o.  h and
+// o are read with coherent loads (__ldcg): the out-projection before it releases it early, and the non-coherent
+// path is only for data no running grid writes.
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const uint16_t* h_in, long long ld_h,
+                                                          const uint16_t* o, long long ld_o,
                                                           uint16_t* h_out, const uint16_t* __restrict__ w,
                                                           uint16_t* __restrict__ hn, long long ld_hn, int H,
                                                           float eps) {
@@ -35,9 +37,9 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const uint16_t* __rest
     float acc = 0.0f;
     // first pass: residual add (written back), sum of squares
     for (int c = tid; c < H; c += 256) {
-        float v = bf2f(h_in[r * ld_h + c]);
+        float v = bf2f(__ldcg(h_in + r * ld_h + c));
         if (o) {
-            v = rbf(v + bf2f(o[r * ld_o + c]));
+            v = rbf(v + bf2f(__ldcg(o + r * ld_o + c)));
             h_out[r * ld_h + c] = f2bf(v);
         }
         acc += v * v;
@@ -51,7 +53,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const uint16_t* __rest
     for (int i = 0; i < 8; ++i) tot += s_red[i];
     const float nrm = 1.0f / sqrtf(tot / (float)H + eps);
     for (int c = tid; c < H; c += 256) {
-        const float v = o ? bf2f(h_out[r * ld_h + c]) : bf2f(h_in[r * ld_h + c]);
+        const float v = o ? bf2f(h_out[r * ld_h + c]) : bf2f(__ldcg(h_in + r * ld_h + c));
         hn[r * ld_hn + c] = f2bf(bf2f(w[c]) * rbf(v * nrm));
     }
 }

@@ -126,8 +126,9 @@ __global__ void __launch_bounds__(Q16_THREADS, 1) gdn_wq16_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // the next kernel may launch once every CTA got here and run its own pre-wait part; it still waits for this
-    // grid to complete before it reads y
+    // The next kernel may launch once every CTA got here and run its own pre-wait part; it waits for this grid
+    // to complete before it reads y, and reads y with coherent loads (TMA, cp.async.cg, __ldcg or plain loads):
+    // the non-coherent path (__ldg) returned stale data to kernels released early.
     pdl_launch_dependents();
 
     if (warp == 0) {
