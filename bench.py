@@ -379,7 +379,7 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
     step's x copied in and h copied out."""
     import importlib
     synth = importlib.import_module("qwen_mlx_b200.synth")
-    plain, q4 = [], []
+    plain, q4, tiled = [], [], []
     keep = []
     n_in = 8192 + 4096 + 64
     for l in range(N_LAYERS):
@@ -395,18 +395,23 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
             sc = (torch.rand((rows, cols // 64), device=dev, generator=gen) * 0.005).to(torch.bfloat16)
             bi = (torch.randn((rows, cols // 64), device=dev, generator=gen) * 0.005).to(torch.bfloat16)
             qt.append(gdn.tile_weight_q4(wq, sc, bi))
-        keep.append((step, w_in, w_out, pre, qt))
+        bt = (gdn.tile_weight(w_in), gdn.tile_weight(w_out))   # bf16 tiles: the repo's streaming kernels
+        keep.append((step, w_in, w_out, pre, qt, bt))
         plain.append(abi.GdnMixerWeightsC(step.c, w_in.data_ptr(), w_out.data_ptr(), pre.data_ptr(),
                                           None, None, None, None))
+        tiled.append(abi.GdnMixerWeightsC(step.c, w_in.data_ptr(), w_out.data_ptr(), pre.data_ptr(),
+                                          bt[0].data_ptr(), bt[1].data_ptr(), None, None))
         q4.append(abi.GdnMixerWeightsC(step.c, None, None, pre.data_ptr(), None, None, qt[0].data_ptr(),
                                        qt[1].data_ptr()))
     arr_p = (abi.GdnMixerWeightsC * N_LAYERS)(*plain)
     arr_q = (abi.GdnMixerWeightsC * N_LAYERS)(*q4)
+    arr_t = (abi.GdnMixerWeightsC * N_LAYERS)(*tiled)
     h = torch.randn((B, cfg.hidden), device=dev, generator=gen).to(torch.bfloat16)
     slots = torch.arange(B, dtype=torch.int32, device=dev)
     cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
     ms, e2e_ms, hb, db = _time_stack(torch, lib, abi, pool, arr_p, h, slots, cu, B, cfg, stream, barrier, dist, args)
     ms_q, e2e_q, _, _ = _time_stack(torch, lib, abi, pool, arr_q, h, slots, cu, B, cfg, stream, barrier, dist, args)
+    ms_t, e2e_t, _, _ = _time_stack(torch, lib, abi, pool, arr_t, h, slots, cu, B, cfg, stream, barrier, dist, args)
     step_bytes = N_LAYERS * (MIXER_WEIGHT_BYTES + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
     step_bytes_q = N_LAYERS * (MIXER_WEIGHT_BYTES_Q4 + B * BYTES_PER_SEQ_LAYER + BYTES_PER_LAUNCH_CONST)
     return {"tok_s": world * B * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps,
@@ -420,7 +425,12 @@ def run_mixer_stack(torch, dev, gen, cfg, gdn, abi, lib, pool, B, stream, barrie
                    "hbm_frac_of_measured": step_bytes_q / (ms_q / args.steps / 1e3) / 1e9 / hbm_peak,
                    "bytes_per_step": step_bytes_q, "e2e_tok_s": world * B * args.steps / (e2e_q / 1e3),
                    "note": "same stack, MLX 4-bit (group 64) projections on the weight-streaming tcgen05 "
-                           "kernel; synthetic random codes"}}
+                           "kernel; synthetic random codes"},
+            "bf16_tiles": {"tok_s": world * B * args.steps / (ms_t / 1e3), "ms_per_step": ms_t / args.steps,
+                           "hbm_frac_of_measured": step_bytes / (ms_t / args.steps / 1e3) / 1e9 / hbm_peak,
+                           "bytes_per_step": step_bytes, "e2e_tok_s": world * B * args.steps / (e2e_t / 1e3),
+                           "note": "same stack, bf16 projections from the tiled weight copies on this repo's "
+                                   "streaming tcgen05 kernels (<= 16 tokens: weight stages in shared memory)"}}
 
 
 # Prefill (chunked WY) algorithmic flops per token per layer, chunk 64: 6*dk*dv + 2*C*(3*dk + 2*dv) per

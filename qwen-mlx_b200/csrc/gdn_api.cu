@@ -531,10 +531,26 @@ static bool wg_rows_ok(int K, const void* x, long long ldx, const void* tiles) {
     return K % 8 == 0 && ldx % 8 == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)tiles & 15u) == 0;
 }
 
-// y = x w^T on the weight-streaming kernel, in token blocks of WG_MAX_M (each block streams the weight); a 4-bit
-// call of at most 16 tokens runs the kernel with the dequantized weight in tensor memory instead.
+// y = x w^T on the weight-streaming kernel, in token blocks of WG_MAX_M (each block streams the weight); a call of
+// at most 16 tokens runs the 16-token kernels instead: 4-bit with the dequantized weight in tensor memory, bf16
+// with the weight tiles streamed into shared-memory stages.
 static int wg_run(gdn_pool* p, bool q4, int M, int N, int K, const uint16_t* x, long long ldx, const void* tiles,
                   uint16_t* y, long long ldy, cudaStream_t s, const char* what) {
+    if (!q4 && gdn::wb16_supported(M, N, K)) {
+        gdn::WgGemm g;
+        g.tiles = reinterpret_cast<const uint8_t*>(tiles);
+        g.q4 = false;
+        g.x = x; g.ldx = ldx;
+        g.y = y; g.ldy = ldy;
+        g.M = M; g.N = N; g.K = K;
+        g.n_sm = p->n_sm; g.ws = p->wg_ws; g.cnt = p->wg_cnt; g.err = p->err;
+        const cudaError_t e = gdn::launch_wb16(g, s);
+        if (e == cudaSuccess) return GDN_OK;
+        if (e != cudaErrorNotSupported)
+            return fail(GDN_E_CUDA, "%s: bf16 projection launch failed (M=%d N=%d K=%d): %s", what, M, N, K,
+                        cudaGetErrorString(e));
+        // a split's tokens do not fit in shared memory: stream the weight below
+    }
     if (q4 && gdn::wq16_supported(M, N, K)) {
         gdn::WgGemm g;
         g.tiles = reinterpret_cast<const uint8_t*>(tiles);

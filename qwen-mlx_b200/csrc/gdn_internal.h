@@ -170,6 +170,11 @@ bool tmap_records(CUtensorMap* map, const void* recs, int n_tokens, long long re
 // (gdn_wq16.cu); same arguments as launch_wg_gemm (q4 tiles).
 bool wq16_supported(int M, int N, int K);
 cudaError_t launch_wq16(const WgGemm& g, cudaStream_t stream);
+// bf16 tiles (wg_tile_bytes layout, K % 64 == 0), at most 16 tokens: the weight streamed by bulk copy into a
+// ring of shared-memory stages that the MMA reads as its A operand (gdn_wq16.cu).  cudaErrorNotSupported when a
+// split's tokens do not fit in shared memory.
+bool wb16_supported(int M, int N, int K);
+cudaError_t launch_wb16(const WgGemm& g, cudaStream_t stream);
 // 4-bit tiles (wq_tile_bytes layout, K % 64 == 0) -> row-major bf16 weight w [N][K], 16-byte aligned.
 cudaError_t launch_wq_untile(const void* tiles, int N, int K, uint16_t* w, cudaStream_t stream);
 
