@@ -678,6 +678,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     // barrier / the parity of the next issue, for the bounded drain at the exit
     uint32_t cp_any = 0, cp_next = 0;
     uint32_t ph_z = 0;         // (epilogue warps) bit b: the phase of bar_z[b] to wait for next
+    uint32_t ph_zc = 0;        // (compute warps) the same, for their SiLU of the raw z boxes
     uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
     pdl_wait();
 
@@ -858,6 +859,29 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                 }
                 ct_ready(2);   // D^T = U^T - S0 W^T onto U by the issuing warp
+                // while D runs: this chunk's z box (the caller's raw z) becomes silu(z) in place, for the epilogue
+                // warps, which read it after this chunk's y (the prefill tiles' fast SiLU, bf2_silu_fast)
+                if (a.z) {
+                    const int zb = c & 1;
+                    if (mbar_wait_bounded(bar_z + zb, (ph_zc >> zb) & 1u, WY_WAIT_NS)) {
+                        uint8_t* zbox = smem + R_Z + zb * 16384;
+                        for (int u = tid; u < WC * 16; u += WY_THREADS) {   // unit u: feature chunk u / 64, token u % 64
+                            if ((u & (WC - 1)) < nv) {
+                                uint4* zp = reinterpret_cast<uint4*>(zbox + (u >> 6) * 1024 + (u & (WC - 1)) * 16);
+                                uint4 zz = *zp;
+                                zz.x = bf2_silu_fast(zz.x);
+                                zz.y = bf2_silu_fast(zz.y);
+                                zz.z = bf2_silu_fast(zz.z);
+                                zz.w = bf2_silu_fast(zz.w);
+                                *zp = zz;
+                            }
+                        }
+                    } else {
+                        atomicOr(a.err, ERR_TIMEOUT);
+                        *s_abort = 1;
+                    }
+                    ph_zc ^= 1u << zb;
+                }
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
                 if (!wy_wait(bar_qs, ph_qs)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
@@ -1087,6 +1111,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     umma_commit(bar);
                 }
                 __syncwarp();
+                if (has_next) {
+                    // D has read -W^T: the next chunk's T beta / T beta gamma tiles stream into R_TB as soon as it
+                    // completes (U / W's phase of bar completed above, so this parity wait is for D's)
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, (nb + 1) & 1u, WY_WAIT_NS));
+                    if (!ok) {
+                        if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                        done = false;
+                        break;
+                    }
+                    if (elect_one()) issue_tiles_tb(c + 1);
+                    __syncwarp();
+                }
                 // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major); the P tiles landed
                 if (!ready(3)) { done = false; break; }
                 if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_tp, ph_tp, WY_WAIT_NS))) {
@@ -1114,9 +1150,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);
                     umma_commit(bar_s);
-                    // D has read -W^T (the compute warps waited for it before reporting phase F): the next chunk's
-                    // T beta / T beta gamma tiles stream into R_TB
-                    if (has_next) issue_tiles_tb(c + 1);
                 }
                 __syncwarp();
                 nb += 3;   // U/W, D and P D completed on bar this chunk
@@ -1127,7 +1160,6 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
             // RMSNorm over the 128 v of the row times silu(z), stored; one token row per thread.  The sum of
             // squares adds four quarter sums as the compute warps' epilogue did (same bits).
             const int et = tid - WY_EPI_WARP * 32;   // token row of the chunk
-            const bool z_raw = a.z != nullptr;
             if (warp == WY_EPI_WARP) {   // the first two chunks' z boxes (both buffers are free)
                 if (elect_one()) {
                     issue_z(0);
@@ -1135,26 +1167,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 __syncwarp();
             }
-            // Chunk cc's z box once it landed: with raw z, each thread replaces its own token row by silu(z) in
-            // place (rows past the chunk's tokens are left), then orders those writes before the box's next copy.
+            // Chunk cc's z box once it landed (with raw z the compute warps turn it into silu(z) during the chunk's
+            // D, before they hand its y over)
             auto take_z = [&](int cc) -> bool {
                 const int zb = cc & 1;
                 const bool zok = mbar_wait_bounded(bar_z + zb, (ph_z >> zb) & 1u, WY_WAIT_NS);
                 ph_z ^= 1u << zb;
-                const int nvz = (T - cc * WC) < WC ? (T - cc * WC) : WC;
-                if (zok && z_raw && et < nvz) {
-                    uint8_t* zrow = smem + R_Z + zb * 16384 + et * 16;
-#pragma unroll 4
-                    for (int i = 0; i < 16; ++i) {
-                        uint4 zz = *reinterpret_cast<const uint4*>(zrow + i * 1024);
-                        zz.x = bf2_silu_fast(zz.x);   // the bits the prep kernel's prefill tiles write
-                        zz.y = bf2_silu_fast(zz.y);
-                        zz.z = bf2_silu_fast(zz.z);
-                        zz.w = bf2_silu_fast(zz.w);
-                        *reinterpret_cast<uint4*>(zrow + i * 1024) = zz;
-                    }
-                    fence_async_shared();
-                }
                 return zok;
             };
             bool z_ok = n_chunks > 0 ? take_z(0) : true;
