@@ -1012,6 +1012,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 issue_tiles_p(0);
                 issue_qkg(0, 0);
                 issue_v(0);
+                if (n_chunks > 1) bulk_prefetch_l2(tiles + tile_step, TILESET);   // chunk 1's tile set into L2
             }
             __syncwarp();
             bool done = true;
@@ -1120,7 +1121,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         done = false;
                         break;
                     }
-                    if (elect_one()) issue_tiles_tb(c + 1);
+                    if (elect_one()) {
+                        issue_tiles_tb(c + 1);
+                        // the tile set after it into L2 now, so its copies hit L2 when they are issued (the
+                        // T beta copy otherwise arrived late for U / W)
+                        if (c + 2 < n_chunks) bulk_prefetch_l2(tiles + (size_t)(c + 2) * tile_step, TILESET);
+                    }
                     __syncwarp();
                 }
                 // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major); the P tiles landed

@@ -71,6 +71,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2: no destination, no completion to wait for (src 16-byte aligned,
+// bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Tiled tensor load (TMA) of a 2-D box at coordinates (c0 innermost, c1) through the tensor map at `tmap`
 // (a __grid_constant__ kernel parameter), completing on `bar` (tx bytes = the whole box, out-of-range
 // elements written as zero).  c0 * element size must be a multiple of 16 bytes; no multicast.
