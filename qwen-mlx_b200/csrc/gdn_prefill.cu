@@ -591,12 +591,12 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
 
 
 // A compute warp's shared-memory and tensor-memory writes for the next MMA batch are done: one arrival per warp.
-// Batch i of a chunk's MMAs (0: U/W, 1: Q S0^T, 2: D, 3: P D + state update) may go: the compute threads' shared-
+// Batch i of a chunk's MMAs (0: U/W, 1: Q S0^T, 2: D, 3: P D, 4: the state update) may go: the compute threads' shared-
 // and tensor-memory writes for it are done.  A hardware named barrier of the 256 compute threads (arriving without
 // waiting) and the issuing warp (waiting): it wakes the issuer within tens of cycles, where an mbarrier poll took
 // hundreds.  Every compute thread arrives on each of the four once per chunk, and on batch 0's before leaving a
 // chunk loop early, so the issuer never waits on one that does not come.
-constexpr int WY_RDY_BAR = 3;   // named barriers 3..6 (1: compute warps, 2: epilogue warps)
+constexpr int WY_RDY_BAR = 3;   // named barriers 3..7 (1: compute warps, 2: epilogue warps)
 __device__ __forceinline__ void ct_ready(int i) {
     fence_async_shared();
     tc_fence_before();
@@ -890,36 +890,37 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
 #pragma unroll
                 for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_U + hh * 32 + j * 16, dr[j]);
                 tmem_ld_wait();
+                uint64_t dp[2][8];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    uint64_t dp[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) dp[e] = f2_of(&dr[j][2 * e]);
-                    {
-                        uint4 hi0, lo0, hi1, lo1;
-                        split8_f2(dp, hi0, lo0);
-                        split8_f2(dp + 4, hi1, lo1);
-                        tmem_st8(tmem + lane_base + TM_AH + hh * 16 + j * 8, hi0, hi1);
-                        tmem_st8(tmem + lane_base + TM_AH + 32 + hh * 16 + j * 8, lo0, lo1);
-                    }
+                    for (int e = 0; e < 8; ++e) dp[j][e] = f2_of(&dr[j][2 * e]);
+                    uint4 hi0, lo0, hi1, lo1;
+                    split8_f2(dp[j], hi0, lo0);
+                    split8_f2(dp[j] + 4, hi1, lo1);
+                    tmem_st8(tmem + lane_base + TM_AH + hh * 16 + j * 8, hi0, hi1);
+                    tmem_st8(tmem + lane_base + TM_AH + 32 + hh * 16 + j * 8, lo0, lo1);
+                }
+                // ---- phase G (issuing warp): (P D)^T = D^T P^T -> PD (waited in H) as soon as D's hi / lo are in
+                tmem_st_wait();
+                ct_ready(3);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
                     const float2* tl2 = reinterpret_cast<const float2*>(tailc + hh * 32 + j * 16);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const float2 tv = tl2[e];
-                        dp[e] = f2_mul(dp[e], f2_pack(tv.x, tv.y));
+                        dp[j][e] = f2_mul(dp[j][e], f2_pack(tv.x, tv.y));
                     }
-                    {
-                        uint4 hi0, lo0, hi1, lo1;
-                        split8_f2(dp, hi0, lo0);
-                        split8_f2(dp + 4, hi1, lo1);
-                        tmem_st8(tmem + lane_base + TM_AL + hh * 16 + j * 8, hi0, hi1);
-                        tmem_st8(tmem + lane_base + TM_AL + 32 + hh * 16 + j * 8, lo0, lo1);
-                    }
+                    uint4 hi0, lo0, hi1, lo1;
+                    split8_f2(dp[j], hi0, lo0);
+                    split8_f2(dp[j] + 4, hi1, lo1);
+                    tmem_st8(tmem + lane_base + TM_AL + hh * 16 + j * 8, hi0, hi1);
+                    tmem_st8(tmem + lane_base + TM_AL + 32 + hh * 16 + j * 8, lo0, lo1);
                 }
-                // ---- phase G (issuing warp): (P D)^T = D^T P^T -> PD (waited in H);  S += Dd^T K -> S (waited when
-                // the state or the K buffer is next touched)
+                // ... then S += Dd^T K -> S (waited when the state or the K buffer is next touched)
                 tmem_st_wait();
-                ct_ready(3);
+                ct_ready(4);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
@@ -1129,7 +1130,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     }
                     __syncwarp();
                 }
-                // (P D)^T = D^T P^T -> PD;  S += Dd^T K -> S (K read MN-major); the P tiles landed
+                // (P D)^T = D^T P^T -> PD once D's hi / lo are written and the P tiles landed
                 if (!ready(3)) { done = false; break; }
                 if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar_tp, ph_tp, WY_WAIT_NS))) {
                     if (lane == 0) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
@@ -1148,13 +1149,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                             umma_bf16_ta(tmem + TM_PD, tmem + ad[p] + ks * 8, db + ks * KSTEP_K, idp, (p | ks) != 0);
                     }
                     umma_commit(bar);
+                }
+                __syncwarp();
+                // S += Dd^T K once the compute warps have written Dd's hi / lo
+                if (!ready(4)) { done = false; break; }
+                if (elect_one()) {
                     const uint32_t ids = umma_idesc_bf16(128, 128, false, true);
                     const uint64_t dk = tok_desc_mn(sK);
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
-                            umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);
+                            umma_bf16_ta(tmem + TM_S, tmem + TM_AL + h * 32 + ks * 8, dk + ks * TOK_KSTEP_MN, ids, 1u);   // K MN-major
                     umma_commit(bar_s);
                 }
                 __syncwarp();
