@@ -627,7 +627,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint64_t* bar_tb = bar + 3;   // the chunk's T beta / T beta gamma tiles (bulk copy; U and W wait for them)
     uint64_t* bar_in = bar + 4;                                   // [2] Q, K and gates of the chunk of that parity
     uint64_t* bar_v = bar + 6;                                    // V of the current / next chunk
-    // bar + 7 .. bar + 10: unused
+    uint64_t* bar_w = bar + 7;     // W^T of the chunk (issued before U, so the -W^T tiles need not wait for U)
+    // bar + 8 .. bar + 10: unused
     uint64_t* bar_fin = bar + 11;  // every MMA of the issuing warp complete (kernel exit)
     uint64_t* bar_z = bar + 12;    // [2] silu(z) box of the chunk of that parity
     uint64_t* epi_full = bar + 14;  // a chunk's y is transposed into s_yt (thread 0 of the compute warps)
@@ -657,6 +658,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
         mbar_init(bar_z + 1, 1);
         mbar_init(epi_full, 1);
         mbar_init(bar_tp, 1);
+        mbar_init(bar_w, 1);
         mbar_init(epi_free, WY_EPI_THREADS / 32);
         *s_abort = 0;
         fence_mbar_init();
@@ -679,6 +681,7 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
     uint32_t cp_any = 0, cp_next = 0;
     uint32_t ph_z = 0;         // (epilogue warps) bit b: the phase of bar_z[b] to wait for next
     uint32_t ph_zc = 0;        // (compute warps) the same, for their SiLU of the raw z boxes
+    uint32_t ph_w = 0;         // (compute warps) the phase of bar_w to wait for next
     uint32_t n_yt = 0;         // chunks whose y this CTA has handed to the epilogue warps (compute and epilogue)
     pdl_wait();
 
@@ -835,13 +838,17 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 }
                 // (Q S0^T)^T = S0 Q^T -> QS by the issuing warp, off the critical path (read in H)
                 ct_ready(1);
-                if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
-
-                // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U
+                // ---- phase E: -W^T hi/lo tiles [d][t]; then D^T = U^T - S0 W^T onto U.  W is issued (and committed)
+                // before U: its split runs while U's MMAs do; the tiles overwrite U's T beta operand, so they are
+                // stored once U / W's completion is seen as well
+                if (!mbar_wait_bounded(bar_w, ph_w, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
+                ph_w ^= 1u;
+                tc_fence_after();
                 uint32_t wr[2][16];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_W + hh * 32 + j * 16, wr[j]);
                 tmem_ld_wait();
+                uint4 whi[2][2], wlo[2][2];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
 #pragma unroll
@@ -852,12 +859,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         for (int e = 0; e < 4; ++e) wp[e] = f2_of(&wr[j][8 * u + 2 * e]);
                         uint4 hi, lo;
                         split8_f2(wp, hi, lo);
-                        hi = make_uint4(hi.x ^ 0x80008000u, hi.y ^ 0x80008000u, hi.z ^ 0x80008000u, hi.w ^ 0x80008000u);
-                        lo = make_uint4(lo.x ^ 0x80008000u, lo.y ^ 0x80008000u, lo.z ^ 0x80008000u, lo.w ^ 0x80008000u);
-                        st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, hi);
-                        st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, lo);
+                        whi[j][u] = make_uint4(hi.x ^ 0x80008000u, hi.y ^ 0x80008000u, hi.z ^ 0x80008000u, hi.w ^ 0x80008000u);
+                        wlo[j][u] = make_uint4(lo.x ^ 0x80008000u, lo.y ^ 0x80008000u, lo.z ^ 0x80008000u, lo.w ^ 0x80008000u);
                     }
                 }
+                if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }   // U / W complete
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        st_tile<64>(smem + R_TB, L, hh * 4 + j * 2 + u, whi[j][u]);
+                        st_tile<64>(smem + R_TB + 16384, L, hh * 4 + j * 2 + u, wlo[j][u]);
+                    }
                 ct_ready(2);   // D^T = U^T - S0 W^T onto U by the issuing warp
                 // while D runs: this chunk's z box (the caller's raw z) becomes silu(z) in place, for the epilogue
                 // warps, which read it after this chunk's y (the prefill tiles' fast SiLU, bf2_silu_fast)
@@ -1058,17 +1071,18 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     const uint64_t dv = tok_desc_mn(sb + R_V), dk = tok_desc_mn(sK);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
-#pragma unroll
-                        for (int ks = 0; ks < 4; ++ks)
-                            umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
-                    }
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
                         const uint64_t dt = umma_desc(sb + R_TB + 16384 + h * 8192, 64, 0);
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks)
                             umma_bf16(tmem + TM_W, dk + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
+                    }
+                    umma_commit(bar_w);   // W first: the compute warps' -W^T tiles wait only for it
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t dt = umma_desc(sb + R_TB + h * 8192, 64, 0);
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks)
+                            umma_bf16(tmem + TM_U, dv + ks * TOK_KSTEP_MN, dt + ks * KSTEP_K, id, (h | ks) != 0);
                     }
                     umma_commit(bar);
                 }
