@@ -934,6 +934,17 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                 // ... then S += Dd^T K -> S (waited when the state or the K buffer is next touched)
                 tmem_st_wait();
                 ct_ready(4);
+                if (has_next && warp == 7) {
+                    // the next chunk's decay scan, from its gate box, while P D runs (its buffers are the other
+                    // parity's; the barrier at the end of this chunk publishes them; the same barrier phase is
+                    // waited again in phase A)
+                    if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
+                        atomicOr(a.err, ERR_TIMEOUT);
+                        *s_abort = 1;
+                    }
+                    wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
+                               s_tail + (kb ^ 1) * WC, lane);
+                }
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
@@ -962,21 +973,12 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                             s_yt[(t + 1) * LDY + L] = (uint16_t)(yb >> 16);
                         }
                 }
-                named_bar_sync(1, WY_THREADS);
-                if (tid == 0) mbar_arrive(epi_full);
-                ++n_yt;
-                if (has_next && warp == 7) {
-                    // the next chunk's decay scan, from its gate box (the same barrier phase is waited again in phase A)
-                    if (!mbar_wait_bounded(bar_in + (kb ^ 1), (ph_in >> (kb ^ 1)) & 1u, WY_WAIT_NS)) {
-                        atomicOr(a.err, ERR_TIMEOUT);
-                        *s_abort = 1;
-                    }
-                    wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
-                               s_tail + (kb ^ 1) * WC, lane);
-                }
+                // y is in s_yt and every TMEM read of the chunk is complete: one barrier, then the epilogue warps
                 tc_fence_before();
                 named_bar_sync(1, WY_THREADS);
                 tc_fence_after();
+                if (tid == 0) mbar_arrive(epi_full);
+                ++n_yt;
             }
             if (n_chunks > 0 && !*s_abort) {
                 if (!mbar_wait_bounded(bar_s, ph_s, WY_WAIT_NS)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
