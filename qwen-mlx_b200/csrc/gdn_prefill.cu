@@ -804,12 +804,14 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                         *reinterpret_cast<uint4*>(base + (rem & 15) * 1024 + (nv + (rem >> 4)) * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                if (c == 0 && warp == 0) wy_scan_g4(s_g4, nv, s_lg, s_gam, s_tail, lane);   // later chunks: scanned in H
+                if (c == 0 && warp == 0) wy_scan_g4(s_g4, nv, s_lg, s_gam, s_tail, lane);   // later chunks: during P D
                 // ---- phase B (issuing warp): U^T = V^T (T beta)^T, W^T = K^T (T beta gamma)^T; they need only the
                 // chunk's own inputs and overlap the state split below
                 fence_async_shared();
                 tc_fence_before();
-                named_bar_sync(1, WY_THREADS);   // the decays and the cleared rows are visible to every compute thread
+                // the decays and the cleared rows visible to every compute thread (a full chunk after the first has
+                // neither to publish: the barrier above suffices)
+                if (c == 0 || nv < WC) named_bar_sync(1, WY_THREADS);
                 named_bar_arrive(WY_RDY_BAR, WY_THREADS + 32);
                 // ---- phase C: S0 hi/lo tiles [v][d]; S *= gamma_last in place
                 {
@@ -945,6 +947,10 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     wy_scan_g4(s_g4 + (kb ^ 1) * WC * 4, nv1, s_lg + (kb ^ 1) * WC, s_gam + (kb ^ 1) * WC,
                                s_tail + (kb ^ 1) * WC, lane);
                 }
+                // Q S0^T completed before phase F: its columns load while P D runs
+                uint32_t qr[2][16], pr[2][16];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_QS + hh * 32 + j * 16, qr[j]);
                 if (!wy_wait(bar, ph)) { atomicOr(a.err, ERR_TIMEOUT); *s_abort = 1; }
 
                 // ---- phase H: y^T[v][t] = gamma_t QS[v][t] + PD[v][t], rounded to bf16, transposed through smem for
@@ -954,12 +960,8 @@ __global__ void __launch_bounds__(WY_BLOCK, 1) gdn_wy_kernel(const RecurArgs a,
                     *s_abort = 1;
                 }
                 {
-                    uint32_t qr[2][16], pr[2][16];
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        tmem_ld16_async(tmem + lane_base + TM_QS + hh * 32 + j * 16, qr[j]);
-                        tmem_ld16_async(tmem + lane_base + TM_PD + hh * 32 + j * 16, pr[j]);
-                    }
+                    for (int j = 0; j < 2; ++j) tmem_ld16_async(tmem + lane_base + TM_PD + hh * 32 + j * 16, pr[j]);
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 2; ++j)
