@@ -46,7 +46,8 @@
 //   R_QK  64K  [Q [64 t][128 d] | K [64 s][128 d]] x 2 (chunk parity), token-major TMA boxes
 //   R_V   16K  V [64 s][128 v], token-major TMA box
 //   R_Z   32K  z [64 t][128 v] x 2 (chunk parity), token-major TMA boxes for the epilogue: raw rows of the
-//              caller's z (SiLU applied there) or silu(z) from the records when z rows are not 16-byte aligned
+//              caller's z (turned into silu(z) in place by the compute warps while the chunk's D runs) or
+//              silu(z) from the records when z rows are not 16-byte aligned
 //   R_T   17K  y [64 t][128 v] bf16 (row stride LDY), the epilogue's transpose
 //   R_TB  32K  (T beta) hi, lo; (T beta gamma) hi, lo [64 t][64 s] (bulk copy) -> -W^T hi, -W^T lo [128 d][64 t]
 //   R_P   16K  (P (.) QK) hi, lo [64 t][64 s] (same bulk copy)
