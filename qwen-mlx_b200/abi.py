@@ -1,4 +1,4 @@
-"""ctypes declarations of include/gdn.h and include/gdn_host.h for libgdn_b200.so.
+"""ctypes declarations of include/gdn.h, include/gdn_host.h and include/gdn_hybrid.h for libgdn_b200.so.
 
 The library is the product; this module only binds it.  Loading fails loudly
 when the library has not been built: there is no fallback implementation.
@@ -68,6 +68,25 @@ class GdnSchedStatsC(C.Structure):
                 ("active", _i32), ("waiting", _i32), ("prefilling", _i32), ("free_slots", _i32)]
 
 
+class GdnAttnConfigC(C.Structure):
+    _fields_ = [("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32), ("rotary_dim", _i32),
+                ("rope_theta", C.c_float), ("rms_norm_eps", C.c_float), ("max_ctx", _i32)]
+
+
+class GdnMoeConfigC(C.Structure):
+    _fields_ = [("hidden", _i32), ("n_experts", _i32), ("top_k", _i32), ("moe_inter", _i32), ("shared_inter", _i32),
+                ("norm_topk_prob", _i32)]
+
+
+class GdnQ4MatrixC(C.Structure):
+    _fields_ = [("q", _vp), ("scales", _vp), ("biases", _vp)]
+
+
+class GdnMoeWeightsC(C.Structure):
+    _fields_ = [("router", _vp), ("gate", GdnQ4MatrixC), ("up", GdnQ4MatrixC), ("down", GdnQ4MatrixC),
+                ("sh_gate", GdnQ4MatrixC), ("sh_up", GdnQ4MatrixC), ("sh_down", GdnQ4MatrixC), ("shared_gate", _vp)]
+
+
 SIGNATURES = {
     "gdn_last_error": (C.c_char_p, []),
     "gdn_version": (C.c_char_p, []),
@@ -117,6 +136,14 @@ SIGNATURES = {
     "gdn_sched_stats_get": (_int, [_vp, C.POINTER(GdnSchedStatsC)]),
     "gdn_sched_active_ids": (_int, [_vp, C.POINTER(C.c_uint64), _i32, C.POINTER(_i32)]),
     "gdn_sched_free_slots": (_int, [_vp, _i32, C.POINTER(_i32)]),
+    # include/gdn_hybrid.h
+    "gdn_attn_workspace_bytes": (_int, [C.POINTER(GdnAttnConfigC), _i32, _i32, C.POINTER(_i64)]),
+    "gdn_attn_step": (_int, [C.POINTER(GdnAttnConfigC), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32,
+                             _i32, _vp, _vp, _i64, _vp]),
+    "gdn_moe_workspace_bytes": (_int, [C.POINTER(GdnMoeConfigC), _i32, C.POINTER(_i64)]),
+    "gdn_moe_route": (_int, [C.POINTER(GdnMoeConfigC), C.POINTER(GdnMoeWeightsC), _vp, _i32, _vp, _vp, _vp, _vp]),
+    "gdn_moe_step": (_int, [C.POINTER(GdnMoeConfigC), C.POINTER(GdnMoeWeightsC), _vp, _i32, _vp, _vp, _vp, _vp, _i64,
+                            _vp]),
 }
 
 

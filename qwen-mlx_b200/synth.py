@@ -234,3 +234,35 @@ def random_states(cfg: GdnConfig, n_seq: int, seed: int, tag: str = "", scale: f
     conv = normal_bf16(seed, tag + "conv_state", (n_seq, cfg.conv_k - 1, cfg.conv_dim))
     rec = (normal(seed, tag + "rec_state", n_seq * cfg.hv * cfg.dv * cfg.dk) * scale).astype(np.float32)
     return conv, rec.reshape(n_seq, cfg.hv, cfg.dv, cfg.dk)
+
+
+# ---------------------------------------------------------------- hybrid layers (attention, MoE)
+
+def _rng(seed: int, stream: str) -> np.random.Generator:
+    return np.random.default_rng(int(_key(seed, stream)))
+
+
+def q4_matrix(seed: int, stream: str, rows: int, cols: int, s_scale: float = 0.01) -> dict:
+    """A random MLX 4-bit matrix (group 64): uniform codes, scales |N(0, s_scale^2)| + s_scale / 4 and
+    biases -8 * scale, both bf16, so dequantised weights centre on 0 with spread ~ 8 * scale."""
+    r = _rng(seed, stream)
+    q = r.integers(0, 2**32, size=(rows, cols // 8), dtype=np.uint32)
+    s = (np.abs(r.standard_normal((rows, cols // 64))) * s_scale + s_scale / 4).astype(np.float32)
+    sb = f32_to_bf16(s)
+    b = f32_to_bf16((-8.0 * bf16_to_f32(sb)).astype(np.float32))
+    return {"q": q, "scales": sb, "biases": b}
+
+
+def moe_weights(hidden: int, n_experts: int, moe_inter: int, shared_inter: int, seed: int = 0) -> dict:
+    """Random-init weights of one SparseMoeBlock (qwen3_5.rs:232-248) in the checkpoint's layout: router and
+    shared_expert_gate bf16, experts stacked by rows as 4-bit matrices."""
+    return {
+        "router": normal_bf16(seed, "moe.router", (n_experts, hidden), 0.02),
+        "shared_gate": normal_bf16(seed, "moe.shared_gate", (hidden,), 0.02),
+        "gate": q4_matrix(seed, "moe.gate", n_experts * moe_inter, hidden),
+        "up": q4_matrix(seed, "moe.up", n_experts * moe_inter, hidden),
+        "down": q4_matrix(seed, "moe.down", n_experts * hidden, moe_inter),
+        "sh_gate": q4_matrix(seed, "moe.sh_gate", shared_inter, hidden),
+        "sh_up": q4_matrix(seed, "moe.sh_up", shared_inter, hidden),
+        "sh_down": q4_matrix(seed, "moe.sh_down", hidden, shared_inter),
+    }
