@@ -84,6 +84,9 @@ def parse():
                    help="run only the chunked-prefill leg and print its result (profiling of that leg)")
     p.add_argument("--prefill-lens", default=None,
                    help="comma-separated prompt lengths for the prefill leg (default: config 4)")
+    p.add_argument("--hybrid-only", action="store_true",
+                   help="time only the attention and MoE layer bodies of the hybrid decoder (B decode tokens)")
+    p.add_argument("--hybrid-ctx", type=int, default=4096, help="cached context of each sequence (hybrid legs)")
     return p.parse_args()
 
 
@@ -670,6 +673,83 @@ def run_prefill(torch, dev, gen, cfg, gdn, abi, lib, pool, lws, stream, barrier,
             "flops_per_token_layer": WY_FLOPS_PER_TOKEN_LAYER}
 
 
+def run_hybrid(args):
+    """Decode-step timing of the hybrid decoder's other layers at Qwen3.5-35B-A3B shapes, through the public API
+    (eager calls; the attention call uploads its routing table each call): one attention layer body (16 q / 2 kv
+    heads of 256, every sequence `--hybrid-ctx` keys deep) and one MoE block (256 4-bit experts, top-8, shared
+    expert).  Roofline: the attention reads every cached key and value once per kv head; the MoE reads the
+    routed experts' 4-bit weights (codes, scales and biases) once, the shared expert's and the router's."""
+    import torch
+    import __graft_entry__ as ge
+    ge.load_package()
+    import importlib
+    synth = importlib.import_module("qwen_mlx_b200.synth")
+    gdn = importlib.import_module("qwen_mlx_b200.gdn")
+    hy = importlib.import_module("qwen_mlx_b200.hybrid")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, ctx = args.batch, args.hybrid_ctx
+    hbm_peak, peak_kind = measured_peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    steps = max(args.steps, 20)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / steps * 1e3   # us per call
+
+    acfg = hy.AttnConfig(max_ctx=ctx)
+    cache = hy.KVCache(acfg, B, dev)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    D = acfg.n_heads * acfg.head_dim
+    qf = torch.randn((B, 2 * D), device=dev, generator=gen).to(torch.bfloat16)
+    kin = torch.randn((B, acfg.n_kv_heads * acfg.head_dim), device=dev, generator=gen).to(torch.bfloat16)
+    vin = torch.randn_like(kin)
+    gain = torch.ones(acfg.head_dim, device=dev, dtype=torch.bfloat16)
+    slots, cu, pos = list(range(B)), list(range(B + 1)), [ctx - 1] * B
+    ws = torch.empty(hy.attn_workspace_bytes(acfg, B, ctx), dtype=torch.uint8, device=dev)
+    out = torch.empty((B, D), dtype=torch.bfloat16, device=dev)
+    us_attn = timed(lambda: hy.attn_step(cache, qf, kin, vin, gain, gain, slots, cu, pos, out=out, workspace=ws))
+    attn_bytes = B * acfg.n_kv_heads * ctx * acfg.head_dim * 2 * 2
+
+    mcfg = hy.MoeConfig()
+    mw_np = synth.moe_weights(mcfg.hidden, mcfg.n_experts, mcfg.moe_inter, mcfg.shared_inter, seed=3)
+    mw = hy.MoeWeights(mw_np, dev)
+    x = torch.randn((B, mcfg.hidden), device=dev, generator=gen).to(torch.bfloat16)
+    mws = torch.empty(hy.moe_workspace_bytes(mcfg, B), dtype=torch.uint8, device=dev)
+    mout = torch.empty((B, mcfg.hidden), dtype=torch.bfloat16, device=dev)
+    us_moe = timed(lambda: hy.moe_step(mcfg, mw, x, out=mout, workspace=mws))
+    ids, _, _ = hy.moe_route(mcfg, mw, x)
+    n_exp = int(torch.unique(ids).numel())
+
+    def q4_bytes(rows, cols):
+        return rows * cols // 2 + 2 * 2 * rows * (cols // 64)
+
+    per_expert = 2 * q4_bytes(mcfg.moe_inter, mcfg.hidden) + q4_bytes(mcfg.hidden, mcfg.moe_inter)
+    shared = 2 * q4_bytes(mcfg.shared_inter, mcfg.hidden) + q4_bytes(mcfg.hidden, mcfg.shared_inter)
+    moe_bytes = n_exp * per_expert + shared + mcfg.n_experts * mcfg.hidden * 2
+    res = {
+        "workload": f"hybrid layers, batched S=1 decode, B={B}, {ctx} cached keys per sequence",
+        "attention": {"us_per_layer": us_attn, "alg_bytes": attn_bytes,
+                      "achieved_gbs": attn_bytes / us_attn / 1e3, "hbm_frac": attn_bytes / us_attn / 1e3 / hbm_peak,
+                      "config": "16 q heads, 2 kv heads, head_dim 256, rotary 64; gdn_attn_step eager"},
+        "moe": {"us_per_layer": us_moe, "experts_touched": n_exp, "alg_bytes": moe_bytes,
+                "achieved_gbs": moe_bytes / us_moe / 1e3, "hbm_frac": moe_bytes / us_moe / 1e3 / hbm_peak,
+                "config": "256 experts (4-bit, group 64), top-8, moe/shared intermediate 512; gdn_moe_step eager"},
+        "hbm_peak_gbs": hbm_peak, "peak_kind": peak_kind,
+    }
+    print(json.dumps({"hybrid": res}), flush=True)
+
+
 def run_ours(args):
     import torch
     world, rank, local, dist, timedelta = dist_setup(args.gpus)
@@ -974,6 +1054,9 @@ def run_ours(args):
 
 def main():
     args = parse()
+    if args.hybrid_only:
+        run_hybrid(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
