@@ -8,10 +8,10 @@
 //                           renormalisation (qwen3_5.rs:268-284), and the shared-expert gate logit;
 //   gdn_moe_bucket_kernel   one CTA: counting sort of the (token, k) pairs by expert, the shared expert
 //                           taken as expert E with one pair per token;
-//   gdn_moe_up_kernel       CTA per (expert, 64 rows of gate|up, 32 of its pairs): 4-bit dequant of
+//   gdn_moe_up_kernel       CTA per (expert, 16 rows of gate|up, 32 of its pairs): 4-bit dequant of
 //                           both rows in registers, dots with up to 8 staged token rows at a time,
 //                           h = silu(gate x) * up x (compiled_ops.rs:99-143);
-//   gdn_moe_down_kernel     CTA per (expert, 64 rows of down, 32 of its pairs): y = down h;
+//   gdn_moe_down_kernel     CTA per (expert, 16 rows of down, 32 of its pairs): y = down h;
 //   gdn_moe_combine_kernel  one CTA per token: sum_j w_j y_j + sigmoid(gate logit) * y_shared.
 // All of it is weight-streaming integer/float work on the CUDA cores: at decode batch sizes a token
 // group shares each dequantised row across its up-to-8 tokens, and the rows are read once.
@@ -27,9 +27,9 @@
 namespace gdn {
 namespace {
 
-constexpr int MR_THREADS = 256;   // route
-constexpr int MX_THREADS = 256;   // up / down: 8 warps x 8 rows
-constexpr int MX_ROWS = 64;       // weight rows per CTA
+constexpr int MR_THREADS = 1024;  // route: 32 warps share the router's rows
+constexpr int MX_THREADS = 256;   // up / down: 8 warps x 2 rows
+constexpr int MX_ROWS = 16;       // weight rows per CTA (many CTAs per expert: decode touches few rows' tokens)
 constexpr int MX_TG = 8;          // token rows staged together
 constexpr int MX_TC = 32;         // pairs per CTA
 constexpr int MAX_HIDDEN = 4096;
@@ -80,6 +80,7 @@ MoeLayout moe_layout(const gdn_moe_config* c, int N) {
 // Dot of x (f32 in shared memory) with a bf16 row, over a warp: lane covers columns [8 lane + 256 i, +8).
 __device__ __forceinline__ float warp_dot_bf16(const float* xs, const uint16_t* row, int H, int lane) {
     float acc = 0.f;
+#pragma unroll 4
     for (int c = lane * 8; c < H; c += 256) {
         const uint4 v = *reinterpret_cast<const uint4*>(row + c);
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
@@ -236,7 +237,7 @@ __device__ __forceinline__ void stage_rows(uint16_t* dst, const uint16_t* src, s
     }
 }
 
-// blockIdx = (expert, 64-row block of gate/up, 32-pair block of the expert's pairs).
+// blockIdx = (expert, 16-row block of gate/up, 32-pair block of the expert's pairs).
 __global__ void __launch_bounds__(MX_THREADS) gdn_moe_up_kernel(const MoeArgs a) {
     extern __shared__ __align__(16) uint16_t xs_up[];   // [MX_TG][H]
     const int e = blockIdx.x;
@@ -264,6 +265,7 @@ __global__ void __launch_bounds__(MX_THREADS) gdn_moe_up_kernel(const MoeArgs a)
             float ag[MX_TG], au[MX_TG];
 #pragma unroll
             for (int k = 0; k < MX_TG; ++k) { ag[k] = 0.f; au[k] = 0.f; }
+#pragma unroll 4
             for (int w = lane; w < wpr; w += 32) {
                 const int grp = w >> 3;
                 float wg[8], wu[8];
@@ -299,7 +301,7 @@ __global__ void __launch_bounds__(MX_THREADS) gdn_moe_up_kernel(const MoeArgs a)
     }
 }
 
-// blockIdx = (expert, 64-row block of down, 32-pair block of the expert's pairs).
+// blockIdx = (expert, 16-row block of down, 32-pair block of the expert's pairs).
 __global__ void __launch_bounds__(MX_THREADS) gdn_moe_down_kernel(const MoeArgs a) {
     extern __shared__ __align__(16) uint16_t hs_dn[];   // [MX_TG][I]
     const int e = blockIdx.x;
@@ -325,6 +327,7 @@ __global__ void __launch_bounds__(MX_THREADS) gdn_moe_down_kernel(const MoeArgs 
             float ac[MX_TG];
 #pragma unroll
             for (int k = 0; k < MX_TG; ++k) ac[k] = 0.f;
+#pragma unroll 2
             for (int w = lane; w < wpr; w += 32) {
                 const int grp = w >> 3;
                 float wd[8];
