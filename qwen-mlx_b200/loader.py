@@ -1,4 +1,4 @@
-"""Weight loader for the reference's checkpoint layout (the GDN layers only).
+"""Weight loader for the reference's checkpoint layout (the GDN layers; the attention and MoE layers at the end).
 
 The reference loads a Qwen3.5 MLX checkpoint in `load_config` / `load_model` (src/models/qwen3_5.rs:886-1086):
 
@@ -223,3 +223,150 @@ def _check_shapes(g: GdnConfig, w: dict, l: int):
         got = w[k][0].shape if isinstance(w[k], tuple) else w[k].shape
         if tuple(got) != shape:
             raise ValueError(f"layer {l}: {k} has shape {tuple(got)}, expected {shape}")
+
+
+# ---------------------------------------------------------------- attention and MoE layers
+#
+# The other layers of the hybrid decoder (qwen3_5.rs:313-460, :78-311) as the reference's checkpoint stores them:
+#   language_model.model.layers.{l}.self_attn.{q_proj, k_proj, v_proj, o_proj}   (l + 1) % interval == 0
+#       q_proj has 2 * n_heads * head_dim rows (queries and the output gate, per head), :345-350
+#   language_model.model.layers.{l}.self_attn.{q_norm, k_norm}.weight [head_dim]
+#   language_model.model.layers.{l}.post_attention_layernorm.weight [hidden]           every layer, :740
+#   language_model.model.layers.{l}.mlp.gate                [E, hidden]                 the router, :241
+#   language_model.model.layers.{l}.mlp.switch_mlp.{gate_proj, up_proj, down_proj}   [E, I, hidden], [E, hidden, I]
+#   language_model.model.layers.{l}.mlp.shared_expert.{gate_proj, up_proj, down_proj}
+#   language_model.model.layers.{l}.mlp.shared_expert_gate [1, hidden]
+# A quantized checkpoint quantizes every one of them with the one (bits, group_size) of its config
+# (nn::quantize over the whole model, qwen3_5.rs:927-935).
+
+def attention_layers(cfg: dict) -> list[int]:
+    """Indices of the full-attention layers: (l + 1) % full_attention_interval == 0 (qwen3_5.rs:73-75)."""
+    n, k = cfg["num_hidden_layers"], cfg["full_attention_interval"]
+    return [l for l in range(n) if (l + 1) % k == 0]
+
+
+def attn_config(cfg: dict, max_ctx: int = 4096) -> dict:
+    """Keyword arguments of hybrid.AttnConfig from a checkpoint config (defaults as Qwen35Config's, :67-68)."""
+    hd = int(cfg["head_dim"])
+    return dict(n_heads=int(cfg["num_attention_heads"]), n_kv_heads=int(cfg["num_key_value_heads"]), head_dim=hd,
+                rotary_dim=int(hd * float(cfg.get("partial_rotary_factor", 0.25))),
+                rope_theta=float(cfg.get("rope_theta", 10_000_000.0)), rms_norm_eps=float(cfg["rms_norm_eps"]),
+                max_ctx=max_ctx)
+
+
+def moe_config(cfg: dict) -> dict:
+    """Keyword arguments of hybrid.MoeConfig from a checkpoint config (qwen3_5.rs:55-63)."""
+    return dict(hidden=int(cfg["hidden_size"]), n_experts=int(cfg["num_experts"]),
+                top_k=int(cfg["num_experts_per_tok"]), moe_inter=int(cfg["moe_intermediate_size"]),
+                shared_inter=int(cfg["shared_expert_intermediate_size"]),
+                norm_topk_prob=bool(cfg.get("norm_topk_prob", True)))
+
+
+def dequantize(w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray, bits: int, group: int) -> np.ndarray:
+    """MLX affine dequantization to bf16: value c of a row = scale[c / group] * q + bias[c / group], q = bits
+    [bits * (c % (32 / bits)), +bits) of word c / (32 / bits), rounded once (exact in f32 for bits <= 8, since a
+    bf16 scale times a code and its bias are exact there)."""
+    per = 32 // bits
+    w_q = np.asarray(w_q, np.uint32)
+    lead, W = w_q.shape[:-1], w_q.shape[-1]
+    shifts = (np.arange(per, dtype=np.uint32) * bits)
+    q = ((w_q[..., None] >> shifts) & np.uint32((1 << bits) - 1)).reshape(*lead, W * per).astype(np.float32)
+    s = (np.asarray(scales, np.uint16).astype(np.uint32) << 16).view(np.float32)
+    b = (np.asarray(biases, np.uint16).astype(np.uint32) << 16).view(np.float32)
+    cols = W * per
+    v = q.reshape(*lead, cols // group, group) * s[..., None] + b[..., None]
+    return f32_to_bf16(v.reshape(*lead, cols).astype(np.float32))
+
+
+def _quant(cfg: dict):
+    q = cfg.get("quantization")
+    if q is None:
+        return None
+    return int(q.get("bits", 4)), int(q.get("group_size", 64))
+
+
+def _dense_bf16(ck: Checkpoint, base: str, quant) -> np.ndarray:
+    """A Linear's weight as bf16, dequantizing a quantized one (the router and the shared-expert gate, which the
+    kernels take in bf16)."""
+    if quant is not None and base + ".scales" in ck:
+        bits, group = quant
+        return dequantize(ck.get(base + ".weight"), _bf16(ck, base + ".scales"), _bf16(ck, base + ".biases"), bits,
+                          group)
+    return _bf16(ck, base + ".weight")
+
+
+def _q4_matrix(ck: Checkpoint, base: str, quant, rows: int, cols: int) -> dict:
+    """A 4-bit (group 64) matrix as {q, scales, biases}, experts stacked by rows: [rows][cols/8] words."""
+    if quant is None or base + ".scales" not in ck:
+        raise ValueError(f"{base}: the MoE kernels take MLX 4-bit (group 64) experts; this tensor is not quantized")
+    if quant != (4, 64):
+        raise ValueError(f"{base}: {quant[0]}-bit group-{quant[1]} quantization; the kernels take bits 4, group 64")
+    wq = ck.get(base + ".weight")
+    if wq.shape[-1] != cols // 8 or wq.size != rows * (cols // 8):
+        raise ValueError(f"{base}: weight of shape {wq.shape}, expected {rows} rows of {cols // 8} words")
+    m = {"q": np.ascontiguousarray(wq, np.uint32).reshape(rows, cols // 8),
+         "scales": _bf16(ck, base + ".scales").reshape(rows, cols // 64),
+         "biases": _bf16(ck, base + ".biases").reshape(rows, cols // 64)}
+    return m
+
+
+def load_attention_layers(model_dir, max_ctx: int = 4096) -> tuple[dict, list[int], list[dict]]:
+    """(hybrid.AttnConfig keyword arguments, attention-layer indices, one weight dict per attention layer):
+    `q_proj` / `k_proj` / `v_proj` / `o_proj` (bf16 [N, K], or (w_q, scales, biases) when quantized; they run as
+    library GEMMs around gdn_attn_step), `q_norm_w` / `k_norm_w` [head_dim], `pre_w` (input_layernorm) and
+    `post_w` (post_attention_layernorm) [hidden], all bf16."""
+    cfg = load_config(model_dir)
+    quant = _quant(cfg)
+    bits, group = quant if quant else (4, 64)
+    a = attn_config(cfg, max_ctx)
+    H, nh, nkv, hd = int(cfg["hidden_size"]), a["n_heads"], a["n_kv_heads"], a["head_dim"]
+    ck = Checkpoint(model_dir)
+    layers = attention_layers(cfg)
+    want = {"q_proj": (2 * nh * hd, H), "k_proj": (nkv * hd, H), "v_proj": (nkv * hd, H), "o_proj": (H, nh * hd)}
+    out = []
+    for l in layers:
+        p = f"{PREFIX}.{l}.self_attn"
+        w = {name: _proj(ck, f"{p}.{name}", quant is not None, bits, group) for name in want}
+        for name, (n, k) in want.items():
+            got = w[name][0].shape if isinstance(w[name], tuple) else w[name].shape
+            exp = (n, k // 8) if isinstance(w[name], tuple) else (n, k)
+            if tuple(got) != exp:
+                raise ValueError(f"layer {l}: {name} has shape {tuple(got)}, expected {exp}")
+        w["q_norm_w"] = _bf16(ck, f"{p}.q_norm.weight")
+        w["k_norm_w"] = _bf16(ck, f"{p}.k_norm.weight")
+        w["pre_w"] = _bf16(ck, f"{PREFIX}.{l}.input_layernorm.weight")
+        w["post_w"] = _bf16(ck, f"{PREFIX}.{l}.post_attention_layernorm.weight")
+        for k, n in (("q_norm_w", hd), ("k_norm_w", hd), ("pre_w", H), ("post_w", H)):
+            if w[k].shape != (n,):
+                raise ValueError(f"layer {l}: {k} has shape {w[k].shape}, expected ({n},)")
+        out.append(w)
+    return a, layers, out
+
+
+def load_moe_layers(model_dir) -> tuple[dict, list[dict]]:
+    """(hybrid.MoeConfig keyword arguments, one hybrid.MoeWeights input dict per decoder layer): `router` [E,
+    hidden] and `shared_gate` [hidden] bf16 (dequantized when the checkpoint quantizes them), the experts'
+    `gate` / `up` [E * I][hidden / 8] and `down` [E * hidden][I / 8] and the shared expert's `sh_gate` /
+    `sh_up` / `sh_down` as 4-bit {q, scales, biases}, and `post_w` (post_attention_layernorm) [hidden]."""
+    cfg = load_config(model_dir)
+    quant = _quant(cfg)
+    m = moe_config(cfg)
+    H, E, I, Is = m["hidden"], m["n_experts"], m["moe_inter"], m["shared_inter"]
+    ck = Checkpoint(model_dir)
+    out = []
+    for l in range(int(cfg["num_hidden_layers"])):
+        p = f"{PREFIX}.{l}.mlp"
+        w = {"router": _dense_bf16(ck, f"{p}.gate", quant),
+             "shared_gate": _dense_bf16(ck, f"{p}.shared_expert_gate", quant).reshape(-1),
+             "gate": _q4_matrix(ck, f"{p}.switch_mlp.gate_proj", quant, E * I, H),
+             "up": _q4_matrix(ck, f"{p}.switch_mlp.up_proj", quant, E * I, H),
+             "down": _q4_matrix(ck, f"{p}.switch_mlp.down_proj", quant, E * H, I),
+             "sh_gate": _q4_matrix(ck, f"{p}.shared_expert.gate_proj", quant, Is, H),
+             "sh_up": _q4_matrix(ck, f"{p}.shared_expert.up_proj", quant, Is, H),
+             "sh_down": _q4_matrix(ck, f"{p}.shared_expert.down_proj", quant, H, Is),
+             "post_w": _bf16(ck, f"{PREFIX}.{l}.post_attention_layernorm.weight")}
+        if w["router"].shape != (E, H) or w["shared_gate"].shape != (H,):
+            raise ValueError(f"layer {l}: router {w['router'].shape} / shared_expert_gate {w['shared_gate'].shape}, "
+                             f"expected ({E}, {H}) / ({H},)")
+        out.append(w)
+    return m, out
