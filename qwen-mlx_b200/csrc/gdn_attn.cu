@@ -60,8 +60,9 @@ struct AttnLayout {
 AttnLayout attn_layout(int N, int nh, int hd, int ns) {
     AttnLayout L{};
     size_t o = 0;
-    L.tok_slot = o; o = align256(o + sizeof(int32_t) * N);
-    L.tok_pos = o;  o = align256(o + sizeof(int32_t) * N);
+    L.tok_slot = o;                                   // [slot x N | position x N]: one upload
+    L.tok_pos = o + sizeof(int32_t) * N;
+    o = align256(o + 2 * sizeof(int32_t) * N);
     L.qbuf = o;     o = align256(o + sizeof(uint16_t) * (size_t)N * nh * hd);
     L.part_m = o;   o = align256(o + sizeof(float) * (size_t)N * nh * ns);
     L.part_l = o;   o = align256(o + sizeof(float) * (size_t)N * nh * ns);
@@ -368,10 +369,8 @@ int gdn_attn_step(const gdn_attn_config* cfg, const gdn_bf16* q_full, const gdn_
     }
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemcpyAsync(ws + L.tok_slot, tab.data(), sizeof(int32_t) * n_tokens, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(ws + L.tok_pos, tab.data() + n_tokens, sizeof(int32_t) * n_tokens, cudaMemcpyHostToDevice,
-                            st);
+    cudaError_t e =
+        cudaMemcpyAsync(ws + L.tok_slot, tab.data(), 2 * sizeof(int32_t) * n_tokens, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) {
         snprintf(msg, sizeof msg, "routing table upload: %s", cudaGetErrorString(e));
         return record_error(GDN_E_CUDA, msg);

@@ -7,11 +7,12 @@
 //   gdn_moe_route_kernel    one CTA per token: router logits (bf16), softmax, top-k by block argmax,
 //                           renormalisation (qwen3_5.rs:268-284), and the shared-expert gate logit;
 //   gdn_moe_bucket_kernel   one CTA: counting sort of the (token, k) pairs by expert, the shared expert
-//                           taken as expert E with one pair per token;
+//                           taken as expert E with one pair per token, and the list of experts with pairs
+//                           (the next two grids cover only those);
 //   gdn_moe_up_kernel       CTA per (expert, 16 rows of gate|up, 32 of its pairs): 4-bit dequant of
 //                           both rows in registers, dots with up to 8 staged token rows at a time,
 //                           h = silu(gate x) * up x (compiled_ops.rs:99-143);
-//   gdn_moe_down_kernel     CTA per (expert, 16 rows of down, 32 of its pairs): y = down h;
+//   gdn_moe_down_kernel     CTA per (expert, 64 rows of down, 32 of its pairs): y = down h;
 //   gdn_moe_combine_kernel  one CTA per token: sum_j w_j y_j + sigmoid(gate logit) * y_shared.
 // All of it is weight-streaming integer/float work on the CUDA cores: at decode batch sizes a token
 // group shares each dequantised row across its up-to-8 tokens, and the rows are read once.
@@ -29,7 +30,8 @@ namespace {
 
 constexpr int MR_THREADS = 1024;  // route: 32 warps share the router's rows
 constexpr int MX_THREADS = 256;   // up / down: 8 warps x 2 rows
-constexpr int MX_ROWS = 16;       // weight rows per CTA (many CTAs per expert: decode touches few rows' tokens)
+constexpr int MX_ROWS = 16;       // gate|up rows per CTA (many CTAs per expert: at decode an expert has few tokens)
+constexpr int MD_ROWS = 64;       // down rows per CTA (a down row is short: moe_inter columns)
 constexpr int MX_TG = 8;          // token rows staged together
 constexpr int MX_TC = 32;         // pairs per CTA
 constexpr int MAX_HIDDEN = 4096;
@@ -48,6 +50,7 @@ struct MoeArgs {
     uint16_t* w;             // [N][K]
     float* sg;               // [N] shared-expert gate logit (bf16 value); null: not computed
     int32_t* off;            // [E + 2] pair offsets by expert (E = shared)
+    int32_t* act;            // [E + 2]: act[0] = experts with pairs, act[1 ..] = their ids (ascending)
     int32_t* list;           // [P] pairs sorted by expert
     uint16_t* h;             // [P][Imax]
     uint16_t* y;             // [P][H]
@@ -58,7 +61,7 @@ struct MoeArgs {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct MoeLayout {
-    size_t ids, w, sg, off, list, h, y, total;
+    size_t ids, w, sg, off, act, list, h, y, total;
 };
 
 MoeLayout moe_layout(const gdn_moe_config* c, int N) {
@@ -70,6 +73,7 @@ MoeLayout moe_layout(const gdn_moe_config* c, int N) {
     L.w = o;    o = align256(o + sizeof(uint16_t) * (size_t)N * c->top_k);
     L.sg = o;   o = align256(o + sizeof(float) * (size_t)N);
     L.off = o;  o = align256(o + sizeof(int32_t) * (size_t)(c->n_experts + 2));
+    L.act = o;  o = align256(o + sizeof(int32_t) * (size_t)(c->n_experts + 2));
     L.list = o; o = align256(o + sizeof(int32_t) * P);
     L.h = o;    o = align256(o + sizeof(uint16_t) * P * Imax);
     L.y = o;    o = align256(o + sizeof(uint16_t) * P * c->hidden);
@@ -202,14 +206,16 @@ __global__ void __launch_bounds__(1024) gdn_moe_bucket_kernel(const MoeArgs a) {
     }
     __syncthreads();
     if (tid == 0) {
-        int run = 0;
+        int run = 0, n_act = 0;
         for (int e = 0; e <= a.E; ++e) {
             const int c = cnt[e];
             cnt[e] = run;   // becomes the expert's cursor
             a.off[e] = run;
             run += c;
+            if (c > 0) a.act[1 + n_act++] = e;
         }
         a.off[a.E + 1] = run;
+        a.act[0] = n_act;
     }
     __syncthreads();
     for (int p = tid; p < P; p += blockDim.x) {
@@ -237,10 +243,11 @@ __device__ __forceinline__ void stage_rows(uint16_t* dst, const uint16_t* src, s
     }
 }
 
-// blockIdx = (expert, 16-row block of gate/up, 32-pair block of the expert's pairs).
+// blockIdx = (active expert, 16-row block of gate/up, 32-pair block of the expert's pairs).
 __global__ void __launch_bounds__(MX_THREADS) gdn_moe_up_kernel(const MoeArgs a) {
     extern __shared__ __align__(16) uint16_t xs_up[];   // [MX_TG][H]
-    const int e = blockIdx.x;
+    if ((int)blockIdx.x >= a.act[0]) return;
+    const int e = a.act[1 + blockIdx.x];
     const bool sh = e == a.E;
     const int I = sh ? a.Is : a.I;
     const int r0 = blockIdx.y * MX_ROWS;
@@ -301,13 +308,14 @@ __global__ void __launch_bounds__(MX_THREADS) gdn_moe_up_kernel(const MoeArgs a)
     }
 }
 
-// blockIdx = (expert, 16-row block of down, 32-pair block of the expert's pairs).
+// blockIdx = (active expert, 64-row block of down, 32-pair block of the expert's pairs).
 __global__ void __launch_bounds__(MX_THREADS) gdn_moe_down_kernel(const MoeArgs a) {
     extern __shared__ __align__(16) uint16_t hs_dn[];   // [MX_TG][I]
-    const int e = blockIdx.x;
+    if ((int)blockIdx.x >= a.act[0]) return;
+    const int e = a.act[1 + blockIdx.x];
     const bool sh = e == a.E;
     const int I = sh ? a.Is : a.I;
-    const int r0 = blockIdx.y * MX_ROWS;
+    const int r0 = blockIdx.y * MD_ROWS;
     const int beg = a.off[e] + blockIdx.z * MX_TC;
     const int end = min(a.off[e + 1], beg + MX_TC);
     if (beg >= end || r0 >= a.H) return;
@@ -320,8 +328,8 @@ __global__ void __launch_bounds__(MX_THREADS) gdn_moe_down_kernel(const MoeArgs 
         __syncthreads();
         stage_rows(hs_dn, a.h, (size_t)a.Imax, I, false, a, g0, ng);
         __syncthreads();
-        for (int rr = 0; rr < MX_ROWS / 8; ++rr) {
-            const int r = r0 + warp * (MX_ROWS / 8) + rr;
+        for (int rr = 0; rr < MD_ROWS / 8; ++rr) {
+            const int r = r0 + warp * (MD_ROWS / 8) + rr;
             if (r >= a.H) break;
             const size_t row = erow + r;
             float ac[MX_TG];
@@ -469,6 +477,7 @@ int gdn_moe_step(const gdn_moe_config* cfg, const gdn_moe_weights* w, const gdn_
     MoeArgs a = moe_args(cfg, w, x, n_tokens);
     a.sg = reinterpret_cast<float*>(ws + L.sg);
     a.off = reinterpret_cast<int32_t*>(ws + L.off);
+    a.act = reinterpret_cast<int32_t*>(ws + L.act);
     a.list = reinterpret_cast<int32_t*>(ws + L.list);
     a.h = reinterpret_cast<uint16_t*>(ws + L.h);
     a.y = reinterpret_cast<uint16_t*>(ws + L.y);
@@ -495,8 +504,11 @@ int gdn_moe_step(const gdn_moe_config* cfg, const gdn_moe_weights* w, const gdn_
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(gdn_moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
         if (e == cudaSuccess) {
-            gdn_moe_up_kernel<<<dim3(a.E + 1, (a.Imax + MX_ROWS - 1) / MX_ROWS, zb), MX_THREADS, up_smem, st>>>(a);
-            gdn_moe_down_kernel<<<dim3(a.E + 1, (a.H + MX_ROWS - 1) / MX_ROWS, zb), MX_THREADS, dn_smem, st>>>(a);
+            // experts with pairs: at most min(E, N K) routed ones plus the shared expert
+            const long long routed = (long long)n_tokens * cfg->top_k;
+            const int gx = (routed < a.E ? (int)routed : a.E) + 1;
+            gdn_moe_up_kernel<<<dim3(gx, (a.Imax + MX_ROWS - 1) / MX_ROWS, zb), MX_THREADS, up_smem, st>>>(a);
+            gdn_moe_down_kernel<<<dim3(gx, (a.H + MD_ROWS - 1) / MD_ROWS, zb), MX_THREADS, dn_smem, st>>>(a);
             gdn_moe_combine_kernel<<<n_tokens, 256, 0, st>>>(a);
             e = cudaGetLastError();
         }
