@@ -56,7 +56,10 @@ GDN_API int gdn_attn_workspace_bytes(const gdn_attn_config* cfg, int32_t n_token
  * q_full [N][2*nh*hd], k_in / v_in [N][nkv*hd], out [N][nh*hd] (input of o_proj), q_norm_w / k_norm_w [hd];
  * k_cache / v_cache [n_slots][nkv][max_ctx][hd] bf16.  slot_ids, cu_seqlens, positions: HOST arrays,
  * checked (slots in range and distinct, positions[i] + tokens <= max_ctx).  The workspace holds
- * gdn_attn_workspace_bytes(cfg, N, max over i of positions[i] + tokens_i) bytes.  Asynchronous. */
+ * gdn_attn_workspace_bytes(cfg, N, max over i of positions[i] + tokens_i) bytes.  The per-token
+ * (slot, position) table is copied into the workspace from host memory during the call, and that
+ * copy waits for the work already queued on `stream`; the kernels then run asynchronously.  Not
+ * capturable in a CUDA graph for that reason. */
 GDN_API int gdn_attn_step(const gdn_attn_config* cfg, const gdn_bf16* q_full, const gdn_bf16* k_in,
                           const gdn_bf16* v_in, const gdn_bf16* q_norm_w, const gdn_bf16* k_norm_w,
                           gdn_bf16* k_cache, gdn_bf16* v_cache, int32_t n_slots, const int32_t* slot_ids,
