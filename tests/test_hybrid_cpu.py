@@ -135,3 +135,88 @@ def test_moe_workspace_and_checks(abi, hy):
     assert rc == abi.GDN_E_INVALID
     rc = L.gdn_moe_step(C.byref(cfg.c()), C.byref(w), fake, 4, None, None, fake, fake, 16, None)
     assert rc == abi.GDN_E_INVALID and "workspace" in abi.last_error()
+
+
+# ------------------------------------------------------------------ independent f64 cross-checks of the oracle
+
+def _f64_attention(H, cfg, qf, kin, vin, qn, kn, kc, vc, slots, cu, positions):
+    """Token by token, in f64 without any bf16 rounding: the same layer written a second way (explicit loops,
+    rotation by angle pairs, a plain softmax), to bound the rounded oracle."""
+    nh, nkv, hd, rot = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["rotary_dim"]
+    th, eps = cfg["rope_theta"], cfg["rms_norm_eps"]
+    G, half = nh // nkv, rot // 2
+    qf = H.bf(qf).astype(np.float64).reshape(len(qf), nh, 2 * hd)
+    kin = H.bf(kin).astype(np.float64).reshape(len(kin), nkv, hd)
+    vin = H.bf(vin).astype(np.float64).reshape(len(vin), nkv, hd)
+    Kc, Vc = H.bf(kc).astype(np.float64), H.bf(vc).astype(np.float64)
+    qn, kn = H.bf(qn).astype(np.float64), H.bf(kn).astype(np.float64)
+
+    def norm_rope(x, g, p):
+        y = x / np.sqrt(np.mean(x * x) + eps) * g
+        out = y.copy()
+        for i in range(half):
+            a = p * th ** (-i / half)
+            out[i] = y[i] * np.cos(a) - y[i + half] * np.sin(a)
+            out[i + half] = y[i] * np.sin(a) + y[i + half] * np.cos(a)
+        return out
+
+    out = np.zeros((len(qf), nh * hd))
+    for s_i, s in enumerate(slots):
+        for t in range(cu[s_i], cu[s_i + 1]):
+            p = positions[s_i] + (t - cu[s_i])
+            for kv in range(nkv):
+                Kc[s, kv, p] = norm_rope(kin[t, kv], kn, p)
+                Vc[s, kv, p] = vin[t, kv]
+        for t in range(cu[s_i], cu[s_i + 1]):
+            p = positions[s_i] + (t - cu[s_i])
+            for h in range(nh):
+                q = norm_rope(qf[t, h, :hd], qn, p)
+                sc = np.array([q @ Kc[s, h // G, j] for j in range(p + 1)]) / np.sqrt(hd)
+                w = np.exp(sc - sc.max())
+                o = (w / w.sum()) @ Vc[s, h // G, :p + 1]
+                out[t, h * hd:(h + 1) * hd] = o / (1.0 + np.exp(-qf[t, h, hd:]))
+    return out
+
+
+def test_attention_oracle_bounded_by_f64_restatement(H, synth):
+    cfg = dict(n_heads=4, n_kv_heads=2, head_dim=64, rotary_dim=16, rope_theta=1e4, rms_norm_eps=1e-6)
+    rng = np.random.default_rng(7)
+    bfr = lambda shape: synth.f32_to_bf16(rng.standard_normal(shape).astype(np.float32))  # noqa: E731
+    slots, lens, positions = [1, 0], [3, 1], [2, 5]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    qf, kin, vin = bfr((4, 4 * 128)), bfr((4, 2 * 64)), bfr((4, 2 * 64))
+    qn = synth.f32_to_bf16((1 + 0.1 * rng.standard_normal(64)).astype(np.float32))
+    kn = synth.f32_to_bf16((1 + 0.1 * rng.standard_normal(64)).astype(np.float32))
+    kc, vc = bfr((2, 2, 8, 64)), bfr((2, 2, 8, 64))
+    got = H.bf(H.attn_step(cfg, qf, kin, vin, qn, kn, kc.copy(), vc.copy(), slots, cu, positions))
+    ref = _f64_attention(H, cfg, qf, kin, vin, qn, kn, kc, vc, slots, cu, positions)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert err < 1e-2   # bf16 roundings of q, k, the SDPA output, the gate and the product
+
+
+def test_moe_oracle_bounded_by_per_pair_restatement(H, synth):
+    """The oracle groups pairs by expert; this runs every (token, k) pair on its own in f64 without bf16
+    rounding (other than the dequantised weights), then weights, sums and adds the gated shared expert."""
+    cfg = dict(hidden=128, n_experts=6, top_k=3, moe_inter=64, shared_inter=64, norm_topk_prob=True)
+    w = synth.moe_weights(128, 6, 64, 64, seed=11)
+    x = synth.normal_bf16(11, "pp.x", (5, 128))
+    got = H.bf(H.moe_step(cfg, w, x))
+    xf = H.bf(x).astype(np.float64)
+    logits = xf @ H.bf(w["router"]).astype(np.float64).T
+    p = np.exp(logits - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    deq = lambda m, r0, r1: H.bf(H.q4_dequant(m, slice(r0, r1))).astype(np.float64)  # noqa: E731
+    silu = lambda v: v / (1.0 + np.exp(-v))  # noqa: E731
+    ref = np.zeros((5, 128))
+    for t in range(5):
+        top = np.argsort(-p[t], kind="stable")[:3]
+        wt = p[t, top] / p[t, top].sum()
+        for e, we in zip(top, wt):
+            g = deq(w["gate"], e * 64, (e + 1) * 64) @ xf[t]
+            u = deq(w["up"], e * 64, (e + 1) * 64) @ xf[t]
+            ref[t] += we * (deq(w["down"], e * 128, (e + 1) * 128) @ (silu(g) * u))
+        gs = deq(w["sh_gate"], 0, 64) @ xf[t]
+        us = deq(w["sh_up"], 0, 64) @ xf[t]
+        ys = deq(w["sh_down"], 0, 128) @ (silu(gs) * us)
+        ref[t] += ys / (1.0 + np.exp(-(xf[t] @ H.bf(w["shared_gate"]).astype(np.float64))))
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-2
