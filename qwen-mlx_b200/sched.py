@@ -48,6 +48,8 @@ class ShardTables:
     cu_seqlens: np.ndarray  # int32 [n_seq + 1]
     row_src: np.ndarray     # int32 [n_tokens] row of the step's packed input
     reset_slots: np.ndarray  # int32 local slots to reset before the step (PREFILL_FIRST entries)
+    positions: np.ndarray = None  # int32 [n_seq] tokens each sequence processed before this step: the KV-cache
+                                  # position of its first token here (gdn_attn_step's `positions`)
 
     @property
     def n_seq(self) -> int:
@@ -82,7 +84,12 @@ def pack_step(entries, n_shards: int, slots_per_shard: int) -> list[ShardTables]
         k, t = int(ns[s]), int(nt[s])
         mine = [e for e in entries if e.slot // slots_per_shard == s]
         reset = np.array([e.slot - s * slots_per_shard for e in mine if e.kind == PREFILL_FIRST], np.int32)
-        out.append(ShardTables(s, slots[sb:sb + k].copy(), cu[cb:cb + k + 1].copy(), rows[rb:rb + t].copy(), reset))
+        local = slots[sb:sb + k].copy()
+        # gdn_pack_step keeps the step's entry order within a shard, so `mine` lines up with `local`
+        if not np.array_equal(local, np.array([e.slot - s * slots_per_shard for e in mine], np.int32)):
+            raise RuntimeError("gdn_pack_step reordered a shard's sequences")
+        pos = np.array([e.pos for e in mine], np.int32)
+        out.append(ShardTables(s, local, cu[cb:cb + k + 1].copy(), rows[rb:rb + t].copy(), reset, pos))
         sb, cb, rb = sb + k, cb + k + 1, rb + t
     return out
 

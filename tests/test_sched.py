@@ -202,3 +202,28 @@ def test_scheduled_tables_pass_the_routing_validator(sched, abi):
         steps += 1
     assert steps > 10 and s.stats["free_slots"] == per * n_shards
     assert len(s.drain_finished()) == 30
+
+
+def test_shard_positions_track_the_kv_cache(sched):
+    """positions[i] of a shard table is where sequence i's first token of the step goes in its slot's KV cache
+    (the attention layers' gdn_attn_step): 0 after a PREFILL_FIRST reset, then the running token count."""
+    per, n_shards = 8, 2
+    s = sched.TokenScheduler(max_batch=6, n_shards=n_shards, slots_per_shard=per, prefill_budget=3, prefill_chunk=16)
+    rng = np.random.default_rng(5)
+    for _ in range(25):
+        s.enqueue(int(rng.integers(1, 50)), int(rng.integers(1, 10)))
+    kv_len = np.full((n_shards, per), -1)
+    steps = 0
+    while s.has_work():
+        p = s.plan()
+        for t in sched.pack_step(p, n_shards, per):
+            for sl in t.reset_slots:
+                kv_len[t.shard, sl] = 0
+            lens = np.diff(t.cu_seqlens)
+            assert t.positions.shape == t.slot_ids.shape
+            for sl, pos, n in zip(t.slot_ids, t.positions, lens):
+                assert kv_len[t.shard, sl] == pos
+                kv_len[t.shard, sl] += n
+        s.complete()
+        steps += 1
+    assert steps > 10
